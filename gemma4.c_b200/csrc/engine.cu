@@ -1,0 +1,596 @@
+// engine.cu — the device-resident decode step: forward of
+// gemma4-4b/cpu-blas/main.c:1838-2029 for B sequences in lockstep, with the
+// weights, KV cache and activations resident in HBM.
+//
+// One step (token ids -> next-token argmax) is a fixed launch sequence that
+// reads the position and the token ids from device memory, so it is captured
+// once per (batch, lm_mode, token source) into a CUDA graph and replayed for
+// every position.  Greedy generation feeds each step's argmax keys straight
+// into the next step's embedding lookup: no host round trip per token.
+//
+// Per layer l (main.c:1865-2010):
+//   resnorm   x = (x + rms(p_raw)*post_norm[l-1]) * out_scale[l-1];
+//             xn = rms(x)*attn_norm[l]; q8 = Q8_K(xn)
+//   gemv      q = Wq.xn; k = Wk.xn; v = Wv.xn (l < 24), one grouped launch
+//   attn      q/k norms, RoPE, KV append, split-K decode attention -> qo
+//   gemv      o_raw = Wo.qo
+//   resnorm   x += rms(o_raw)*post_attn_norm; xn = rms(x)*ffn_norm; q8
+//   gemv      hb = gelu(Wgate.xn) * (Wup.xn)           (fused epilogue)
+//   gemv      d_raw = Wdown.hb
+//   resnorm   x += rms(d_raw)*post_ffw_norm
+//   gemv      g = gelu(Winp_gate.x) * ple[l]           (fused epilogue)
+//   gemv      p_raw = Wproj.g
+// then the final residual, output norm, tied LM head + softcap + argmax.
+#include <math.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "g4_internal.cuh"
+#include "g4_kernels.cuh"
+
+namespace g4 {
+
+struct LayerDev {
+    int swa, hd, n_rot, qd, kvd, src;
+    const void *wq, *wk, *wv, *wo, *gate, *up, *down, *inp_gate, *proj;
+    int wq_t, wk_t, wv_t, wo_t, gate_t, up_t, down_t, inp_gate_t, proj_t;
+    const float *attn_norm, *post_attn_norm, *ffn_norm, *post_ffw_norm, *q_norm, *k_norm, *post_norm, *out_scale;
+    float *kc, *vc;
+    int ring;
+};
+
+int prime_kernel_attrs();
+
+}  // namespace g4
+
+using namespace g4;
+
+struct g4_engine {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    int dim = 0, hidden = 0, L = 0, nh = 0, nkv = 0, vocab = 0, pd = 0, window = 0, max_seq = 0, max_batch = 0;
+    int qd_max = 0, kvd_max = 0, hd_max = 0;
+    float eps = 0, softcap = 0, emb_scale = 0, ple_scale = 0, ctx_scale = 0, mix_scale = 0;
+    std::vector<LayerDev> layers;
+    const void *embd = nullptr, *ple_tok = nullptr, *ple_proj = nullptr;
+    int embd_t = 0, ple_tok_t = 0, ple_proj_t = 0;
+    const float *ple_proj_norm = nullptr, *norm_out = nullptr;
+    float2 *rope_swa = nullptr, *rope_full = nullptr;
+    // state
+    float *x = nullptr, *xn = nullptr, *xf = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qn = nullptr,
+          *qo = nullptr, *o_raw = nullptr, *hb = nullptr, *hb2 = nullptr, *d_raw = nullptr, *g = nullptr,
+          *p_raw = nullptr, *ple_tokb = nullptr, *ple_ctx = nullptr, *ple = nullptr, *logits = nullptr,
+          *attn_part = nullptr;
+    uint8_t *q8 = nullptr;
+    int q8_blocks = 0, max_chunks = 0;
+    unsigned long long *keys = nullptr;
+    int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr;
+    int *h_pos = nullptr, *h_tok = nullptr;
+    std::vector<void *> allocs;
+    size_t dev_bytes = 0;
+    std::map<long, cudaGraphExec_t> graphs;
+    int last_lm_mode = 0;
+    std::mutex mu;
+};
+
+namespace {
+
+int dalloc(g4_engine *e, void **p, size_t bytes) {
+    *p = nullptr;
+    if (bytes == 0) bytes = 16;
+    G4_CUDA(cudaMalloc(p, bytes));
+    e->allocs.push_back(*p);
+    e->dev_bytes += bytes;
+    G4_CUDA(cudaMemsetAsync(*p, 0, bytes, e->st));
+    return G4_OK;
+}
+
+template <class T>
+int dalloc_t(g4_engine *e, T **p, size_t count) {
+    void *v = nullptr;
+    int rc = dalloc(e, &v, count * sizeof(T));
+    *p = (T *)v;
+    return rc;
+}
+
+int upload_w(g4_engine *e, const void *host, int type, int n, int rows, const void **out, const char *name) {
+    *out = nullptr;
+    if (!host) { set_error(G4_ERR_ARG, "engine: tensor %s missing", name); return G4_ERR_ARG; }
+    if (!type_known(type)) { set_error(G4_ERR_TYPE, "engine: tensor %s has unsupported type %d", name, type); return G4_ERR_TYPE; }
+    if ((type == G4_Q4_K || type == G4_Q5_K || type == G4_Q6_K) && n % G4_QK) {
+        set_error(G4_ERR_ARG, "engine: tensor %s row length %d not a multiple of 256", name, n);
+        return G4_ERR_ARG;
+    }
+    void *d = nullptr;
+    int rc = dalloc(e, &d, device_tensor_bytes(type, n, rows));
+    if (rc) return rc;
+    rc = upload_tensor(d, host, type, n, rows, e->st);
+    *out = d;
+    return rc;
+}
+
+int upload_f(g4_engine *e, const float *host, int n, const float **out, const char *name, bool optional = false) {
+    *out = nullptr;
+    if (!host) {
+        if (optional) return G4_OK;
+        set_error(G4_ERR_ARG, "engine: vector %s missing", name);
+        return G4_ERR_ARG;
+    }
+    void *d = nullptr;
+    int rc = dalloc(e, &d, (size_t)n * 4);
+    if (rc) return rc;
+    G4_CUDA(cudaMemcpyAsync(d, host, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
+    *out = (const float *)d;
+    return G4_OK;
+}
+
+bool is_swa(const g4_model_desc *m, int l) {  // main.c:716-721
+    if (m->swa_layers) return m->swa_layers[l] != 0;
+    if (m->swa_pattern <= 0) return false;
+    return (l % m->swa_pattern) < (m->swa_pattern - 1);
+}
+
+void destroy(g4_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->st) cudaStreamSynchronize(e->st);
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (void *p : e->allocs) cudaFree(p);
+    if (e->h_pos) cudaFreeHost(e->h_pos);
+    if (e->h_tok) cudaFreeHost(e->h_tok);
+    if (e->st) cudaStreamDestroy(e->st);
+    delete e;
+}
+
+#define TRY(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
+
+// y[B][rows] = W . act for any weight type; act is fp32 [B][ld].  For
+// Q4_K/Q5_K the activation is quantized into e->q8 unless q8_ready.
+int gemv(g4_engine *e, const void *w, int type, int n, int rows, const float *act, int ld, bool q8_ready,
+         float *out, int ldo, int B, int epi = EPI_STORE, const float *evec = nullptr, int ld_evec = 0,
+         unsigned long long *keys = nullptr, float cap = 0.0f) {
+    if (type == G4_F32 || type == G4_F16 || type == G4_BF16) {
+        TRY(launch_gemv_dense(w, type, n, rows, act, ld, out, ldo, B, epi == EPI_SOFTCAP_ARGMAX ? EPI_STORE : epi,
+                              evec, ld_evec, e->st));
+        if (epi == EPI_SOFTCAP_ARGMAX) TRY(launch_softcap_argmax(out, rows, ldo, cap, keys, B, e->st));
+        return G4_OK;
+    }
+    if (is_q8_type(type) && !q8_ready) TRY(launch_quantize_q8k(act, ld, e->q8, n, B, e->st));
+    GemvJobs jobs{};
+    jobs.njobs = 1;
+    GemvJob &J = jobs.j[0];
+    J.w = w; J.type = type; J.n = n; J.rows = rows;
+    J.act = is_q8_type(type) ? (const void *)e->q8 : (const void *)act;
+    J.act_stride = ld; J.out = out; J.out_stride = ldo; J.epi = epi; J.evec = evec; J.ld_evec = ld_evec;
+    J.amax = keys; J.cap = cap;
+    return launch_gemv_kquant(jobs, B, e->st);
+}
+
+int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+    const int dim = e->dim, L = e->L, pd = e->pd;
+    TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
+                       e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
+    TRY(gemv(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
+    TRY(launch_ple_mix(e->ple_tokb, e->ple_ctx, e->ple_proj_norm, pd, L, e->ctx_scale, e->mix_scale, e->eps, e->ple,
+                       B, e->st));
+    for (int l = 0; l < L; l++) {
+        const LayerDev &ly = e->layers[l];
+        const LayerDev *prev = l > 0 ? &e->layers[l - 1] : nullptr;
+        const bool has_kv = l < G4_N_LAYER_KV;
+        const bool q8_in = is_q8_type(ly.wq_t) || (has_kv && (is_q8_type(ly.wk_t) || is_q8_type(ly.wv_t)));
+        ResNorm r{};
+        r.x_in = e->x; r.delta = prev ? e->p_raw : nullptr; r.post_w = prev ? prev->post_norm : nullptr;
+        r.scale = prev ? prev->out_scale : nullptr; r.x_out = e->x; r.pre_w = ly.attn_norm; r.xn_out = e->xn;
+        r.q8_out = q8_in ? e->q8 : nullptr; r.dim = dim; r.eps = e->eps;
+        TRY(launch_resnorm(r, B, e->st));
+
+        // Q / K / V projections (main.c:1884-1891)
+        GemvJobs jobs{};
+        struct Proj { const void *w; int t; int rows; float *out; };
+        Proj pr[3] = {{ly.wq, ly.wq_t, ly.qd, e->q}, {ly.wk, ly.wk_t, ly.kvd, e->k}, {ly.wv, ly.wv_t, ly.kvd, e->v}};
+        const int np = has_kv ? 3 : 1;
+        for (int i = 0; i < np; i++) {
+            if (pr[i].t == G4_F32 || pr[i].t == G4_F16 || pr[i].t == G4_BF16) {
+                TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
+                continue;
+            }
+            GemvJob &J = jobs.j[jobs.njobs++];
+            J.w = pr[i].w; J.type = pr[i].t; J.n = dim; J.rows = pr[i].rows;
+            J.act = is_q8_type(pr[i].t) ? (const void *)e->q8 : (const void *)e->xn;
+            J.act_stride = dim; J.out = pr[i].out; J.out_stride = pr[i].rows; J.epi = EPI_STORE;
+        }
+        if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
+
+        // attention (main.c:1886-1950)
+        AttnLayer A{};
+        A.hd = ly.hd; A.n_rot = ly.n_rot; A.n_heads = e->nh; A.n_kv = e->nkv;
+        A.q_norm = ly.q_norm; A.k_norm = ly.k_norm;
+        A.rope = ly.swa ? e->rope_swa : e->rope_full;
+        A.append = has_kv; A.kc = ly.kc; A.vc = ly.vc; A.ring = ly.ring;
+        const LayerDev &src = e->layers[ly.src];
+        A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
+        A.window = ly.swa ? e->window : 0;
+        A.eps = e->eps;
+        TRY(launch_attn_prep(A, e->q, e->k, e->v, e->qn, B, e->d_pos, e->max_seq, e->st));
+        TRY(launch_attn_decode(A, e->qn, e->attn_part, e->qo, B, e->d_pos, e->max_chunks, e->max_seq, e->st));
+
+        // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
+        TRY(gemv(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
+        const bool q8_ffn = is_q8_type(ly.gate_t) || is_q8_type(ly.up_t);
+        ResNorm r2{};
+        r2.x_in = e->x; r2.delta = e->o_raw; r2.post_w = ly.post_attn_norm; r2.x_out = e->x; r2.pre_w = ly.ffn_norm;
+        r2.xn_out = e->xn; r2.q8_out = q8_ffn ? e->q8 : nullptr; r2.dim = dim; r2.eps = e->eps;
+        TRY(launch_resnorm(r2, B, e->st));
+
+        // gate / up with the GELU product fused (1976-1978)
+        const bool kq = !(ly.gate_t == G4_F32 || ly.gate_t == G4_F16 || ly.gate_t == G4_BF16);
+        if (kq && ly.gate_t == ly.up_t) {
+            GemvJobs fj{};
+            fj.njobs = 1;
+            GemvJob &J = fj.j[0];
+            J.w = ly.gate; J.w2 = ly.up; J.type = ly.gate_t; J.n = dim; J.rows = e->hidden;
+            J.act = is_q8_type(ly.gate_t) ? (const void *)e->q8 : (const void *)e->xn;
+            J.act_stride = dim; J.out = e->hb; J.out_stride = e->hidden; J.epi = EPI_GELU_MUL;
+            TRY(launch_gemv_kquant(fj, B, e->st));
+        } else {
+            TRY(gemv(e, ly.gate, ly.gate_t, dim, e->hidden, e->xn, dim, is_q8_type(ly.gate_t), e->hb, e->hidden, B));
+            TRY(gemv(e, ly.up, ly.up_t, dim, e->hidden, e->xn, dim, is_q8_type(ly.up_t), e->hb2, e->hidden, B));
+            TRY(launch_gelu_mul(e->hb, e->hb2, (size_t)B * e->hidden, e->st));
+        }
+        // down projection, post-FFN norm + residual (1979-1984)
+        TRY(gemv(e, ly.down, ly.down_t, e->hidden, dim, e->hb, e->hidden, false, e->d_raw, dim, B));
+        ResNorm r3{};
+        r3.x_in = e->x; r3.delta = e->d_raw; r3.post_w = ly.post_ffw_norm; r3.x_out = e->x; r3.dim = dim;
+        r3.eps = e->eps;
+        TRY(launch_resnorm(r3, B, e->st));
+        // per-layer embedding injection (1986-1997)
+        TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
+                 e->ple + (size_t)l * pd, pd * L));
+        TRY(gemv(e, ly.proj, ly.proj_t, pd, dim, e->g, pd, false, e->p_raw, dim, B));
+    }
+    // last residual + out_scale (1995-2003), output norm (2021)
+    const LayerDev &last = e->layers[L - 1];
+    ResNorm rf{};
+    rf.x_in = e->x; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = e->x;
+    rf.pre_w = lm_mode ? e->norm_out : nullptr; rf.xn_out = e->xf; rf.dim = dim; rf.eps = e->eps;
+    TRY(launch_resnorm(rf, B, e->st));
+    if (!lm_mode) return G4_OK;
+    // tied LM head + softcap + first-max argmax (1780-1796, 2045-2050)
+    G4_CUDA(cudaMemsetAsync(e->keys, 0, sizeof(unsigned long long) * B, e->st));
+    const bool dense = e->embd_t == G4_F32 || e->embd_t == G4_F16 || e->embd_t == G4_BF16;
+    TRY(gemv(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, (want_logits || dense) ? e->logits : nullptr,
+             e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
+    TRY(launch_keys_to_tokens(e->keys, e->d_next, B, e->st));
+    return G4_OK;
+}
+
+int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+    const long key = ((long)B << 8) | ((long)lm_mode << 2) | ((long)from_keys << 1) | (long)want_logits;
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        G4_CUDA(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_step(e, B, lm_mode, from_keys, want_logits);
+        cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture", __FILE__, __LINE__);
+        cudaGraphExec_t ge = nullptr;
+        ce = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate", __FILE__, __LINE__);
+        it = e->graphs.emplace(key, ge).first;
+    }
+    G4_CUDA(cudaGraphLaunch(it->second, e->st));
+    e->last_lm_mode = lm_mode;
+    return G4_OK;
+}
+
+int set_pos(g4_engine *e, int pos) {
+    if (pos < 0 || pos >= e->max_seq) {
+        set_error(G4_ERR_STATE, "position %d outside [0, max_seq=%d)", pos, e->max_seq);
+        return G4_ERR_STATE;
+    }
+    G4_CUDA(cudaMemcpyAsync(e->d_pos, e->h_pos + pos, 4, cudaMemcpyHostToDevice, e->st));
+    return G4_OK;
+}
+
+int stage_tokens(g4_engine *e, const int *tokens, int B, int pos) {
+    int *h = e->h_tok + (size_t)pos * e->max_batch;
+    for (int b = 0; b < B; b++) {
+        if (tokens[b] < 0 || tokens[b] >= e->vocab) {
+            set_error(G4_ERR_ARG, "token %d outside the vocabulary (%d)", tokens[b], e->vocab);
+            return G4_ERR_ARG;
+        }
+        h[b] = tokens[b];
+    }
+    G4_CUDA(cudaMemcpyAsync(e->d_tokens, h, sizeof(int) * B, cudaMemcpyHostToDevice, e->st));
+    return G4_OK;
+}
+
+int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
+    if (!m || max_seq <= 0 || max_batch <= 0) { set_error(G4_ERR_ARG, "engine: bad arguments"); return G4_ERR_ARG; }
+    if (m->dim <= 0 || m->dim % G4_QK || m->hidden_dim <= 0 || m->n_layers <= 0 || m->n_heads <= 0 ||
+        m->n_kv_heads <= 0 || m->n_heads % m->n_kv_heads || m->vocab_size <= 0 || m->ple_dim <= 0 || m->ple_dim > 1024 ||
+        m->dim > 12288) {
+        set_error(G4_ERR_ARG, "engine: unsupported model shape");
+        return G4_ERR_ARG;
+    }
+    e->dim = m->dim; e->hidden = m->hidden_dim; e->L = m->n_layers; e->nh = m->n_heads; e->nkv = m->n_kv_heads;
+    e->vocab = m->vocab_size; e->pd = m->ple_dim; e->window = m->sliding_window; e->max_seq = max_seq;
+    e->max_batch = max_batch; e->eps = m->norm_eps; e->softcap = m->logit_softcapping;
+    // scale constants exactly as the reference computes them (main.c:1851, 1757, 1762, 1769)
+    e->emb_scale = sqrtf((float)m->dim);
+    e->ple_scale = sqrtf((float)m->ple_dim);
+    e->ctx_scale = 1.0f / sqrtf((float)m->dim);
+    e->mix_scale = 1.0f / sqrtf(2.0f);
+
+    G4_CUDA(cudaSetDevice(e->device));
+    cudaDeviceProp p;
+    G4_CUDA(cudaGetDeviceProperties(&p, e->device));
+    if (p.major != 10) { set_error(G4_ERR_NO_DEVICE, "device %d is not sm_100", e->device); return G4_ERR_NO_DEVICE; }
+    G4_CUDA(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
+    TRY(prime_kernel_attrs());
+
+    const int L = e->L, dim = e->dim, pd = e->pd;
+    TRY(upload_w(e, m->embd, m->embd_t, dim, e->vocab, &e->embd, "token_embd"));
+    e->embd_t = m->embd_t;
+    TRY(upload_w(e, m->ple_tok, m->ple_tok_t, pd * L, e->vocab, &e->ple_tok, "per_layer_token_embd"));
+    e->ple_tok_t = m->ple_tok_t;
+    TRY(upload_w(e, m->ple_proj, m->ple_proj_t, dim, pd * L, &e->ple_proj, "per_layer_model_proj"));
+    e->ple_proj_t = m->ple_proj_t;
+    TRY(upload_f(e, m->ple_proj_norm, pd, &e->ple_proj_norm, "per_layer_proj_norm"));
+    TRY(upload_f(e, m->norm_out, dim, &e->norm_out, "output_norm"));
+
+    e->layers.resize(L);
+    char nm[64];
+    for (int l = 0; l < L; l++) {
+        LayerDev &ly = e->layers[l];
+        memset(&ly, 0, sizeof ly);
+        ly.swa = is_swa(m, l);
+        ly.hd = ly.swa ? m->head_dim_swa : m->head_dim_full;
+        ly.n_rot = ly.swa ? m->n_rot_swa : m->n_rot_full;
+        if (ly.hd != 64 && ly.hd != 128 && ly.hd != 256 && ly.hd != 512) {
+            set_error(G4_ERR_ARG, "engine: layer %d head_dim %d unsupported", l, ly.hd);
+            return G4_ERR_ARG;
+        }
+        if (ly.n_rot < 0 || ly.n_rot > ly.hd || ly.n_rot % 2) { set_error(G4_ERR_ARG, "engine: layer %d n_rot %d", l, ly.n_rot); return G4_ERR_ARG; }
+        ly.qd = e->nh * ly.hd;
+        ly.kvd = e->nkv * ly.hd;
+        e->qd_max = ly.qd > e->qd_max ? ly.qd : e->qd_max;
+        e->kvd_max = ly.kvd > e->kvd_max ? ly.kvd : e->kvd_max;
+        e->hd_max = ly.hd > e->hd_max ? ly.hd : e->hd_max;
+#define W(field, n_in, rows)                                                                     \
+    do {                                                                                         \
+        snprintf(nm, sizeof nm, "blk.%d." #field, l);                                            \
+        ly.field##_t = m->field##_t[l];                                                          \
+        TRY(upload_w(e, m->field[l], ly.field##_t, n_in, rows, &ly.field, nm));                  \
+    } while (0)
+#define V(field, n, opt)                                                                         \
+    do {                                                                                         \
+        snprintf(nm, sizeof nm, "blk.%d." #field, l);                                            \
+        TRY(upload_f(e, m->field ? m->field[l] : nullptr, n, &ly.field, nm, opt));               \
+    } while (0)
+        W(wq, dim, ly.qd);
+        if (l < G4_N_LAYER_KV) { W(wk, dim, ly.kvd); W(wv, dim, ly.kvd); }
+        W(wo, ly.qd, dim);
+        W(gate, dim, e->hidden);
+        W(up, dim, e->hidden);
+        W(down, e->hidden, dim);
+        W(inp_gate, dim, pd);
+        W(proj, pd, dim);
+        V(attn_norm, dim, false); V(post_attn_norm, dim, false); V(ffn_norm, dim, false); V(post_ffw_norm, dim, false);
+        V(q_norm, ly.hd, false); V(k_norm, ly.hd, false); V(post_norm, dim, false); V(out_scale, 1, true);
+#undef W
+#undef V
+        if (is_q8_type(ly.wo_t) && ly.qd % G4_QK) { set_error(G4_ERR_ARG, "engine: q_dim %d not a multiple of 256", ly.qd); return G4_ERR_ARG; }
+        if (is_q8_type(ly.proj_t) && pd % G4_QK) { set_error(G4_ERR_ARG, "engine: ple_dim %d with a K-quant proj", pd); return G4_ERR_ARG; }
+    }
+    // KV caches and shared-KV sources (main.c:739-746, 1402-1404)
+    for (int l = 0; l < L; l++) {
+        LayerDev &ly = e->layers[l];
+        if (l < G4_N_LAYER_KV) {
+            ly.src = l;
+            ly.ring = (ly.swa && e->window > 0 && e->window < max_seq) ? e->window : max_seq;
+            const size_t n = (size_t)max_batch * e->nkv * ly.ring * ly.hd;
+            TRY(dalloc_t(e, &ly.kc, n));
+            TRY(dalloc_t(e, &ly.vc, n));
+        } else {
+            ly.src = ly.swa ? 22 : 23;
+            const LayerDev &s = e->layers[ly.src];
+            if (s.hd != ly.hd || (!ly.swa && s.ring < max_seq)) {
+                set_error(G4_ERR_ARG, "engine: layer %d cannot read the KV of layer %d", l, ly.src);
+                return G4_ERR_ARG;
+            }
+        }
+    }
+    // RoPE tables (host libm, reference-exact angles)
+    {
+        std::vector<float2> t;
+        const int hs = m->n_rot_swa / 2 > 0 ? m->n_rot_swa / 2 : 1, hf = m->n_rot_full / 2 > 0 ? m->n_rot_full / 2 : 1;
+        t.resize((size_t)max_seq * hs);
+        rope_table_host(t.data(), max_seq, m->n_rot_swa, m->rope_theta_swa, 1.0f, nullptr);
+        TRY(dalloc_t(e, &e->rope_swa, t.size()));
+        G4_CUDA(cudaMemcpyAsync(e->rope_swa, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice, e->st));
+        G4_CUDA(cudaStreamSynchronize(e->st));
+        t.assign((size_t)max_seq * hf, make_float2(0, 0));
+        rope_table_host(t.data(), max_seq, m->n_rot_full, m->rope_theta, 1.0f, m->rope_freqs);
+        TRY(dalloc_t(e, &e->rope_full, t.size()));
+        G4_CUDA(cudaMemcpyAsync(e->rope_full, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice, e->st));
+        G4_CUDA(cudaStreamSynchronize(e->st));
+    }
+    // activations
+    const size_t B = max_batch;
+    TRY(dalloc_t(e, &e->x, B * dim)); TRY(dalloc_t(e, &e->xn, B * dim)); TRY(dalloc_t(e, &e->xf, B * dim));
+    TRY(dalloc_t(e, &e->q, B * e->qd_max)); TRY(dalloc_t(e, &e->qn, B * e->qd_max)); TRY(dalloc_t(e, &e->qo, B * e->qd_max));
+    TRY(dalloc_t(e, &e->k, B * e->kvd_max)); TRY(dalloc_t(e, &e->v, B * e->kvd_max));
+    TRY(dalloc_t(e, &e->o_raw, B * dim)); TRY(dalloc_t(e, &e->d_raw, B * dim)); TRY(dalloc_t(e, &e->p_raw, B * dim));
+    TRY(dalloc_t(e, &e->hb, B * e->hidden)); TRY(dalloc_t(e, &e->hb2, B * e->hidden));
+    TRY(dalloc_t(e, &e->g, B * pd));
+    TRY(dalloc_t(e, &e->ple_tokb, B * pd * L)); TRY(dalloc_t(e, &e->ple_ctx, B * pd * L)); TRY(dalloc_t(e, &e->ple, B * pd * L));
+    TRY(dalloc_t(e, &e->logits, B * e->vocab));
+    int nmax = dim > e->qd_max ? dim : e->qd_max;
+    nmax = nmax > e->hidden ? nmax : e->hidden;
+    nmax = nmax > pd ? nmax : pd;
+    e->q8_blocks = (nmax + G4_QK - 1) / G4_QK;
+    TRY(dalloc_t(e, &e->q8, B * e->q8_blocks * G4_Q8_BYTES));
+    e->max_chunks = (max_seq + attn_chunk_size() - 1) / attn_chunk_size();
+    TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
+    TRY(dalloc_t(e, &e->keys, B));
+    TRY(dalloc_t(e, &e->d_tokens, B)); TRY(dalloc_t(e, &e->d_next, B)); TRY(dalloc_t(e, &e->d_pos, 1));
+    TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * B));
+    G4_CUDA(cudaMallocHost((void **)&e->h_pos, sizeof(int) * (size_t)max_seq));
+    for (int i = 0; i < max_seq; i++) e->h_pos[i] = i;
+    G4_CUDA(cudaMallocHost((void **)&e->h_tok, sizeof(int) * (size_t)max_seq * B));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+g4_engine *g4_engine_create(const g4_model_desc *m, int device, int max_seq, int max_batch) {
+    g4_engine *e = new g4_engine();
+    e->device = device;
+    if (create(e, m, max_seq, max_batch) != G4_OK) {
+        const int code = g4_last_error();
+        char msg[512];
+        snprintf(msg, sizeof msg, "%s", g4_last_error_string());
+        destroy(e);
+        set_error(code ? code : G4_ERR_CUDA, "%s", msg);
+        return nullptr;
+    }
+    return e;
+}
+
+int g4_engine_destroy(g4_engine *e) {
+    destroy(e);
+    return G4_OK;
+}
+
+size_t g4_engine_device_bytes(const g4_engine *e) { return e ? e->dev_bytes : 0; }
+
+size_t g4_model_desc_bytes(void) { return sizeof(g4_model_desc); }
+
+void *g4_engine_stream(g4_engine *e) { return e ? (void *)e->st : nullptr; }
+
+int g4_engine_sync(g4_engine *e) {
+    if (!e) { set_error(G4_ERR_ARG, "engine is NULL"); return G4_ERR_ARG; }
+    G4_CUDA(cudaSetDevice(e->device));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
+int g4_forward(g4_engine *e, int token, int pos, int lm_mode, float *logits) {
+    if (!e || lm_mode < 0 || lm_mode > 2) { set_error(G4_ERR_ARG, "forward: bad arguments"); return -1; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (cudaSetDevice(e->device) != cudaSuccess) { set_error(G4_ERR_CUDA, "cudaSetDevice failed"); return -1; }
+    if (set_pos(e, pos) || stage_tokens(e, &token, 1, pos)) return -1;
+    if (run_step(e, 1, lm_mode, false, lm_mode != 0 && logits != nullptr)) return -1;
+    int next = 0;
+    if (lm_mode) {
+        if (cudaMemcpyAsync(&next, e->d_next, 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) { set_error(G4_ERR_CUDA, "readback failed"); return -1; }
+        if (logits && cudaMemcpyAsync(logits, e->logits, sizeof(float) * e->vocab, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) {
+            set_error(G4_ERR_CUDA, "logits readback failed");
+            return -1;
+        }
+    }
+    cudaError_t ce = cudaStreamSynchronize(e->st);
+    if (ce != cudaSuccess) { cuda_fail(ce, "forward", __FILE__, __LINE__); return -1; }
+    return next;
+}
+
+int g4_generate_greedy(g4_engine *e, const int *prompt, int n_prompt, int max_new, int eos, int *out_tokens) {
+    if (!e || !prompt || n_prompt <= 0 || max_new < 0 || (max_new > 0 && !out_tokens)) {
+        set_error(G4_ERR_ARG, "generate: bad arguments");
+        return -1;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (cudaSetDevice(e->device) != cudaSuccess) { set_error(G4_ERR_CUDA, "cudaSetDevice failed"); return -1; }
+    int total = n_prompt + max_new - 1;  // generate's position loop (main.c:2366-2370)
+    if (total > e->max_seq) total = e->max_seq;
+    int ngen = 0;
+    for (int pos = 0; pos < total; pos++) {
+        const int lm = pos < n_prompt - 1 ? 0 : 1;
+        if (set_pos(e, pos)) return -1;
+        const bool from_keys = pos >= n_prompt;
+        if (!from_keys && stage_tokens(e, prompt + pos, 1, pos)) return -1;
+        if (run_step(e, 1, lm, from_keys, false)) return -1;
+        if (lm) {
+            if (cudaMemcpyAsync(e->d_hist + ngen, e->d_next, 4, cudaMemcpyDeviceToDevice, e->st) != cudaSuccess) {
+                set_error(G4_ERR_CUDA, "history copy failed");
+                return -1;
+            }
+            ngen++;
+        }
+    }
+    if (ngen && cudaMemcpyAsync(out_tokens, e->d_hist, sizeof(int) * ngen, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) {
+        set_error(G4_ERR_CUDA, "history readback failed");
+        return -1;
+    }
+    cudaError_t ce = cudaStreamSynchronize(e->st);
+    if (ce != cudaSuccess) { cuda_fail(ce, "generate", __FILE__, __LINE__); return -1; }
+    for (int i = 0; i < ngen; i++)
+        if (out_tokens[i] == eos) return i;  // the reference stops before emitting eos (main.c:2435)
+    return ngen;
+}
+
+int g4_decode_batch(g4_engine *e, int B, const int *tokens, int pos, int lm_mode, int *next) {
+    if (!e || !tokens || B <= 0 || lm_mode < 0 || lm_mode > 2 || (lm_mode && !next)) { set_error(G4_ERR_ARG, "decode_batch: bad arguments"); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (B > e->max_batch) { set_error(G4_ERR_STATE, "batch %d > engine max_batch %d", B, e->max_batch); return G4_ERR_STATE; }
+    G4_CUDA(cudaSetDevice(e->device));
+    TRY(set_pos(e, pos));
+    TRY(stage_tokens(e, tokens, B, pos));
+    TRY(run_step(e, B, lm_mode, false, false));
+    if (lm_mode) G4_CUDA(cudaMemcpyAsync(next, e->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, e->st));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
+int g4_decode_batch_device(g4_engine *e, int B, const int *tokens_dev, int pos, int lm_mode, int *next_dev) {
+    if (!e || B <= 0 || lm_mode < 0 || lm_mode > 2) { set_error(G4_ERR_ARG, "decode_batch_device: bad arguments"); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (B > e->max_batch) { set_error(G4_ERR_STATE, "batch %d > engine max_batch %d", B, e->max_batch); return G4_ERR_STATE; }
+    G4_CUDA(cudaSetDevice(e->device));
+    TRY(set_pos(e, pos));
+    if (tokens_dev) G4_CUDA(cudaMemcpyAsync(e->d_tokens, tokens_dev, sizeof(int) * B, cudaMemcpyDeviceToDevice, e->st));
+    TRY(run_step(e, B, lm_mode, tokens_dev == nullptr, false));
+    if (lm_mode && next_dev) G4_CUDA(cudaMemcpyAsync(next_dev, e->d_next, sizeof(int) * B, cudaMemcpyDeviceToDevice, e->st));
+    return G4_OK;
+}
+
+int g4_engine_get_hidden(g4_engine *e, int b, float *x) {
+    if (!e || !x || b < 0 || b >= e->max_batch) { set_error(G4_ERR_ARG, "get_hidden: bad arguments"); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    G4_CUDA(cudaSetDevice(e->device));
+    // after an LM-head step the reference's State.x holds the output-normed vector (main.c:2021)
+    const float *src = (e->last_lm_mode ? e->xf : e->x) + (size_t)b * e->dim;
+    G4_CUDA(cudaMemcpyAsync(x, src, sizeof(float) * e->dim, cudaMemcpyDeviceToHost, e->st));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
+int g4_engine_get_kv(g4_engine *e, int b, int layer, int pos, float *k, float *v) {
+    if (!e || b < 0 || b >= e->max_batch || layer < 0 || layer >= e->L || layer >= G4_N_LAYER_KV || pos < 0 ||
+        pos >= e->max_seq) {
+        set_error(G4_ERR_ARG, "get_kv: bad arguments");
+        return G4_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    G4_CUDA(cudaSetDevice(e->device));
+    const LayerDev &ly = e->layers[layer];
+    const int slot = pos % ly.ring;
+    for (int h = 0; h < e->nkv; h++) {
+        const size_t row = (((size_t)b * e->nkv + h) * ly.ring + slot) * ly.hd;
+        if (k) G4_CUDA(cudaMemcpyAsync(k + (size_t)h * ly.hd, ly.kc + row, sizeof(float) * ly.hd, cudaMemcpyDeviceToHost, e->st));
+        if (v) G4_CUDA(cudaMemcpyAsync(v + (size_t)h * ly.hd, ly.vc + row, sizeof(float) * ly.hd, cudaMemcpyDeviceToHost, e->st));
+    }
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
+}  // extern "C"

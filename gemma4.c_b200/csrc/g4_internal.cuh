@@ -1,0 +1,116 @@
+// g4_internal.cuh — shared device/host internals of libg4b200 (sm_100a).
+//
+// Weight tensors keep the GGUF super-block layouts of
+// gemma4-4b/cpu-blas/main.c:95-115 in HBM (Q4_K 144 B and Q5_K 176 B blocks
+// are multiples of 16 B, so a row is read with 128-bit loads), except Q6_K:
+// its 210-byte blocks are not 16-byte aligned, so the device copy of a Q6_K
+// tensor is split into four planes (ql 128 B, qh 64 B, scales 16 B per block,
+// then the fp16 d of every block) — same bytes, 16-byte aligned vector loads.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/g4b200.h"
+
+#define G4_QK 256
+#define G4_Q8_BYTES 292
+#define G4_N_LAYER_KV 24  // layers 0..23 store KV, main.c:77
+
+namespace g4 {
+
+// ---------------------------------------------------------------- errors
+void set_error(int code, const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
+#define G4_CUDA(call)                                                       \
+    do {                                                                    \
+        cudaError_t e_ = (call);                                            \
+        if (e_ != cudaSuccess) return ::g4::cuda_fail(e_, #call, __FILE__, __LINE__); \
+    } while (0)
+#define G4_LAUNCHED() ::g4::note_launch()
+void note_launch();
+
+inline size_t block_bytes(int type) {
+    return type == G4_Q4_K ? 144 : type == G4_Q5_K ? 176 : type == G4_Q6_K ? 210 : 0;
+}
+inline size_t row_bytes(int type, int n) {
+    if (type == G4_F32) return (size_t)n * 4;
+    if (type == G4_F16 || type == G4_BF16) return (size_t)n * 2;
+    return (size_t)(n / G4_QK) * block_bytes(type);
+}
+inline bool type_known(int t) {
+    return t == G4_F32 || t == G4_F16 || t == G4_BF16 || t == G4_Q4_K || t == G4_Q5_K || t == G4_Q6_K;
+}
+inline bool is_q8_type(int t) { return t == G4_Q4_K || t == G4_Q5_K; }  // is_q8_mm_type, main.c:615-617
+
+// Device copy of a Q6_K tensor with R rows of nb blocks (NB = R*nb blocks):
+//   ql plane NB*128 | qh plane NB*64 | sc plane NB*16 | d plane NB*2 (+pad)
+struct Q6Planes {
+    const uint4 *ql;
+    const uint4 *qh;
+    const uint4 *sc;
+    const uint16_t *d;
+};
+inline size_t q6_device_bytes(size_t nblocks) { return nblocks * 208 + ((nblocks * 2 + 15) & ~(size_t)15); }
+__host__ __device__ inline Q6Planes q6_planes(const void *base, size_t nblocks) {
+    const uint8_t *b = (const uint8_t *)base;
+    Q6Planes p;
+    p.ql = (const uint4 *)b;
+    p.qh = (const uint4 *)(b + nblocks * 128);
+    p.sc = (const uint4 *)(b + nblocks * 192);
+    p.d = (const uint16_t *)(b + nblocks * 208);
+    return p;
+}
+// Device byte size of a weight tensor of `rows` rows of `n` elements.
+inline size_t device_tensor_bytes(int type, int n, int rows) {
+    if (type == G4_Q6_K) return q6_device_bytes((size_t)rows * (n / G4_QK));
+    return row_bytes(type, n) * (size_t)rows;
+}
+
+// Host -> device upload of one weight tensor (Q6_K is split into planes).
+int upload_tensor(void *dst_dev, const void *src_host, int type, int n, int rows, cudaStream_t st);
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ float f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+template <int W = 32>
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, W);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// 6-bit scale and min of sub-block j of a Q4_K/Q5_K block (the bit packing
+// of get_scale_min_k4, main.c:162-170).  s0/s1/s2 are scale bytes 0-3/4-7/8-11.
+__device__ __forceinline__ void k4_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2, int &sc, int &mn) {
+    if (j < 4) {
+        sc = (s0 >> (8 * j)) & 63;
+        mn = (s1 >> (8 * j)) & 63;
+    } else {
+        const int i = j - 4;
+        const uint32_t b8 = (s2 >> (8 * i)) & 0xff;       // byte j+4
+        sc = (int)((b8 & 15) | (((s0 >> (8 * i + 6)) & 3) << 4));
+        mn = (int)((b8 >> 4) | (((s1 >> (8 * i + 6)) & 3) << 4));
+    }
+}
+
+// Packed (value, index) key whose unsigned max is the largest value with the
+// LOWEST index among equals: the first-max rule of sample_token
+// (main.c:2045-2050).  NaN is not expected (softcapped logits are finite).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // order-preserving map
+    return ((unsigned long long)b << 32) | (uint32_t)(0xffffffffu - (uint32_t)idx);
+}
+__host__ __device__ inline int argmax_key_index(unsigned long long k) {
+    return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+}
+
+}  // namespace g4

@@ -1,0 +1,90 @@
+// g4_kernels.cuh — launchers of the sm_100a kernels (internal to libg4b200).
+#pragma once
+#include "g4_internal.cuh"
+
+namespace g4 {
+
+enum Epilogue {
+    EPI_STORE = 0,           // out[row] = acc
+    EPI_GELU_MUL = 1,        // out[row] = gelu(acc(w)) * acc(w2)        (FFN, main.c:1973-1978)
+    EPI_SOFTCAP_ARGMAX = 2,  // out[row] = cap*tanh(acc/cap); argmax key (LM head, main.c:1780-1796)
+    EPI_GELU_SCALE = 3       // out[row] = gelu(acc) * evec[row]           (PLE gate, main.c:1986-1991)
+};
+
+constexpr int kMaxJobs = 3;
+
+// One matrix of a grouped K-quant GEMV launch.
+struct GemvJob {
+    const void *w;       // device tensor (GGUF blocks; Q6_K as planes)
+    const void *w2;      // second matrix of EPI_GELU_MUL (same type and shape) or null
+    const void *act;     // Q4/Q5: BlockQ8_K [B][n/256];  Q6: fp32 [B][act_stride]
+    float *out;          // [B][out_stride] (may be null for EPI_SOFTCAP_ARGMAX)
+    unsigned long long *amax;  // [B] argmax keys for EPI_SOFTCAP_ARGMAX
+    const float *evec;   // [B][ld_evec] multiplier of EPI_GELU_SCALE
+    int type, n, rows, act_stride, out_stride, epi, rt, cta_begin, ld_evec;
+    float cap;
+};
+struct GemvJobs {
+    GemvJob j[kMaxJobs];
+    int njobs;
+};
+
+int default_rt(int type, int n, int rows);
+int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStream_t st);
+int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st);
+int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
+                      int B, int epi, const float *evec, int ld_evec, cudaStream_t st);
+int launch_qk_block_sums(const void *w, int type, int n, int rows, const void *q8, int *ss, int *sm,
+                         cudaStream_t st);
+
+// ---- attention (k_attn.cu)
+
+// Neox RoPE cos/sin table: cs[pos][j] = (cos, sin) of the reference angle
+// for pair j < n_rot/2 (computed on the host, see rope_table_host).
+struct AttnLayer {
+    int hd, n_rot, n_heads, n_kv;
+    const float *q_norm, *k_norm;   // device [hd]
+    const float2 *rope;             // device [max_seq][n_rot/2]
+    int append;                     // 1: this layer stores K/V (l < 24)
+    float *kc, *vc;                 // cache of THIS layer (append target)
+    int ring;                       // slots of this layer's cache (window ring or max_seq)
+    const float *src_kc, *src_vc;   // cache read by attention (this layer or 22/23)
+    int src_ring;                   // slots of the source cache
+    int window;                     // 0: full causal, else sliding window
+    float eps;
+};
+int launch_attn_prep(const AttnLayer &L, const float *q, const float *k, const float *v, float *qn, int B,
+                     const int *pos_dev, int max_seq, cudaStream_t st);
+int launch_attn_decode(const AttnLayer &L, const float *qn, float *part, float *qo, int B, const int *pos_dev,
+                       int max_chunks, int max_seq, cudaStream_t st);
+int attn_chunk_size();
+// Host: reference-exact RoPE table for positions [0, npos).
+void rope_table_host(float2 *out, int npos, int n_rot, float base, float freq_scale, const float *ff);
+
+// ---- glue (k_glue.cu)
+struct ResNorm {
+    const float *x_in;      // [B][dim] residual stream
+    const float *delta;     // [B][dim] sublayer output or null
+    const float *post_w;    // norm weight for delta
+    const float *scale;     // layer_output_scale (device, 1 float) or null
+    float *x_out;           // [B][dim] (may alias x_in)
+    const float *pre_w;     // pre-norm weight or null
+    float *xn_out;          // [B][dim] normed output (pre_w) or null
+    void *q8_out;           // [B][dim/256] BlockQ8_K of xn_out or null
+    int dim;
+    float eps;
+};
+int launch_resnorm(const ResNorm &r, int B, cudaStream_t st);
+int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
+                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, const unsigned long long *keys,
+                   float *x, float *ple_out, int B, cudaStream_t st);
+int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st);
+int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned long long *keys, int B,
+                          cudaStream_t st);
+int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, size_t nblk_total,
+                     cudaStream_t st);
+int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, int pd, int L, float ctx_scale,
+                   float mix_scale, float eps, float *ple_out, int B, cudaStream_t st);
+int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
+
+}  // namespace g4

@@ -1,0 +1,317 @@
+// k_glue.cu — the per-step glue of forward around the GEMVs and attention.
+//
+//   resnorm   x = (x + rmsnorm(delta)*w_post) * out_scale, then the next
+//             pre-norm xn = rmsnorm(x)*w_pre and its Q8_K quantization
+//             (residual chain of main.c:1959-2003, norms 1451-1456,
+//             quantize_row_q8_K 282-340).  One CTA per sequence.
+//   embed     token row of token_embd times sqrt(dim) and the per-layer
+//             token row times sqrt(ple_dim) (main.c:1849-1854, 1753-1758,
+//             emb_lookup 1696-1723).  The token comes from a token array or
+//             straight from the previous step's argmax keys.
+//   ple_mix   ple = (tok + rmsnorm(ctx / sqrt(dim)) * w) / sqrt(2) per layer
+//             (build_ple, main.c:1760-1777).
+#include <math.h>
+
+#include "g4_internal.cuh"
+#include "g4_kernels.cuh"
+#include "g4_quant.cuh"
+
+namespace g4 {
+
+__device__ __forceinline__ float cta_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int nw = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    return t;
+}
+
+// rmsnorm (main.c:1451-1456): o = (x * (1/sqrt(mean(x^2) + eps))) * w
+__global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
+    extern __shared__ __align__(16) float xs[];  // [dim] x, then [dim] xn
+    __shared__ float red[32];
+    const int b = blockIdx.x, dim = r.dim, tid = threadIdx.x;
+    float *xn = xs + dim;
+    const float *xi = r.x_in + (size_t)b * dim;
+    for (int i = tid; i < dim; i += blockDim.x) xs[i] = xi[i];
+    if (r.delta) {
+        const float *dl = r.delta + (size_t)b * dim;
+        float ss = 0.0f;
+        for (int i = tid; i < dim; i += blockDim.x) ss = fmaf(dl[i], dl[i], ss);
+        ss = cta_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
+        for (int i = tid; i < dim; i += blockDim.x)
+            xs[i] = __fadd_rn(xs[i], __fmul_rn(__fmul_rn(dl[i], inv), r.post_w[i]));
+    }
+    if (r.scale) {
+        const float sc = *r.scale;
+        for (int i = tid; i < dim; i += blockDim.x) xs[i] = xs[i] * sc;
+    }
+    __syncthreads();
+    if (r.x_out) {
+        float *xo = r.x_out + (size_t)b * dim;
+        for (int i = tid; i < dim; i += blockDim.x) xo[i] = xs[i];
+    }
+    if (!r.pre_w) return;
+    float ss = 0.0f;
+    for (int i = tid; i < dim; i += blockDim.x) ss = fmaf(xs[i], xs[i], ss);
+    ss = cta_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
+    for (int i = tid; i < dim; i += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(xs[i], inv), r.pre_w[i]);
+        xn[i] = v;
+        if (r.xn_out) r.xn_out[(size_t)b * dim + i] = v;
+    }
+    if (!r.q8_out) return;
+    __syncthreads();
+    const int nb = dim / G4_QK, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    uint8_t *q8 = (uint8_t *)r.q8_out + (size_t)b * nb * G4_Q8_BYTES;
+    for (int k = warp; k < nb; k += nw) {
+        uint32_t q[2];
+        float d;
+        int ls;
+        warp_quant_block(xn + k * G4_QK, lane, q, d, ls);
+        store_q8_block(q8 + (size_t)k * G4_Q8_BYTES, lane, q, d, ls);
+    }
+}
+
+int launch_resnorm(const ResNorm &r, int B, cudaStream_t st) {
+    if (r.q8_out && r.dim % G4_QK) { set_error(G4_ERR_ARG, "resnorm: dim %d not a multiple of 256", r.dim); return G4_ERR_ARG; }
+    const size_t smem = (size_t)r.dim * 8;
+    if (smem > 100 * 1024) { set_error(G4_ERR_ARG, "resnorm: dim %d too large", r.dim); return G4_ERR_ARG; }
+    resnorm_kernel<<<B, 512, smem, st>>>(r);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+// Element e of row `row` of a weight tensor with `ncols` columns, dequantized
+// with the reference's float expressions (dequant_q4_k/q5_k/q6_k,
+// main.c:172-237; f16/bf16 decode 128-156).  Q6_K uses the device planes.
+__device__ __forceinline__ float weight_elem(const void *w, int type, int ncols, size_t nrows_total, long row, int e) {
+    if (type == G4_F32) return ((const float *)w)[(size_t)row * ncols + e];
+    if (type == G4_F16) return f16_to_f32(((const uint16_t *)w)[(size_t)row * ncols + e]);
+    if (type == G4_BF16) return bf16_to_f32(((const uint16_t *)w)[(size_t)row * ncols + e]);
+    const int nb = ncols / G4_QK, k = e / G4_QK, i = e % G4_QK;
+    if (type == G4_Q6_K) {
+        const Q6Planes P = q6_planes(w, nrows_total * nb);
+        const size_t bi = (size_t)row * nb + k;
+        const uint8_t *ql = (const uint8_t *)(P.ql + bi * 8);
+        const uint8_t *qh = (const uint8_t *)(P.qh + bi * 4);
+        const int8_t *sc = (const int8_t *)(P.sc + bi);
+        const int n6 = i / 128, r = i % 128, qd = r / 32, l = r % 32;
+        const int qlb = ql[64 * n6 + (qd & 1) * 32 + l];
+        const int lo = (qd >= 2) ? (qlb >> 4) : (qlb & 15);
+        const int q = (lo | (((qh[32 * n6 + l] >> (2 * qd)) & 3) << 4)) - 32;
+        const float d = f16_to_f32(P.d[bi]);
+        return __fmul_rn(__fmul_rn(d, (float)sc[8 * n6 + l / 16 + 2 * qd]), (float)q);
+    }
+    const size_t bb = type == G4_Q4_K ? 144 : 176;
+    const uint8_t *blk = (const uint8_t *)w + ((size_t)row * nb + k) * bb;
+    const uint16_t *dd = (const uint16_t *)blk;
+    const uint32_t *s32 = (const uint32_t *)(blk + 4);
+    const int c = i / 64, hi = (i / 32) & 1, l = i % 32;
+    int sc, mn;
+    k4_scale_min(2 * c + hi, s32[0], s32[1], s32[2], sc, mn);
+    const uint8_t *qs = blk + (type == G4_Q4_K ? 16 : 48);
+    int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 15);
+    if (type == G4_Q5_K && ((blk[16 + l] >> (2 * c + hi)) & 1)) q += 16;
+    const float d1 = __fmul_rn(f16_to_f32(dd[0]), (float)sc);
+    const float m1 = __fmul_rn(f16_to_f32(dd[1]), (float)mn);
+    return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+}
+
+__global__ void embed_kernel(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
+                             int ple_tok_t, int ple_row, float ple_scale, const int *tokens,
+                             const unsigned long long *keys, float *x, float *ple_out) {
+    const int b = blockIdx.x;
+    int tok = tokens ? tokens[b] : argmax_key_index(keys[b]);
+    if (tok < 0 || (size_t)tok >= vocab) tok = 0;  // no LM-head result yet: never index out of the table
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        x[(size_t)b * dim + i] = __fmul_rn(weight_elem(embd, embd_t, dim, vocab, tok, i), emb_scale);
+    if (ple_out)
+        for (int i = threadIdx.x; i < ple_row; i += blockDim.x)
+            ple_out[(size_t)b * ple_row + i] = __fmul_rn(weight_elem(ple_tok, ple_tok_t, ple_row, vocab, tok, i), ple_scale);
+}
+
+int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
+                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, const unsigned long long *keys,
+                   float *x, float *ple_out, int B, cudaStream_t st) {
+    embed_kernel<<<B, 512, 0, st>>>(embd, embd_t, dim, vocab, emb_scale, ple_tok, ple_tok_t, ple_row, ple_scale, tokens,
+                                    keys, x, ple_out);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+// build_ple mixing (main.c:1760-1777), one CTA per (layer, sequence).
+__global__ void ple_mix_kernel(const float *ple_tok, const float *ple_ctx, const float *norm_w, int pd, int L,
+                               float ctx_scale, float mix_scale, float eps, float *ple_out) {
+    __shared__ float red[32];
+    __shared__ float cs[1024];
+    const int l = blockIdx.x, b = blockIdx.y;
+    const size_t off = (size_t)b * L * pd + (size_t)l * pd;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < pd; i += blockDim.x) {
+        const float c = __fmul_rn(ple_ctx[off + i], ctx_scale);
+        cs[i] = c;
+        ss = fmaf(c, c, ss);
+    }
+    ss = cta_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)pd + eps);
+    for (int i = threadIdx.x; i < pd; i += blockDim.x) {
+        const float c = __fmul_rn(__fmul_rn(cs[i], inv), norm_w[i]);
+        ple_out[off + i] = __fmul_rn(__fadd_rn(ple_tok[off + i], c), mix_scale);
+    }
+}
+
+int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, int pd, int L, float ctx_scale,
+                   float mix_scale, float eps, float *ple_out, int B, cudaStream_t st) {
+    if (pd > 1024) { set_error(G4_ERR_ARG, "ple_dim %d > 1024", pd); return G4_ERR_ARG; }
+    ple_mix_kernel<<<dim3(L, B), 256, 0, st>>>(ple_tok, ple_ctx, norm_w, pd, L, ctx_scale, mix_scale, eps, ple_out);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+__global__ void keys_to_tokens_kernel(const unsigned long long *keys, int *tokens, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) tokens[b] = argmax_key_index(keys[b]);
+}
+
+int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st) {
+    keys_to_tokens_kernel<<<(B + 127) / 128, 128, 0, st>>>(keys, tokens, B);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+}  // namespace g4
+
+namespace g4 {
+
+__device__ __forceinline__ float gelu_ref(float x) {  // gelu_f32, main.c:1490-1492
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
+}
+
+__global__ void gelu_mul_kernel(float *a, const float *b, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) a[i] = gelu_ref(a[i]) * b[i];
+}
+
+int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st) {
+    gelu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, b, n);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+// Softcap in place (main.c:1790-1795) and first-max argmax per sequence
+// (sample_token temp <= 0, main.c:2045-2050) for LM heads of dense types.
+__global__ void softcap_argmax_kernel(float *logits, int vocab, int ld, float cap, unsigned long long *keys) {
+    const int b = blockIdx.y;
+    float *lg = logits + (size_t)b * ld;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
+        float v = lg[i];
+        if (cap > 0.0f) { v = cap * tanhf(v * (1.0f / cap)); lg[i] = v; }
+        const unsigned long long k = argmax_key(v, i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+        best = ok > best ? ok : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best) atomicMax(keys + b, best);
+}
+
+int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned long long *keys, int B,
+                          cudaStream_t st) {
+    softcap_argmax_kernel<<<dim3(148, B), 256, 0, st>>>(logits, vocab, ld, cap, keys);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+// GGUF Q6_K blocks (210 B) -> device planes (ql | qh | scales | d).
+__global__ void repack_q6_kernel(const uint8_t *raw, size_t nblk, size_t off, uint8_t *planes, size_t total) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblk) return;
+    const uint8_t *b = raw + i * 210;
+    const size_t gi = off + i;
+    uint8_t *ql = planes + gi * 128, *qh = planes + total * 128 + gi * 64, *sc = planes + total * 192 + gi * 16;
+    uint16_t *d = reinterpret_cast<uint16_t *>(planes + total * 208) + gi;
+    for (int j = 0; j < 128; j++) ql[j] = b[j];
+    for (int j = 0; j < 64; j++) qh[j] = b[128 + j];
+    for (int j = 0; j < 16; j++) sc[j] = b[192 + j];
+    *d = (uint16_t)(b[208] | (b[209] << 8));
+}
+
+int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, size_t nblk_total,
+                     cudaStream_t st) {
+    if (!nblk) return G4_OK;
+    repack_q6_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>((const uint8_t *)raw_dev, nblk, blk_offset,
+                                                                     (uint8_t *)planes_dev, nblk_total);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+}  // namespace g4
+
+namespace g4 {
+
+// apply_rope_neox (main.c:1725-1745) with a precomputed (cos, sin) row.
+__global__ void rope_kernel(float *vec, int hd, int n_rot, const float2 *cs) {
+    float *seg = vec + (size_t)blockIdx.x * hd;
+    const int half = hd / 2;
+    for (int j = threadIdx.x; j < n_rot / 2; j += blockDim.x) {
+        const float v0 = seg[j], v1 = seg[j + half];
+        const float2 c = cs[j];
+        seg[j] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+        seg[j + half] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
+    }
+}
+
+int launch_rope(float *vec, int n_heads, int hd, int n_rot, const float2 *cs, cudaStream_t st) {
+    if (n_rot < 2) return G4_OK;
+    rope_kernel<<<n_heads, 128, 0, st>>>(vec, hd, n_rot, cs);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+// mm_quant_rows for Q4_K/Q5_K (main.c:1539-1556, the --f32-matmul debug
+// path): dequantize each weight with the reference expression, fp32 dot.
+__global__ void gemv_deq_kernel(const void *w, int type, int n, int rows, const float *x, float *out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    float acc = 0.0f;
+    for (int e = lane; e < n; e += 32) acc = fmaf(x[e], weight_elem(w, type, n, rows, warp, e), acc);
+    acc = warp_sum(acc);
+    if (lane == 0) out[warp] = acc;
+}
+
+int launch_gemv_deq(const void *w, int type, int n, int rows, const float *x, float *out, cudaStream_t st) {
+    gemv_deq_kernel<<<(rows + 7) / 8, 256, 0, st>>>(w, type, n, rows, x, out);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+}  // namespace g4
+
+namespace g4 {
+int prime_gemv_attrs();
+int prime_attn_attrs();
+int prime_kernel_attrs() {
+    G4_CUDA(cudaFuncSetAttribute(resnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    int rc = prime_gemv_attrs();
+    if (rc) return rc;
+    return prime_attn_attrs();
+}
+}  // namespace g4

@@ -1,0 +1,146 @@
+"""GPU parity of the device-resident decode engine (g4_forward / g4_generate_greedy
+/ g4_decode_batch) against the reference and the oracle on synthetic models.
+
+* TINY_F (fp32-path projections, no Q8_K activation rounding): logits, hidden
+  state and KV rows at pos >= 1 within 5e-5 of the reference, and the greedy
+  stream token-identical to the reference's.
+* TINY (the Q4_K_M mix): logits within the reference's own AVX2-vs-generic
+  spread (Q8_K re-rounding of activations turns last-ulp differences into
+  ~1e-2 logit differences, in the reference too).
+* batched decode: each sequence of a batch is bit-identical to decoding it alone.
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from _tol import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tinyf(g4):
+    return g4.synth.make_model(g4.synth.TINY_F, seed=3)
+
+
+@pytest.fixture(scope="module")
+def tiny(g4):
+    return g4.synth.make_model(g4.synth.TINY, seed=3)
+
+
+def run_prefix(eng, prompt, upto):
+    for pos in range(upto + 1):
+        r = eng.forward(int(prompt[pos]), pos, 0 if pos < upto else 1, want_logits=(pos == upto))
+    return r
+
+
+def test_tinyf_forward_matches_reference(g4, gpu, tinyf, golden):
+    eng = g4.Engine(tinyf, 0, max_seq=64)
+    am, lg = run_prefix(eng, golden["tiny_prompt"], 7)
+    assert_close(lg, golden["tinyf_logits_p7"], rel=5e-5, what="logits pos 7")
+    assert am == int(np.argmax(golden["tinyf_logits_p7"]))
+    assert_close(eng.hidden(), golden["tinyf_hidden_p7"], rel=5e-5, what="final-normed hidden")
+    k, v = eng.kv(0, 1, 128)
+    assert_close(k, golden["tinyf_k_l0_p1"], rel=1e-5, what="K L0 P1")
+    assert_close(v, golden["tinyf_v_l0_p1"], rel=1e-5, what="V L0 P1")
+    k, v = eng.kv(5, 5, 256)
+    assert_close(k, golden["tinyf_k_l5_p5"], rel=1e-5, what="K L5 P5 (global layer)")
+    assert_close(v, golden["tinyf_v_l5_p5"], rel=1e-5, what="V L5 P5 (global layer)")
+    eng.close()
+
+
+def test_tinyf_greedy_identical(g4, gpu, tinyf, golden):
+    eng = g4.Engine(tinyf, 0, max_seq=64)
+    got = eng.generate_greedy(golden["tiny_prompt"], 32)
+    assert (got == golden["tinyf_greedy"]).all(), (got, golden["tinyf_greedy"])
+    # eos handling: the stream stops before the eos token (main.c:2435)
+    eos = int(golden["tinyf_greedy"][5])
+    got2 = eng.generate_greedy(golden["tiny_prompt"], 32, eos=eos)
+    assert (got2 == golden["tinyf_greedy"][:list(golden["tinyf_greedy"]).index(eos)]).all()
+    eng.close()
+
+
+def test_tinyf_against_live_reference_long_window(g4, gpu, ref):
+    """Positions past the 16-token sliding window and the shared-KV layers."""
+    m = g4.synth.make_model(g4.synth.TINY_F, seed=5)
+    eng = g4.Engine(m, 0, max_seq=64)
+    rm = ref.model(m.desc(), 64)
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 4096, 40)
+    for pos, t in enumerate(toks):
+        lm = 1 if pos % 13 == 12 or pos == 39 else 0
+        am = eng.forward(int(t), pos, lm, want_logits=bool(lm))
+        rm.forward(int(t), pos, lm)
+        if lm:
+            assert_close(am[1], rm.logits(), rel=5e-5, what="logits pos %d" % pos)
+    for l, hd in ((0, 64), (5, 128), (22, 64), (23, 128)):
+        n = 2 * hd
+        for pos in (33, 39):
+            k, v = eng.kv(l, pos, n)
+            rk, rv = rm.kv(l, pos, n)
+            assert_close(k, rk, rel=2e-5, what="K L%d P%d" % (l, pos))
+            assert_close(v, rv, rel=2e-5, what="V L%d P%d" % (l, pos))
+    eng.close()
+    rm.close()
+
+
+def test_tiny_q4km_logits(g4, gpu, tiny, golden):
+    eng = g4.Engine(tiny, 0, max_seq=64)
+    _, lg = run_prefix(eng, golden["tiny_prompt"], 7)
+    assert_close(lg, golden["tiny_logits_p7"], rel=0.1, what="Q4_K_M-mix logits pos 7")
+    eng.close()
+
+
+def test_tiny_q5_mixed_types(g4, gpu, orc):
+    m = g4.synth.make_model(g4.synth.TINY_Q5, seed=8)
+    eng = g4.Engine(m, 0, max_seq=32)
+    om = orc.model(m.desc(), 32)
+    toks = np.random.default_rng(8).integers(0, 4096, 6)
+    for pos, t in enumerate(toks):
+        _, lg = eng.forward(int(t), pos, 1, want_logits=True)
+        om.forward(int(t), pos, 1)
+        assert_close(lg, om.logits(), rel=0.1, what="TINY_Q5 pos %d" % pos)
+    eng.close()
+
+
+def test_head_dim_512_global_layers(g4, gpu, ref):
+    """True-E4B shape of the global layers (head_dim 512, p-RoPE), fp32 paths."""
+    shape = dataclasses.replace(g4.synth.TINY_F, head_dim_full=512, n_rot_full=512)
+    m = g4.synth.make_model(shape, seed=6)
+    eng = g4.Engine(m, 0, max_seq=32)
+    rm = ref.model(m.desc(), 32)
+    toks = np.random.default_rng(6).integers(0, 4096, 10)
+    for pos, t in enumerate(toks):
+        lm = 1 if pos in (4, 9) else 0
+        r = eng.forward(int(t), pos, lm, want_logits=bool(lm))
+        rm.forward(int(t), pos, lm)
+        if lm:
+            assert_close(r[1], rm.logits(), rel=5e-5, what="hd512 logits pos %d" % pos)
+    k, v = eng.kv(5, 9, 1024)
+    rk, rv = rm.kv(5, 9, 1024)
+    assert_close(k, rk, rel=2e-5, what="hd512 K")
+    eng.close()
+    rm.close()
+
+
+def test_batched_decode_equals_single(g4, gpu, tiny):
+    B, steps = 4, 12
+    rng = np.random.default_rng(21)
+    prompts = rng.integers(0, 4096, (B, 4)).astype(np.int32)
+    eb = g4.Engine(tiny, 0, max_seq=32, max_batch=B)
+    toks = prompts[:, 0].copy()
+    outs_b = []
+    for pos in range(steps):
+        lm = 0 if pos < 3 else 1
+        nxt = eb.decode_batch(toks, pos, lm)
+        toks = prompts[:, pos + 1].copy() if pos < 3 else nxt
+        if lm:
+            outs_b.append(nxt.copy())
+    eb.close()
+    outs_b = np.stack(outs_b, 1)
+    for b in range(B):
+        es = g4.Engine(tiny, 0, max_seq=32, max_batch=1)
+        got = es.generate_greedy(prompts[b], steps - 3)
+        es.close()
+        assert (got == outs_b[b]).all(), (b, got, outs_b[b])
