@@ -1,0 +1,399 @@
+"""Benchmark of the decode hot path (BASELINE metric: decode tok/s; Q4_K GEMV
+HBM GB/s vs peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl g4|reference]
+                    [--workload batch64|batch1]
+
+Workloads (seeded synthetic data with the reference configurations' shapes;
+random-init Gemma-4-E4B-shaped Q4_K_M model, no network, no real GGUF):
+  batch64  BASELINE config 4: 64 independent sequences, each prefilled with a
+           seeded random prompt (4096 tokens), then greedy decode.  The 64
+           sequences are sharded over the N ranks (one process per GPU, no
+           collective on the data path) -> "scaling": "strong".
+  batch1   BASELINE config 3: one sequence, 512-token prompt, greedy decode.
+A step is one decode position for all local sequences.  `value` is whole-job
+tokens/s with token ids and weights already in HBM (greedy feedback on the
+device, CUDA-graph replay); `e2e` is the same metric through the public C-ABI
+call g4_decode_batch with host token buffers (H2D + D2H every step).
+
+Extras on rank 0: the kernel roofline of the dominant kernel (the K-quant GEMV,
+timed with CUDA events on the engine's own stream over the config-1 layer
+matrices at the workload's batch), the config-0 Q4_K GEMV GB/s, and the
+reference CPU path (gemma4-4b/cpu-blas/main.c compiled unchanged, OpenMP on
+all host cores) timed on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gemma4.c_b200")
+
+
+def load_pkg():
+    if "g4b200" in sys.modules:
+        return sys.modules["g4b200"]
+    spec = importlib.util.spec_from_file_location("g4b200", os.path.join(PKG, "__init__.py"),
+                                                  submodule_search_locations=[PKG])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["g4b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during a region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.Q,
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.rows.append([c.strip() for c in out.stdout.strip().split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+class Dist:
+    def __init__(self, n_gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        if n_gpus != self.world and self.world > 1:
+            raise SystemExit("--gpus %d but WORLD_SIZE=%d" % (n_gpus, self.world))
+
+    def barrier(self):
+        if self.pg:
+            import torch
+            self.pg.barrier(device_ids=[self.local])
+            torch.cuda.synchronize()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- reference CPU path
+def reference_sample(g4, model, ctx: int, n_steps: int, threads: int):
+    """Time the reference forward() (main.c compiled unchanged) for n_steps
+    greedy decode positions of one sequence at context `ctx` (KV rows [0, ctx)
+    filled with seeded values first).  Returns (tok/s, seconds, threads, blas)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    if not oracle.have_reference():
+        return None
+    ref = oracle.Reference(threads=threads)
+    rm = ref.model(model.desc(), ctx + n_steps + 2)
+    rm.fill_kv(ctx, seed=7)
+    tok = 1
+    rm.forward(tok, ctx, 1)  # warm-up: page in the weights
+    tok = int(np.argmax(rm.logits()))
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        rm.forward(tok, ctx + 1 + i, 1)
+        tok = ref.sample_greedy(rm.logits())
+    dt = time.perf_counter() - t0
+    rm.close()
+    return n_steps / dt, dt, ref.max_threads, ref.blas
+
+
+# ---------------------------------------------------------------- GEMV roofline
+def gemv_roofline(g4, B: int, stream: int, reps: int = 20):
+    """Time g4d_mm launches of the config-1 layer matrices at batch B with CUDA
+    events on `stream`.  Weights rotate over enough copies to exceed L2."""
+    import torch
+    S = g4.synth
+    rng = np.random.default_rng(1)
+    mats = [("q", S.Q4_K, 2048, 2560), ("k", S.Q4_K, 512, 2560), ("v", S.Q6_K, 512, 2560),
+            ("o", S.Q4_K, 2560, 2048), ("gate", S.Q4_K, 10240, 2560), ("up", S.Q4_K, 10240, 2560),
+            ("down", S.Q6_K, 2560, 10240)]
+    layer_bytes = sum(S.row_bytes(t, n) * r for _, t, r, n in mats)
+    copies = max(2, int(np.ceil(300e6 / layer_bytes)))
+    dev = []
+    for c in range(copies):
+        dev.append([(nm, t, r, n, g4.weight_upload(S._qmat(rng, t, r, n, 0.02), t, n, r)) for nm, t, r, n in mats])
+    nmax = 10240
+    x = torch.randn(B, nmax, device="cuda", dtype=torch.float32)
+    o = torch.empty(B, 10240, device="cuda", dtype=torch.float32)
+    q8 = torch.empty(B * (nmax // 256) * 292, device="cuda", dtype=torch.uint8)
+    s = torch.cuda.ExternalStream(stream)
+    res = {}
+
+    def one_pass(kind_filter=None):
+        for ci in range(copies):
+            for nm, t, r, n, w in dev[ci]:
+                if kind_filter and nm not in kind_filter:
+                    continue
+                # q8_ready=1: the activation quantization is a separate kernel in the step
+                g4.mm_device(o.data_ptr(), x.data_ptr(), w, n, r, t, q8.data_ptr(), 1 if t != S.Q6_K else 0, B, stream)
+
+    with torch.cuda.stream(s):
+        for nm, t, r, n, w in dev[0]:
+            if t != S.Q6_K:
+                g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), n, B, stream)
+                break
+        for _ in range(2):
+            one_pass()
+        torch.cuda.synchronize()
+        for label, filt in (("layer", None), ("q4k_gate_up", ("gate", "up")), ("q6k_down", ("down",))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                one_pass(filt)
+            e1.record(s)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            launches = reps * copies * sum(1 for m in mats if (filt is None or m[0] in filt))
+            byts = reps * copies * sum(S.row_bytes(t, n) * r + B * (n * 4 + r * 4) for nm, t, r, n in mats
+                                       if filt is None or nm in filt)
+            res[label] = {"ms_per_launch": ms / launches, "bytes_per_launch": byts / launches,
+                          "gbs": byts / (ms * 1e-3) / 1e9}
+    for c in dev:
+        for *_, w in c:
+            g4.free(w)
+    return res
+
+
+def config0_gemv(g4, stream: int, reps: int = 50):
+    """Q4_K 10240 x 2560 GEMV at batch 1, weights rotated
+    over 20 copies (295 MB > L2)."""
+    import torch
+    S = g4.synth
+    copies = 20
+    ws = []
+    for c in range(copies):
+        w, xh = S.config0_weights(seed=c)
+        ws.append(g4.weight_upload(w, S.Q4_K, 2560, 10240))
+    x = torch.from_numpy(xh).cuda()
+    o = torch.empty(10240, device="cuda", dtype=torch.float32)
+    q8 = torch.empty(10 * 292, device="cuda", dtype=torch.uint8)
+    s = torch.cuda.ExternalStream(stream)
+    with torch.cuda.stream(s):
+        g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), 2560, 1, stream)
+        for w in ws:
+            g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, 10240, S.Q4_K, q8.data_ptr(), 1, 1, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            for w in ws:
+                g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, 10240, S.Q4_K, q8.data_ptr(), 1, 1, stream)
+        e1.record(s)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * copies)
+    byts = 14745600 + 2920 + 40960
+    for w in ws:
+        g4.free(w)
+    return {"us_per_gemv": ms * 1e3, "gbs": byts / (ms * 1e-3) / 1e9, "bytes": byts}
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
+    ap.add_argument("--workload", default="batch64", choices=["batch64", "batch1"])
+    ap.add_argument("--seqs", type=int, default=None, help="total sequences (default 64 / 1)")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    a = ap.parse_args()
+    if a.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    seqs = a.seqs or (64 if a.workload == "batch64" else 1)
+    prompt = a.prompt or (4096 if a.workload == "batch64" else 512)
+    g4 = load_pkg()
+    S = g4.synth
+    metric = "decode tok/s"
+    cfg = {"workload": "config4 batched greedy decode" if a.workload == "batch64" else "config3 batch-1 greedy decode",
+           "model": "Gemma-4-E4B-shaped Q4_K_M (random init, 42 layers, d 2560, ffn 10240, 8:2 GQA, hd 256, "
+                    "vocab 262144, tied Q6_K head)",
+           "sequences": seqs, "prompt_tokens": prompt, "global_batch": seqs, "seq_len": prompt,
+           "parallelism": "sequence shards (dp%d), no collective" % a.gpus,
+           "l2": "no flush needed: each step streams 3.2 GB of weights (> 126 MB L2)"}
+
+    if a.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        model = S.make_model(S.E4B, seed=3)
+        r = reference_sample(g4, model, prompt, max(1, a.steps // 4), threads)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libg4ref.so was not built"}))
+            return
+        tps, dt, thr, blas = r
+        print(json.dumps({"impl": "reference", "metric": metric, "value": tps, "unit": "tok/s", "n_gpus": a.gpus,
+                          "steps": max(1, a.steps // 4), "warmup": 1, "ms_per_step": 1e3 * dt / max(1, a.steps // 4),
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32",
+                          "data": "synthetic", "config": cfg,
+                          "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": thr, "kind": "reference",
+                                           "sample": "%d greedy decode steps of one sequence at context %d "
+                                                     "(reference processes sequences one by one; BLAS: %s)"
+                                                     % (max(1, a.steps // 4), prompt, blas)},
+                          "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    dist = Dist(a.gpus)
+    import torch
+    torch.cuda.set_device(dist.local)
+    if seqs % dist.world:
+        raise SystemExit("sequences must divide evenly over ranks")
+    B = seqs // dist.world
+    model = S.make_model(S.E4B, seed=3)
+    wbytes = model.weight_bytes()
+    max_seq = prompt + a.warmup + a.steps * 2 + 8
+    eng = g4.Engine(model, dist.local, max_seq=max_seq, max_batch=B)
+    model_keep = model  # host tensors stay alive until the end
+    stream = eng.stream()
+    # prompts: seeded per global sequence id
+    rng = np.random.default_rng(1234)
+    allp = rng.integers(0, S.E4B.vocab_size, size=(seqs, prompt), dtype=np.int32)
+    mine = allp[dist.rank * B:(dist.rank + 1) * B]
+    prompts_dev = torch.from_numpy(np.ascontiguousarray(mine.T)).cuda()  # [prompt][B]
+    t0 = time.perf_counter()
+    for pos in range(prompt):
+        lm = 1 if pos == prompt - 1 else 0
+        eng.decode_batch_device(B, prompts_dev.data_ptr() + pos * B * 4, pos, lm, None)
+    eng.sync()
+    prefill_s = time.perf_counter() - t0
+    pos = prompt
+    for _ in range(a.warmup):
+        eng.decode_batch_device(B, None, pos, 1, None)
+        pos += 1
+    eng.sync()
+    dist.barrier()
+    s = torch.cuda.ExternalStream(stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dist.local) as clk:
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(a.steps):
+            eng.decode_batch_device(B, None, pos, 1, None)
+            pos += 1
+        e1.record(s)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    kernels_per_step = eng.last_step_kernels()
+    dist.barrier()
+    ms_max = dist.max(ms)
+    value = seqs * a.steps / (ms_max / 1e3)
+
+    # e2e: the public C-ABI call with host token buffers, H2D + D2H inside each step
+    toks = np.zeros(B, np.int32)
+    nxt = eng.decode_batch(toks + 1, pos, 1)
+    pos += 1
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        nxt = eng.decode_batch(nxt, pos, 1)
+        pos += 1
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e = {"value": seqs * a.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+           "d2h_bytes_per_step": 4 * B, "api": "g4_decode_batch (host token ids in, host next ids out)"}
+
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    out = {"metric": metric, "value": value, "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "int8xint4/int32 dots + fp32 (Q6_K, norms, attention)",
+           "data": "synthetic (seeded random-init model and prompts)", "config": cfg,
+           "e2e": e2e, "gpu_launches": int(kernels_per_step * a.steps),
+           "kernels_per_step": kernels_per_step, "prefill_s": prefill_s,
+           "weights_gb": wbytes / 1e9, "clocks": clk.summary()}
+    if dist.rank == 0 and not a.no_extras:
+        rl = gemv_roofline(g4, B, stream)
+        lay = rl["layer"]
+        out["roofline"] = {"kernel": "gemv_kquant_kernel (config-1 layer matrices, batch %d)" % B, "bound": "hbm",
+                           "achieved": lay["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": lay["gbs"] / hbm_peak,
+                           "peak_kind": peak_kind, "traffic": None,
+                           "algorithmic_bytes_per_launch": lay["bytes_per_launch"],
+                           "us_per_launch": lay["ms_per_launch"] * 1e3, "parts": rl}
+        out["q4k_gemv_config0"] = config0_gemv(g4, stream)
+        out["q4k_gemv_config0"]["frac"] = out["q4k_gemv_config0"]["gbs"] / hbm_peak
+        out["step_hbm_gbs"] = wbytes / (ms_max / a.steps * 1e-3) / 1e9
+        if dist.world == 1:
+            r = reference_sample(g4, model, prompt, a.cpu_steps, os.cpu_count() or 1)
+            if r:
+                tps, dt, thr, blas = r
+                out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": thr, "kind": "reference",
+                                       "sample": "%d greedy decode steps of one sequence at context %d, %.1f s "
+                                                 "(BLAS: %s)" % (a.cpu_steps, prompt, dt, blas)}
+    eng.close()
+    del model_keep
+    if dist.rank == 0:
+        print(json.dumps(out))
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

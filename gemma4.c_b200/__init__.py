@@ -64,6 +64,10 @@ SIGNATURES = [
     ("g4_apply_rope_neox_ex", ip, [vp, ip, ip, ip, ip, fp, fp, vp]),
     ("g4_logits_tied", ip, [vp, vp, vp, vp, ip, ip, ip, fp]),
     ("g4_attn_decode", ip, [vp, vp, vp, vp, ip, ip, ip, ip, ip]),
+    ("g4d_weight_upload", ip, [vp, ip, ip, ip, vp]),
+    ("g4d_free", ip, [vp]),
+    ("g4d_quantize_row_q8_K", ip, [vp, vp, ip, ip, vp]),
+    ("g4d_mm", ip, [vp, vp, vp, ip, ip, ip, vp, ip, ip, vp]),
     ("g4_model_desc_bytes", C.c_size_t, []),
     ("g4_engine_create", vp, [vp, ip, ip, ip]),
     ("g4_engine_destroy", ip, [vp]),
@@ -76,6 +80,7 @@ SIGNATURES = [
     ("g4_engine_stream", vp, [vp]),
     ("g4_engine_get_hidden", ip, [vp, ip, vp]),
     ("g4_engine_get_kv", ip, [vp, ip, ip, ip, vp, vp]),
+    ("g4_engine_last_step_kernels", ip, [vp]),
 ]
 
 _lib = None
@@ -188,6 +193,22 @@ def attn_decode(q, k, v, nwin, kv_stride, n_heads, n_kv, hd):
     return out
 
 
+def weight_upload(host: np.ndarray, t: int, n: int, rows: int) -> int:
+    """Device copy of a weight tensor (device layout); returns the pointer."""
+    d = C.c_void_p()
+    _check(lib().g4d_weight_upload(_p(host), t, n, rows, C.byref(d)))
+    return d.value
+
+
+def free(dev: int):
+    _check(lib().g4d_free(dev))
+
+
+def mm_device(o, x, w, n, d, t, q8, q8_ready, batch, stream):
+    """g4d_mm on raw device pointers (ints)."""
+    _check(lib().g4d_mm(o, x, w, n, d, t, q8, q8_ready, batch, stream))
+
+
 def registry_clear():
     _check(lib().g4_registry_clear())
 
@@ -251,6 +272,9 @@ class Engine:
         v = np.zeros(n, np.float32)
         _check(lib().g4_engine_get_kv(self.h, b, layer, pos, _p(k), _p(v)))
         return k, v
+
+    def last_step_kernels(self) -> int:
+        return int(lib().g4_engine_last_step_kernels(self.h))
 
     def device_bytes(self) -> int:
         return int(lib().g4_engine_device_bytes(self.h))

@@ -508,3 +508,54 @@ int g4_attn_decode(float *out, const float *q, const float *k, const float *v, i
 }
 
 }  // extern "C"
+
+extern "C" {
+
+int g4d_weight_upload(const void *host, int type, int n, int rows, void **dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!host || !dev || n <= 0 || rows <= 0) { set_error(G4_ERR_ARG, "weight_upload: bad arguments"); return G4_ERR_ARG; }
+    float dummy;
+    G4_TRY(check_mm_args(&dummy, host, n, rows, type));
+    G4_TRY(ctx_ready());
+    void *d = nullptr;
+    G4_CUDA(cudaMalloc(&d, device_tensor_bytes(type, n, rows)));
+    const int rc = upload_tensor(d, host, type, n, rows, g_ctx.st);
+    if (rc) { cudaFree(d); return rc; }
+    *dev = d;
+    return G4_OK;
+}
+
+int g4d_free(void *dev) {
+    G4_CUDA(cudaFree(dev));
+    return G4_OK;
+}
+
+int g4d_quantize_row_q8_K(const float *x, g4_block_q8_K *y, int k, int batch, void *stream) {
+    if (!x || !y || k < 0 || k % G4_QK || batch < 0) { set_error(G4_ERR_ARG, "quantize: k=%d must be a multiple of 256", k); return G4_ERR_ARG; }
+    return launch_quantize_q8k(x, k, y, k, batch, (cudaStream_t)stream);
+}
+
+int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_block_q8_K *q8, int q8_ready,
+           int batch, void *stream) {
+    G4_TRY(check_mm_args(o, w, n, d, type));
+    if (batch <= 0) { set_error(G4_ERR_ARG, "mm: batch %d", batch); return G4_ERR_ARG; }
+    cudaStream_t st = (cudaStream_t)stream;
+    if (is_q8_type(type)) {
+        if (!q8 || (!q8_ready && !x)) { set_error(G4_ERR_ARG, "mm: Q8_K buffer / x required"); return G4_ERR_ARG; }
+        if (!q8_ready) G4_TRY(launch_quantize_q8k(x, n, q8, n, batch, st));
+    } else if (!x) {
+        set_error(G4_ERR_ARG, "mm: x is NULL");
+        return G4_ERR_ARG;
+    }
+    if (type == G4_F32 || type == G4_F16 || type == G4_BF16)
+        return launch_gemv_dense(w, type, n, d, x, n, o, d, batch, EPI_STORE, nullptr, 0, st);
+    GemvJobs jobs{};
+    jobs.njobs = 1;
+    GemvJob &J = jobs.j[0];
+    J.w = w; J.type = type; J.n = n; J.rows = d;
+    J.act = type == G4_Q6_K ? (const void *)x : (const void *)q8;
+    J.act_stride = n; J.out = o; J.out_stride = d; J.epi = EPI_STORE;
+    return launch_gemv_kquant(jobs, batch, st);
+}
+
+}  // extern "C"

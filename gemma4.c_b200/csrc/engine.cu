@@ -72,7 +72,8 @@ struct g4_engine {
     std::vector<void *> allocs;
     size_t dev_bytes = 0;
     std::map<long, cudaGraphExec_t> graphs;
-    int last_lm_mode = 0;
+    std::map<long, int> graph_kernels;  // kernel nodes per captured step
+    int last_lm_mode = 0, last_step_kernels = 0;
     std::mutex mu;
 };
 
@@ -277,6 +278,17 @@ int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits)
         cudaError_t ce = cudaStreamEndCapture(e->st, &g);
         if (rc) { if (g) cudaGraphDestroy(g); return rc; }
         if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture", __FILE__, __LINE__);
+        size_t nn = 0;
+        int nk = 0;
+        if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+                for (auto nd : nodes) {
+                    cudaGraphNodeType ty;
+                    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) nk++;
+                }
+        }
+        e->graph_kernels[key] = nk;
         cudaGraphExec_t ge = nullptr;
         ce = cudaGraphInstantiate(&ge, g, 0);
         cudaGraphDestroy(g);
@@ -285,6 +297,7 @@ int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits)
     }
     G4_CUDA(cudaGraphLaunch(it->second, e->st));
     e->last_lm_mode = lm_mode;
+    e->last_step_kernels = e->graph_kernels[key];
     return G4_OK;
 }
 
@@ -474,6 +487,8 @@ int g4_engine_destroy(g4_engine *e) {
 size_t g4_engine_device_bytes(const g4_engine *e) { return e ? e->dev_bytes : 0; }
 
 size_t g4_model_desc_bytes(void) { return sizeof(g4_model_desc); }
+
+int g4_engine_last_step_kernels(const g4_engine *e) { return e ? e->last_step_kernels : -1; }
 
 void *g4_engine_stream(g4_engine *e) { return e ? (void *)e->st : nullptr; }
 

@@ -144,6 +144,19 @@ int g4_logits_tied(float *logits, int *argmax, const float *x, const void *embd,
 int g4_attn_decode(float *out, const float *q, const float *k, const float *v, int nwin,
                    int kv_stride, int n_heads, int n_kv_heads, int hd);
 
+/* Device-pointer forms for callers that keep activations in HBM.  `stream`
+ * is a cudaStream_t (NULL = the legacy default stream); nothing is
+ * synchronised.  Weight pointers must come from g4d_weight_upload (device
+ * layout: GGUF blocks, Q6_K split into planes).  `batch` activation vectors
+ * are laid out back to back ([batch][n] in, [batch][d] out). */
+int g4d_weight_upload(const void *host, int type, int n, int rows, void **dev);
+int g4d_free(void *dev);
+/* quantize_row_q8_K on device: y[batch][k/256] from x[batch][k]. */
+int g4d_quantize_row_q8_K(const float *x, g4_block_q8_K *y, int k, int batch, void *stream);
+/* mm on device (same semantics as g4_mm; q8 is a device buffer). */
+int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_block_q8_K *q8, int q8_ready,
+           int batch, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* 2. Device-resident engine                                           */
 /* ------------------------------------------------------------------ */
@@ -224,6 +237,9 @@ int g4_decode_batch_device(g4_engine *e, int B, const int *tokens_dev, int pos, 
 int g4_engine_sync(g4_engine *e);
 /* The engine's CUDA stream (cudaStream_t as void*) for event timing. */
 void *g4_engine_stream(g4_engine *e);
+
+/* Number of kernels in the most recent step (the nodes of its CUDA graph). */
+int g4_engine_last_step_kernels(const g4_engine *e);
 
 /* Test taps: hidden state x[dim] of sequence b after the last step, and the
  * K/V rows (n_kv_heads * head_dim floats each) stored for (layer, pos). */

@@ -179,6 +179,7 @@ class Reference(_Lib):
         self._mkc = self.fn("model_kc", fp, vp, C.c_int, C.c_int)
         self._mvc = self.fn("model_vc", fp, vp, C.c_int, C.c_int)
         self._gen = self.fn("generate_greedy", C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, vp)
+        self._fillkv = self.fn("model_fill_kv", None, vp, C.c_int, C.c_uint64)
         try:
             with open(os.path.join(os.path.dirname(path), "BLAS")) as f:
                 self.blas = f.read().strip()
@@ -260,6 +261,9 @@ class _Model:
         k = np.ctypeslib.as_array(self.lib._mkc(self.h, layer, pos), shape=(n,)).copy()
         v = np.ctypeslib.as_array(self.lib._mvc(self.h, layer, pos), shape=(n,)).copy()
         return k, v
+
+    def fill_kv(self, npos, seed=1):
+        self.lib._fillkv(self.h, npos, seed)
 
     def generate_greedy(self, prompt, max_new, eos=-1):
         p = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -176,3 +176,21 @@ int ref_generate_greedy(void *mp, const int *prompt, int n_prompt, int max_new, 
     }
     return gen;
 }
+
+/* Fill the KV cache rows [0, npos) of every KV layer with seeded values in
+ * [-1, 1) (xorshift64*).  Used only to time forward() at a long context
+ * without running the prefill first: the work of a decode step does not
+ * depend on the cached values. */
+void ref_model_fill_kv(void *mp, int npos, uint64_t seed) {
+    Model *m = (Model *)mp;
+    uint64_t s = seed ? seed : 1;
+    if (npos > m->cfg.max_seq) npos = m->cfg.max_seq;
+    for (int l = 0; l < N_LAYER_KV && l < m->cfg.n_layers; l++)
+        for (int p = 0; p < npos; p++) {
+            float *k = kc_at(&m->s, l, p, m->cfg.max_seq), *v = vc_at(&m->s, l, p, m->cfg.max_seq);
+            for (int i = 0; i < MAX_KV_DIM; i++) {
+                k[i] = 2.0f * rng_f32(&s) - 1.0f;
+                v[i] = 2.0f * rng_f32(&s) - 1.0f;
+            }
+        }
+}
