@@ -99,7 +99,8 @@ class ClockSampler:
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].strip().lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(self.rows)}
 

@@ -188,22 +188,25 @@ int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_log
         r.q8_out = q8_in ? e->q8 : nullptr; r.dim = dim; r.eps = e->eps;
         TRY(launch_resnorm(r, B, e->st));
 
-        // Q / K / V projections (main.c:1884-1891)
-        GemvJobs jobs{};
+        // Q / K / V projections (main.c:1884-1891): one launch per tensor type
         struct Proj { const void *w; int t; int rows; float *out; };
         Proj pr[3] = {{ly.wq, ly.wq_t, ly.qd, e->q}, {ly.wk, ly.wk_t, ly.kvd, e->k}, {ly.wv, ly.wv_t, ly.kvd, e->v}};
         const int np = has_kv ? 3 : 1;
-        for (int i = 0; i < np; i++) {
-            if (pr[i].t == G4_F32 || pr[i].t == G4_F16 || pr[i].t == G4_BF16) {
-                TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
-                continue;
+        const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
+        for (int kt : ktypes) {
+            GemvJobs jobs{};
+            for (int i = 0; i < np; i++) {
+                if (pr[i].t != kt) continue;
+                GemvJob &J = jobs.j[jobs.njobs++];
+                J.w = pr[i].w; J.type = pr[i].t; J.n = dim; J.rows = pr[i].rows;
+                J.act = is_q8_type(pr[i].t) ? (const void *)e->q8 : (const void *)e->xn;
+                J.act_stride = dim; J.out = pr[i].out; J.out_stride = pr[i].rows; J.epi = EPI_STORE;
             }
-            GemvJob &J = jobs.j[jobs.njobs++];
-            J.w = pr[i].w; J.type = pr[i].t; J.n = dim; J.rows = pr[i].rows;
-            J.act = is_q8_type(pr[i].t) ? (const void *)e->q8 : (const void *)e->xn;
-            J.act_stride = dim; J.out = pr[i].out; J.out_stride = pr[i].rows; J.epi = EPI_STORE;
+            if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
         }
-        if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
+        for (int i = 0; i < np; i++)
+            if (pr[i].t == G4_F32 || pr[i].t == G4_F16 || pr[i].t == G4_BF16)
+                TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
 
         // attention (main.c:1886-1950)
         AttnLayer A{};

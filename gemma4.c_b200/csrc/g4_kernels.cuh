@@ -21,7 +21,7 @@ struct GemvJob {
     float *out;          // [B][out_stride] (may be null for EPI_SOFTCAP_ARGMAX)
     unsigned long long *amax;  // [B] argmax keys for EPI_SOFTCAP_ARGMAX
     const float *evec;   // [B][ld_evec] multiplier of EPI_GELU_SCALE
-    int type, n, rows, act_stride, out_stride, epi, rt, cta_begin, ld_evec;
+    int type, n, rows, act_stride, out_stride, epi, rt, cta_begin, ld_evec, ctas;
     float cap;
 };
 struct GemvJobs {
@@ -29,7 +29,6 @@ struct GemvJobs {
     int njobs;
 };
 
-int default_rt(int type, int n, int rows);
 int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStream_t st);
 int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st);
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
