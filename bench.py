@@ -168,9 +168,34 @@ def reference_sample(g4, model, ctx: int, n_steps: int, threads: int):
 
 
 # ---------------------------------------------------------------- GEMV roofline
-def gemv_roofline(g4, B: int, stream: int, reps: int = 20):
-    """Time g4d_mm launches of the config-1 layer matrices at batch B with CUDA
-    events on `stream`.  Weights rotate over enough copies to exceed L2."""
+def _graph_time(fn, reps: int, stream_holder):
+    """Capture fn() (which enqueues kernels on the torch current stream) into a
+    CUDA graph and time `reps` replays with CUDA events; returns ms per replay.
+    Timing graph replays keeps host launch overhead out of kernel timings."""
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fn(s.cuda_stream)           # warm-up outside capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            fn(s.cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+        e1.synchronize()
+    del g
+    return e0.elapsed_time(e1) / reps
+
+
+def gemv_roofline(g4, B: int, reps: int = 10):
+    """The K-quant GEMV kernel over the config-1 layer matrices at batch B,
+    weights rotated over enough copies to exceed L2, timed as CUDA-graph
+    replays with CUDA events."""
     import torch
     S = g4.synth
     rng = np.random.default_rng(1)
@@ -186,47 +211,33 @@ def gemv_roofline(g4, B: int, stream: int, reps: int = 20):
     x = torch.randn(B, nmax, device="cuda", dtype=torch.float32)
     o = torch.empty(B, 10240, device="cuda", dtype=torch.float32)
     q8 = torch.empty(B * (nmax // 256) * 292, device="cuda", dtype=torch.uint8)
-    s = torch.cuda.ExternalStream(stream)
+    g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), 2560, B, None)
+    torch.cuda.synchronize()
     res = {}
+    for label, filt in (("layer", None), ("q4k_gate_up", ("gate", "up")), ("q6k_down", ("down",))):
+        sel = [(nm, t, r, n) for nm, t, r, n in mats if filt is None or nm in filt]
 
-    def one_pass(kind_filter=None):
-        for ci in range(copies):
-            for nm, t, r, n, w in dev[ci]:
-                if kind_filter and nm not in kind_filter:
-                    continue
-                # q8_ready=1: the activation quantization is a separate kernel in the step
-                g4.mm_device(o.data_ptr(), x.data_ptr(), w, n, r, t, q8.data_ptr(), 1 if t != S.Q6_K else 0, B, stream)
+        def run(stream, sel=sel, filt=filt):
+            for ci in range(copies):
+                for nm, t, r, n, w in dev[ci]:
+                    if filt is None or nm in filt:
+                        g4.mm_device(o.data_ptr(), x.data_ptr(), w, n, r, t, q8.data_ptr(), 1, B, stream)
 
-    with torch.cuda.stream(s):
-        for nm, t, r, n, w in dev[0]:
-            if t != S.Q6_K:
-                g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), n, B, stream)
-                break
-        for _ in range(2):
-            one_pass()
-        torch.cuda.synchronize()
-        for label, filt in (("layer", None), ("q4k_gate_up", ("gate", "up")), ("q6k_down", ("down",))):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(s)
-            for _ in range(reps):
-                one_pass(filt)
-            e1.record(s)
-            e1.synchronize()
-            ms = e0.elapsed_time(e1)
-            launches = reps * copies * sum(1 for m in mats if (filt is None or m[0] in filt))
-            byts = reps * copies * sum(S.row_bytes(t, n) * r + B * (n * 4 + r * 4) for nm, t, r, n in mats
-                                       if filt is None or nm in filt)
-            res[label] = {"ms_per_launch": ms / launches, "bytes_per_launch": byts / launches,
-                          "gbs": byts / (ms * 1e-3) / 1e9}
+        ms = _graph_time(run, reps, None)
+        launches = copies * len(sel)
+        byts = copies * sum(S.row_bytes(t, n) * r + B * (n * 4 + r * 4) for nm, t, r, n in sel)
+        res[label] = {"us_per_launch": 1e3 * ms / launches, "bytes_per_launch": byts / launches,
+                      "gbs": byts / (ms * 1e-3) / 1e9}
     for c in dev:
         for *_, w in c:
             g4.free(w)
     return res
 
 
-def config0_gemv(g4, stream: int, reps: int = 50):
-    """Q4_K 10240 x 2560 GEMV at batch 1, weights rotated
-    over 20 copies (295 MB > L2)."""
+def config0_gemv(g4, reps: int = 20):
+    """Q4_K 10240 x 2560 GEMV at batch 1 (activation
+    quantized to Q8_K once), weights rotated over 20 copies (295 MB > L2),
+    timed as CUDA-graph replays with CUDA events."""
     import torch
     S = g4.synth
     copies = 20
@@ -237,19 +248,14 @@ def config0_gemv(g4, stream: int, reps: int = 50):
     x = torch.from_numpy(xh).cuda()
     o = torch.empty(10240, device="cuda", dtype=torch.float32)
     q8 = torch.empty(10 * 292, device="cuda", dtype=torch.uint8)
-    s = torch.cuda.ExternalStream(stream)
-    with torch.cuda.stream(s):
-        g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), 2560, 1, stream)
+    g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), 2560, 1, None)
+    torch.cuda.synchronize()
+
+    def run(stream):
         for w in ws:
             g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, 10240, S.Q4_K, q8.data_ptr(), 1, 1, stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for _ in range(reps):
-            for w in ws:
-                g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, 10240, S.Q4_K, q8.data_ptr(), 1, 1, stream)
-        e1.record(s)
-        e1.synchronize()
-    ms = e0.elapsed_time(e1) / (reps * copies)
+
+    ms = _graph_time(run, reps, None) / copies
     byts = 14745600 + 2920 + 40960
     for w in ws:
         g4.free(w)
@@ -263,7 +269,7 @@ def main():
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
-    ap.add_argument("--workload", default="batch64", choices=["batch64", "batch1"])
+    ap.add_argument("--workload", default="batch64", choices=["batch64", "batch1", "gemv0"])
     ap.add_argument("--seqs", type=int, default=None, help="total sequences (default 64 / 1)")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
     ap.add_argument("--no-extras", action="store_true")
@@ -283,6 +289,18 @@ def main():
            "parallelism": "sequence shards (dp%d), no collective" % a.gpus,
            "l2": "no flush needed: each step streams 3.2 GB of weights (> 126 MB L2)"}
 
+    if a.workload == "gemv0":  # BASELINE config 0 alone (used for kernel profiling)
+        import torch
+        torch.cuda.set_device(0)
+        r = config0_gemv(g4, reps=max(a.steps, 1))
+        hbm_peak, _, kind = measured_peaks()
+        print(json.dumps({"metric": "Q4_K GEMV HBM GB/s", "value": r["gbs"], "unit": "GB/s", "n_gpus": 1,
+                          "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["us_per_gemv"] / 1e3,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4",
+                          "data": "synthetic", "config": {"workload": "config0 Q4_K 10240x2560 GEMV"},
+                          "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": hbm_peak, "unit": "GB/s",
+                                       "frac": r["gbs"] / hbm_peak, "peak_kind": kind, "traffic": None}}))
+        return
     if a.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
@@ -372,14 +390,14 @@ def main():
            "kernels_per_step": kernels_per_step, "prefill_s": prefill_s,
            "weights_gb": wbytes / 1e9, "clocks": clk.summary()}
     if dist.rank == 0 and not a.no_extras:
-        rl = gemv_roofline(g4, B, stream)
+        rl = gemv_roofline(g4, B)
         lay = rl["layer"]
         out["roofline"] = {"kernel": "gemv_kquant_kernel (config-1 layer matrices, batch %d)" % B, "bound": "hbm",
                            "achieved": lay["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": lay["gbs"] / hbm_peak,
                            "peak_kind": peak_kind, "traffic": None,
                            "algorithmic_bytes_per_launch": lay["bytes_per_launch"],
-                           "us_per_launch": lay["ms_per_launch"] * 1e3, "parts": rl}
-        out["q4k_gemv_config0"] = config0_gemv(g4, stream)
+                           "us_per_launch": lay["us_per_launch"], "parts": rl}
+        out["q4k_gemv_config0"] = config0_gemv(g4)
         out["q4k_gemv_config0"]["frac"] = out["q4k_gemv_config0"]["gbs"] / hbm_peak
         out["step_hbm_gbs"] = wbytes / (ms_max / a.steps * 1e-3) / 1e9
         if dist.world == 1:
