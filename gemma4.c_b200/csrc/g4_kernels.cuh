@@ -1,6 +1,7 @@
 // g4_kernels.cuh — launchers of the sm_100a kernels (internal to libg4b200).
 #pragma once
 #include "g4_internal.cuh"
+#include "g4_prologue.cuh"
 
 namespace g4 {
 
@@ -27,12 +28,20 @@ struct GemvJob {
 struct GemvJobs {
     GemvJob j[kMaxJobs];
     int njobs;
+    // Optional fused prologue (batch <= 8): the activation of every job is
+    // computed per CTA from the residual stream instead of read from `act`.
+    Prologue pro;
+    int has_pro;     // 1: run `pro`; jobs' act/act_stride are ignored
+    int pro_writer;  // 1: CTA 0 of this launch stores x' (pro.x_out)
+    int red_floats;  // set by the launcher: offset of the prologue area in shared memory
 };
+constexpr int kFusedMaxBatch = 8;
 
 int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStream_t st);
 int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st);
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
-                      int B, int epi, const float *evec, int ld_evec, cudaStream_t st);
+                      int B, int epi, const float *evec, int ld_evec, cudaStream_t st,
+                      const Prologue *pro = nullptr, int pro_writer = 0);
 int launch_qk_block_sums(const void *w, int type, int n, int rows, const void *q8, int *ss, int *sm,
                          cudaStream_t st);
 

@@ -9,6 +9,7 @@
 
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
+#include "g4_prologue.cuh"
 #include "g4_quant.cuh"
 
 namespace g4 {
@@ -49,12 +50,22 @@ __device__ __forceinline__ float gelu_tanh(float x) {  // gelu_f32, main.c:1490-
 __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                          const float *__restrict__ x, int ldx,
                                                          float *__restrict__ out, int ldo, int epi,
-                                                         const float *__restrict__ evec, int ld_evec) {
+                                                         const float *__restrict__ evec, int ld_evec, Prologue pro,
+                                                         int has_pro, int pro_writer) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ float pred[8];
     float *xs = (float *)smem_raw;
     const int s = blockIdx.y;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[(size_t)s * ldx + i];
-    __syncthreads();
+    if (has_pro) {  // x' = x + rmsnorm(delta)*w (per sequence), computed by every CTA
+        Prologue P = pro;
+        P.x_in += (size_t)s * P.dim;
+        if (P.delta) P.delta += (size_t)s * P.dim;
+        if (P.x_out) P.x_out += (size_t)s * P.dim;
+        prologue_run(P, 1, xs, nullptr, pro_writer && blockIdx.x == 0, pred);
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[(size_t)s * ldx + i];
+        __syncthreads();
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + warp;
     if (row >= rows) return;
@@ -100,7 +111,8 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
 }
 
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
-                      int B, int epi, const float *evec, int ld_evec, cudaStream_t st) {
+                      int B, int epi, const float *evec, int ld_evec, cudaStream_t st, const Prologue *pro,
+                      int pro_writer) {
     if (type != G4_F32 && type != G4_F16 && type != G4_BF16) {
         set_error(G4_ERR_TYPE, "gemv_dense: unsupported type %d", type);
         return G4_ERR_TYPE;
@@ -108,7 +120,11 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
     if (rows <= 0 || n <= 0 || B <= 0) return G4_OK;
     const size_t smem = (size_t)n * 4;
     if (smem > 200 * 1024) { set_error(G4_ERR_ARG, "gemv_dense: n=%d too large", n); return G4_ERR_ARG; }
-    gemv_dense_kernel<<<dim3((rows + 7) / 8, B), 256, smem, st>>>(w, type, n, rows, x, ldx, out, ldo, epi, evec, ld_evec);
+    if (pro && pro->dim != n) { set_error(G4_ERR_ARG, "gemv_dense: prologue dim %d != n %d", pro->dim, n); return G4_ERR_ARG; }
+    Prologue P{};
+    if (pro) P = *pro;
+    gemv_dense_kernel<<<dim3((rows + 7) / 8, B), 256, smem, st>>>(w, type, n, rows, x, ldx, out, ldo, epi, evec, ld_evec,
+                                                                  P, pro ? 1 : 0, pro_writer);
     G4_LAUNCHED();
     G4_CUDA(cudaGetLastError());
     return G4_OK;

@@ -14,6 +14,7 @@
 
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
+#include "g4_prologue.cuh"
 #include "g4_quant.cuh"
 
 namespace g4 {
@@ -39,9 +40,7 @@ __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
     for (int i = tid; i < dim; i += blockDim.x) xs[i] = xi[i];
     if (r.delta) {
         const float *dl = r.delta + (size_t)b * dim;
-        float ss = 0.0f;
-        for (int i = tid; i < dim; i += blockDim.x) ss = fmaf(dl[i], dl[i], ss);
-        ss = cta_sum(ss, red);
+        const float ss = canon_sumsq(dl, dim, red);
         const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
         for (int i = tid; i < dim; i += blockDim.x)
             xs[i] = __fadd_rn(xs[i], __fmul_rn(__fmul_rn(dl[i], inv), r.post_w[i]));
@@ -56,9 +55,7 @@ __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
         for (int i = tid; i < dim; i += blockDim.x) xo[i] = xs[i];
     }
     if (!r.pre_w) return;
-    float ss = 0.0f;
-    for (int i = tid; i < dim; i += blockDim.x) ss = fmaf(xs[i], xs[i], ss);
-    ss = cta_sum(ss, red);
+    const float ss = canon_sumsq(xs, dim, red);
     const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
     for (int i = tid; i < dim; i += blockDim.x) {
         const float v = __fmul_rn(__fmul_rn(xs[i], inv), r.pre_w[i]);
