@@ -8,15 +8,17 @@
 //   Q6_K:        sum_e x[e] * ((d*sc)*(q-32)) in fp32, the weight dequantized
 //                exactly like dequant_q6_k (mm_quant_rows, main.c:213-237, 1539-1556).
 //
-// Mapping.  A CTA has 40 lane groups of 8 lanes.  A group owns whole output
-// rows (R = 1 row; 2 rows for the fused gate/up product), so the hot loop has
-// no barrier: the 8 lanes split each 256-weight super-block (16 bytes of
-// quants each), issue the 128-bit loads of up to KU super-blocks at once,
-// accumulate per-lane fp32 partials over the row and reduce them with three
-// shuffles at the end.  The activation (Q8_K values or fp32) sits in shared
-// memory, staged once per CTA, or computed there by the fused prologue.
-// Rows are dealt round-robin over every group of a persistent grid (1 CTA
-// per SM), so each SM streams the same share of the weights.
+// Mapping.  A CTA has 40 lane groups of 8 lanes (10 warps).  1, 2 or 4
+// groups of one warp own an output row (R = 1 row; 2 rows for the fused
+// gate/up product), each summing a contiguous run of its super-blocks, so the
+// hot loop has no barrier: the 8 lanes split each 256-weight super-block (16
+// bytes of quants each), issue the 128-bit loads of KU super-blocks at once,
+// accumulate per-lane fp32 partials and reduce them with 3-5 shuffles at the
+// end.  The activation (Q8_K values or fp32) sits in shared memory, staged
+// once per CTA or computed there by the fused prologue; the first weight
+// loads are issued before that, so staging hides under them.  Rows are dealt
+// round-robin over the warps of a persistent grid (2 CTAs per SM), so every
+// SM streams the same share of the weights.
 #include <math.h>
 
 #include "g4_internal.cuh"
@@ -57,132 +59,197 @@ __device__ __forceinline__ void rs_scales(const uint4 &m, int j, int c, int &sc_
     mn_c = (int)__byte_perm(mn03, mn47, 0x4440 | c) & 0xff;
 }
 
-template <int TYPE, int KU, int R, int NB>
-__device__ __forceinline__ void rs_row_unit(const GemvJob &J, const RsAct &A, int nbc, int row, bool valid,
-                                            float (&acc)[NB][R], int c) {
+template <int TYPE> constexpr int rs_ku(int R) {  // super-blocks per load chunk (registers)
+    return TYPE == G4_Q6_K ? (R == 1 ? 3 : 2) : TYPE == G4_Q5_K ? (R == 1 ? 4 : 2) : (R == 1 ? 5 : 3);
+}
+
+template <int TYPE, int KU, int R>
+struct RsChunk {
+    uint4 a[KU][R], b[KU][R], c[KU][R];
+};
+
+// Issue the loads of super-blocks [k0, k0+KU) (clamped to ke) of `row`.
+template <int TYPE, int KU, int R>
+__device__ __forceinline__ void rs_load(RsChunk<TYPE, KU, R> &w, const GemvJob &J, int row, int k0, int ke, int c) {
     const int nb = J.n / G4_QK;
     const size_t nblk_total = (size_t)J.rows * nb;
+    const int n6 = c >> 2, par = c & 1, h = c & 1;
+#pragma unroll
+    for (int u = 0; u < KU; u++) {
+        const int k = min(k0 + u, ke - 1);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const uint8_t *W = (const uint8_t *)(r ? J.w2 : J.w);
+            const size_t bi = (size_t)row * nb + k;
+            if (TYPE == G4_Q6_K) {
+                const Q6Planes P = q6_planes(W, nblk_total);
+                w.a[u][r] = __ldg(P.ql + bi * 8 + c);
+                w.b[u][r] = __ldg(P.qh + bi * 4 + 2 * n6 + par);
+                const uint2 sc = __ldg(reinterpret_cast<const uint2 *>(P.sc + bi) + n6);
+                w.c[u][r] = make_uint4(sc.x, sc.y, (uint32_t)__ldg(P.d + bi), 0u);
+            } else if (TYPE == G4_Q4_K) {
+                const uint4 *blk = reinterpret_cast<const uint4 *>(W + bi * 144);
+                w.a[u][r] = __ldg(blk);
+                w.b[u][r] = __ldg(blk + 1 + c);
+            } else {
+                const uint4 *blk = reinterpret_cast<const uint4 *>(W + bi * 176);
+                w.a[u][r] = __ldg(blk);
+                w.c[u][r] = __ldg(blk + 1 + h);
+                w.b[u][r] = __ldg(blk + 3 + c);
+            }
+        }
+    }
+}
+
+// Accumulate the loaded chunk into acc[s][r] for the staged sequences.
+template <int TYPE, int KU, int R, int NB>
+__device__ __forceinline__ void rs_compute(const RsChunk<TYPE, KU, R> &w, const GemvJob &J, const RsAct &A, int nbc,
+                                           int k0, int ke, float (&acc)[NB][R], int c) {
+    const int nb = J.n / G4_QK;
     const int j = c >> 1, h = c & 1;
     const int n6 = c >> 2, second = (c >> 1) & 1, par = c & 1;
 #pragma unroll
-    for (int s = 0; s < NB; s++)
+    for (int u = 0; u < KU; u++) {
+        const int k = k0 + u;
+        if (k >= ke) break;
 #pragma unroll
-        for (int r = 0; r < R; r++) acc[s][r] = 0.0f;
-    if (!valid) return;
-    for (int k0 = 0; k0 < nb; k0 += KU) {
-        uint4 wa[KU][R], wb[KU][R], wc[KU][R];
-        // all loads of this chunk first
+        for (int r = 0; r < R; r++) {
+            if (TYPE == G4_Q6_K) {
+                const int sidx = 2 * second + par;
+                const float d = f16_to_f32((uint16_t)w.c[u][r].z);
+                const float dsl = d * (float)(int)(int8_t)((w.c[u][r].x >> (8 * sidx)) & 0xffu);
+                const float dsh = d * (float)(int)(int8_t)((w.c[u][r].y >> (8 * sidx)) & 0xffu);
+                const uint32_t ql[4] = {w.a[u][r].x, w.a[u][r].y, w.a[u][r].z, w.a[u][r].w};
+                const uint32_t qh[4] = {w.b[u][r].x, w.b[u][r].y, w.b[u][r].z, w.b[u][r].w};
+                uint32_t lo[4], hi[4];
 #pragma unroll
-        for (int u = 0; u < KU; u++) {
-            const int k = min(k0 + u, nb - 1);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const uint8_t *W = (const uint8_t *)(r ? J.w2 : J.w);
-                const size_t bi = (size_t)row * nb + k;
-                if (TYPE == G4_Q6_K) {
-                    const Q6Planes P = q6_planes(W, nblk_total);
-                    wa[u][r] = __ldg(P.ql + bi * 8 + c);
-                    wb[u][r] = __ldg(P.qh + bi * 4 + 2 * n6 + par);
-                    const uint2 sc = __ldg(reinterpret_cast<const uint2 *>(P.sc + bi) + n6);
-                    wc[u][r] = make_uint4(sc.x, sc.y, (uint32_t)__ldg(P.d + bi), 0u);
-                } else if (TYPE == G4_Q4_K) {
-                    const uint4 *blk = reinterpret_cast<const uint4 *>(W + bi * 144);
-                    wa[u][r] = __ldg(blk);
-                    wb[u][r] = __ldg(blk + 1 + c);
-                } else {
-                    const uint4 *blk = reinterpret_cast<const uint4 *>(W + bi * 176);
-                    wa[u][r] = __ldg(blk);
-                    wc[u][r] = __ldg(blk + 1 + h);
-                    wb[u][r] = __ldg(blk + 3 + c);
+                for (int i = 0; i < 4; i++) {
+                    lo[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * second)) & 0x03030303u) << 4);
+                    hi[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (4 + 2 * second)) & 0x03030303u) << 4);
                 }
-            }
-        }
+                const int e_lo = k * G4_QK + 128 * n6 + 32 * second + 16 * par;
 #pragma unroll
-        for (int u = 0; u < KU; u++) {
-            const int k = k0 + u;
-            if (k >= nb) break;
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                if (TYPE == G4_Q6_K) {
-                    const int sidx = 2 * second + par;
-                    const float d = f16_to_f32((uint16_t)wc[u][r].z);
-                    const float dsl = d * (float)(int)(int8_t)((wc[u][r].x >> (8 * sidx)) & 0xffu);
-                    const float dsh = d * (float)(int)(int8_t)((wc[u][r].y >> (8 * sidx)) & 0xffu);
-                    const uint32_t ql[4] = {wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w};
-                    const uint32_t qh[4] = {wb[u][r].x, wb[u][r].y, wb[u][r].z, wb[u][r].w};
-                    uint32_t lo[4], hi[4];
+                for (int s = 0; s < NB; s++) {
+                    if (s >= nbc) break;
+                    const float4 *xl = reinterpret_cast<const float4 *>(A.x + (size_t)s * J.n + e_lo);
+                    float a = acc[s][r];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        lo[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * second)) & 0x03030303u) << 4);
-                        hi[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (4 + 2 * second)) & 0x03030303u) << 4);
+                        const float4 vl = xl[i], vh = xl[16 + i];  // +64 elements
+                        a = fmaf(vl.x, dsl * rs_q6(lo[i], 0), a);
+                        a = fmaf(vl.y, dsl * rs_q6(lo[i], 1), a);
+                        a = fmaf(vl.z, dsl * rs_q6(lo[i], 2), a);
+                        a = fmaf(vl.w, dsl * rs_q6(lo[i], 3), a);
+                        a = fmaf(vh.x, dsh * rs_q6(hi[i], 0), a);
+                        a = fmaf(vh.y, dsh * rs_q6(hi[i], 1), a);
+                        a = fmaf(vh.z, dsh * rs_q6(hi[i], 2), a);
+                        a = fmaf(vh.w, dsh * rs_q6(hi[i], 3), a);
                     }
-                    const int e_lo = k * G4_QK + 128 * n6 + 32 * second + 16 * par;
+                    acc[s][r] = a;
+                }
+            } else {
+                const uint32_t qw[4] = {w.b[u][r].x, w.b[u][r].y, w.b[u][r].z, w.b[u][r].w};
+                uint32_t lo[4], hi[4];
 #pragma unroll
-                    for (int s = 0; s < NB; s++) {
-                        if (s >= nbc) break;
-                        const float4 *xl = reinterpret_cast<const float4 *>(A.x + (size_t)s * J.n + e_lo);
-                        float a = acc[s][r];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const float4 vl = xl[i], vh = xl[16 + i];  // +64 elements
-                            a = fmaf(vl.x, dsl * rs_q6(lo[i], 0), a);
-                            a = fmaf(vl.y, dsl * rs_q6(lo[i], 1), a);
-                            a = fmaf(vl.z, dsl * rs_q6(lo[i], 2), a);
-                            a = fmaf(vl.w, dsl * rs_q6(lo[i], 3), a);
-                            a = fmaf(vh.x, dsh * rs_q6(hi[i], 0), a);
-                            a = fmaf(vh.y, dsh * rs_q6(hi[i], 1), a);
-                            a = fmaf(vh.z, dsh * rs_q6(hi[i], 2), a);
-                            a = fmaf(vh.w, dsh * rs_q6(hi[i], 3), a);
-                        }
-                        acc[s][r] = a;
-                    }
-                } else {
-                    const uint32_t qw[4] = {wb[u][r].x, wb[u][r].y, wb[u][r].z, wb[u][r].w};
-                    uint32_t lo[4], hi[4];
+                for (int i = 0; i < 4; i++) {
+                    lo[i] = qw[i] & 0x0F0F0F0Fu;
+                    hi[i] = (qw[i] >> 4) & 0x0F0F0F0Fu;
+                }
+                if (TYPE == G4_Q5_K) {  // 5th bit: bit 2j (low nibbles) / 2j+1 (high) of qh
+                    const uint32_t hw[4] = {w.c[u][r].x, w.c[u][r].y, w.c[u][r].z, w.c[u][r].w};
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        lo[i] = qw[i] & 0x0F0F0F0Fu;
-                        hi[i] = (qw[i] >> 4) & 0x0F0F0F0Fu;
+                        lo[i] |= ((hw[i] >> (2 * j)) & 0x01010101u) << 4;
+                        hi[i] |= ((hw[i] >> (2 * j + 1)) & 0x01010101u) << 4;
                     }
-                    if (TYPE == G4_Q5_K) {  // 5th bit: bit 2j (low nibbles) / 2j+1 (high) of qh
-                        const uint32_t hw[4] = {wc[u][r].x, wc[u][r].y, wc[u][r].z, wc[u][r].w};
+                }
+                int sc_lo, sc_hi, mn_c;
+                rs_scales(w.a[u][r], j, c, sc_lo, sc_hi, mn_c);
+                const float dw = f16_to_f32((uint16_t)(w.a[u][r].x & 0xffffu));
+                const float dmw = f16_to_f32((uint16_t)(w.a[u][r].x >> 16));
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            lo[i] |= ((hw[i] >> (2 * j)) & 0x01010101u) << 4;
-                            hi[i] |= ((hw[i] >> (2 * j + 1)) & 0x01010101u) << 4;
-                        }
-                    }
-                    int sc_lo, sc_hi, mn_c;
-                    rs_scales(wa[u][r], j, c, sc_lo, sc_hi, mn_c);
-                    const float dw = f16_to_f32((uint16_t)(wa[u][r].x & 0xffffu));
-                    const float dmw = f16_to_f32((uint16_t)(wa[u][r].x >> 16));
-#pragma unroll
-                    for (int s = 0; s < NB; s++) {
-                        if (s >= nbc) break;
-                        const int8_t *q8 = A.qs + (size_t)s * J.n + k * G4_QK + 64 * j + 16 * h;
-                        const uint4 al = *reinterpret_cast<const uint4 *>(q8);
-                        const uint4 ah = *reinterpret_cast<const uint4 *>(q8 + 32);
-                        int dl = __dp4a((int)lo[0], (int)al.x, 0);
-                        dl = __dp4a((int)lo[1], (int)al.y, dl);
-                        dl = __dp4a((int)lo[2], (int)al.z, dl);
-                        dl = __dp4a((int)lo[3], (int)al.w, dl);
-                        int dh = __dp4a((int)hi[0], (int)ah.x, 0);
-                        dh = __dp4a((int)hi[1], (int)ah.y, dh);
-                        dh = __dp4a((int)hi[2], (int)ah.z, dh);
-                        dh = __dp4a((int)hi[3], (int)ah.w, dh);
-                        const float dx = A.dx[s * nb + k];
-                        const int ps = sc_lo * dl + sc_hi * dh;
-                        const int pm = mn_c * A.bs2[(s * nb + k) * 8 + c];
-                        acc[s][r] = fmaf(dx * dw, (float)ps, fmaf(-(dx * dmw), (float)pm, acc[s][r]));
-                    }
+                for (int s = 0; s < NB; s++) {
+                    if (s >= nbc) break;
+                    const int8_t *q8 = A.qs + (size_t)s * J.n + k * G4_QK + 64 * j + 16 * h;
+                    const uint4 al = *reinterpret_cast<const uint4 *>(q8);
+                    const uint4 ah = *reinterpret_cast<const uint4 *>(q8 + 32);
+                    int dl = __dp4a((int)lo[0], (int)al.x, 0);
+                    dl = __dp4a((int)lo[1], (int)al.y, dl);
+                    dl = __dp4a((int)lo[2], (int)al.z, dl);
+                    dl = __dp4a((int)lo[3], (int)al.w, dl);
+                    int dh = __dp4a((int)hi[0], (int)ah.x, 0);
+                    dh = __dp4a((int)hi[1], (int)ah.y, dh);
+                    dh = __dp4a((int)hi[2], (int)ah.z, dh);
+                    dh = __dp4a((int)hi[3], (int)ah.w, dh);
+                    const float dx = A.dx[s * nb + k];
+                    const int ps = sc_lo * dl + sc_hi * dh;
+                    const int pm = mn_c * A.bs2[(s * nb + k) * 8 + c];
+                    acc[s][r] = fmaf(dx * dw, (float)ps, fmaf(-(dx * dmw), (float)pm, acc[s][r]));
                 }
             }
         }
     }
 }
 
+// Stage (or compute, with the fused prologue) the activation of sequences
+// [s0, s0+nbc) into shared memory.  Ends with a CTA barrier.
 template <int TYPE, int NB>
-__global__ void __launch_bounds__(kRsThreads, 1) gemv_rs_kernel(GemvJobs jobs, int B) {
+__device__ __forceinline__ void rs_stage(const GemvJobs &jobs, const GemvJob &J, RsAct &A, float *pro_x, int s0,
+                                         int nbc, bool writer, float *pred) {
+    const int n = J.n, nb = n / G4_QK, tid = threadIdx.x, lane = tid & 31;
+    if (jobs.has_pro) {
+        Prologue P = jobs.pro;
+        P.x_in += (size_t)s0 * P.dim;
+        if (P.delta) P.delta += (size_t)s0 * P.dim;
+        if (P.x_out) P.x_out += (size_t)s0 * P.dim;
+        float *xs = TYPE == G4_Q6_K ? A.x : pro_x;
+        prologue_run(P, nbc, xs, nullptr, writer, pred);
+        if (TYPE != G4_Q6_K) {  // quantize into planes
+            const int warp = tid >> 5, nw = blockDim.x >> 5;
+            for (int t = warp; t < nbc * nb; t += nw) {
+                const int s = t / nb, k = t % nb;
+                uint32_t q[2];
+                float d;
+                int ls;
+                warp_quant_block(xs + (size_t)s * n + (size_t)k * G4_QK, lane, q, d, ls);
+                uint32_t *dst = reinterpret_cast<uint32_t *>(A.qs + (size_t)s * n + (size_t)k * G4_QK + 8 * lane);
+                dst[0] = q[0];
+                dst[1] = q[1];
+                int sub = ls + __shfl_xor_sync(0xffffffffu, ls, 1);
+                sub += __shfl_xor_sync(0xffffffffu, sub, 2);
+                if ((lane & 3) == 0) A.bs2[(s * nb + k) * 8 + (lane >> 2)] = sub;
+                if (lane == 0) A.dx[s * nb + k] = d;
+            }
+        }
+    } else if (TYPE == G4_Q6_K) {
+        for (int s = 0; s < nbc; s++) {
+            const float4 *src = reinterpret_cast<const float4 *>((const float *)J.act + (size_t)(s0 + s) * J.act_stride);
+            float4 *dst = reinterpret_cast<float4 *>(A.x + (size_t)s * n);
+            for (int i = tid; i < n / 4; i += blockDim.x) dst[i] = src[i];
+        }
+    } else {
+        const uint8_t *src = (const uint8_t *)J.act + (size_t)s0 * nb * G4_Q8_BYTES;
+        for (int i = tid; i < nbc * nb * 64; i += blockDim.x) {
+            const int blk = i >> 6, w = i & 63;
+            reinterpret_cast<uint32_t *>(A.qs)[blk * 64 + w] =
+                *reinterpret_cast<const uint32_t *>(src + (size_t)blk * G4_Q8_BYTES + 4 + 4 * w);
+        }
+        for (int i = tid; i < nbc * nb * 8; i += blockDim.x) {
+            const int blk = i >> 3, jj = i & 7;
+            const int16_t *bs = reinterpret_cast<const int16_t *>(src + (size_t)blk * G4_Q8_BYTES + 260);
+            A.bs2[i] = (int)bs[2 * jj] + (int)bs[2 * jj + 1];
+            if (jj == 0) A.dx[blk] = *reinterpret_cast<const float *>(src + (size_t)blk * G4_Q8_BYTES);
+        }
+    }
+    __syncthreads();
+}
+
+// Units: a warp takes 4/GPR rows per round (GPR lane groups per row, each
+// summing a contiguous run of the row's super-blocks); warp-round wu =
+// cta + nctas * (warp + 10 * round).
+template <int TYPE, int NB, int R>
+__global__ void __launch_bounds__(kRsThreads, 2) gemv_rs_kernel(GemvJobs jobs, int B) {
+    constexpr int KU = rs_ku<TYPE>(R);
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ unsigned long long best[NB];
     __shared__ float pred[8];
@@ -190,10 +257,13 @@ __global__ void __launch_bounds__(kRsThreads, 1) gemv_rs_kernel(GemvJobs jobs, i
     const GemvJob J = (jobs.njobs > 2 && bx >= jobs.j[2].cta_begin) ? jobs.j[2]
                     : (jobs.njobs > 1 && bx >= jobs.j[1].cta_begin) ? jobs.j[1] : jobs.j[0];
     const int n = J.n, nb = n / G4_QK;
-    const int tid = threadIdx.x, lane = tid & 31, c = lane & 7, g = tid >> 3;
+    const int tid = threadIdx.x, lane = tid & 31, c = lane & 7, warp = tid >> 5, q = (lane >> 3);
     const int cta = bx - J.cta_begin, nctas = J.ctas;
-    constexpr int R = 1;
-    const bool two = J.w2 != nullptr;  // fused gate/up: the unit is a row of both matrices
+    const int GPR = J.rt;                      // lane groups per row (1, 2, 4)
+    const int rpw = 4 / GPR;                   // rows per warp-round
+    const int part = q % GPR;
+    const int bpg = (nb + GPR - 1) / GPR;      // super-blocks per group
+    const int kb = min(part * bpg, nb), ke = min(kb + bpg, nb);
 
     RsAct A;
     uint8_t *p = smem;
@@ -213,91 +283,52 @@ __global__ void __launch_bounds__(kRsThreads, 1) gemv_rs_kernel(GemvJobs jobs, i
     for (int s0 = 0; s0 < B; s0 += NB) {
         const int nbc = min(NB, B - s0);
         if (s0 > 0) __syncthreads();  // previous pass done with the staged activation
-        // ---- stage (or compute) the activation of sequences [s0, s0+nbc)
-        if (jobs.has_pro) {
-            Prologue P = jobs.pro;
-            P.x_in += (size_t)s0 * P.dim;
-            if (P.delta) P.delta += (size_t)s0 * P.dim;
-            if (P.x_out) P.x_out += (size_t)s0 * P.dim;
-            float *xs = TYPE == G4_Q6_K ? A.x : pro_x;
-            prologue_run(P, nbc, xs, nullptr, jobs.pro_writer && bx == 0, pred);
-            if (TYPE != G4_Q6_K) {  // quantize into planes
-                const int warp = tid >> 5, nw = kRsThreads >> 5;
-                for (int t = warp; t < nbc * nb; t += nw) {
-                    const int s = t / nb, k = t % nb;
-                    uint32_t q[2];
-                    float d;
-                    int ls;
-                    warp_quant_block(xs + (size_t)s * n + (size_t)k * G4_QK, lane, q, d, ls);
-                    uint32_t *dst = reinterpret_cast<uint32_t *>(A.qs + (size_t)s * n + (size_t)k * G4_QK + 8 * lane);
-                    dst[0] = q[0];
-                    dst[1] = q[1];
-                    int sub = ls + __shfl_xor_sync(0xffffffffu, ls, 1);
-                    sub += __shfl_xor_sync(0xffffffffu, sub, 2);
-                    if ((lane & 3) == 0) A.bs2[(s * nb + k) * 8 + (lane >> 2)] = sub;
-                    if (lane == 0) A.dx[s * nb + k] = d;
-                }
-            }
-        } else if (TYPE == G4_Q6_K) {
-            for (int s = 0; s < nbc; s++) {
-                const float4 *src = reinterpret_cast<const float4 *>((const float *)J.act + (size_t)(s0 + s) * J.act_stride);
-                float4 *dst = reinterpret_cast<float4 *>(A.x + (size_t)s * n);
-                for (int i = tid; i < n / 4; i += kRsThreads) dst[i] = src[i];
-            }
-        } else {
-            const uint8_t *src = (const uint8_t *)J.act + (size_t)s0 * nb * G4_Q8_BYTES;
-            for (int i = tid; i < nbc * nb * 64; i += kRsThreads) {
-                const int blk = i >> 6, w = i & 63;
-                reinterpret_cast<uint32_t *>(A.qs)[blk * 64 + w] =
-                    *reinterpret_cast<const uint32_t *>(src + (size_t)blk * G4_Q8_BYTES + 4 + 4 * w);
-            }
-            for (int i = tid; i < nbc * nb * 8; i += kRsThreads) {
-                const int blk = i >> 3, jj = i & 7;
-                const int16_t *bs = reinterpret_cast<const int16_t *>(src + (size_t)blk * G4_Q8_BYTES + 260);
-                A.bs2[i] = (int)bs[2 * jj] + (int)bs[2 * jj + 1];
-                if (jj == 0) A.dx[blk] = *reinterpret_cast<const float *>(src + (size_t)blk * G4_Q8_BYTES);
-            }
-        }
         if (tid < NB) best[tid] = 0ull;
-        __syncthreads();
-
-        // ---- rows: unit u = cta + nctas * (g + 40 * round)
         unsigned long long mykey[NB];
 #pragma unroll
         for (int s = 0; s < NB; s++) mykey[s] = 0ull;
+        RsChunk<TYPE, KU, R> w;
+        // first chunk of round 0 is issued before the activation is staged
+        int row0 = (cta + nctas * warp) * rpw + q / GPR;
+        bool v0 = (long)(cta + nctas * warp) * rpw < J.rows && row0 < J.rows && kb < ke;
+        if (v0) rs_load<TYPE, KU, R>(w, J, row0, kb, ke, c);
+        rs_stage<TYPE, NB>(jobs, J, A, pro_x, s0, nbc, jobs.pro_writer && bx == 0, pred);
         for (int round = 0;; round++) {
-            const long u = (long)cta + (long)nctas * (g + (long)kRsGroups * round);
-            // uniform loop exit per warp: all 4 groups of a warp share `round`
-            const long u_warp0 = (long)cta + (long)nctas * ((g & ~3) + (long)kRsGroups * round);
-            if (u_warp0 >= J.rows) break;
-            const bool valid = u < J.rows;
-            const int row = valid ? (int)u : 0;
-            float acc[NB][2];
-            if (two) {
-                float a2[NB][2];
-                rs_row_unit<TYPE, (TYPE == G4_Q6_K ? 2 : 5), 2, NB>(J, A, nbc, row, valid, a2, c);
+            const long wu = (long)cta + (long)nctas * (warp + 10L * round);
+            if (wu * rpw >= J.rows) break;  // uniform per warp
+            const int row = (int)(wu * rpw) + q / GPR;
+            const bool valid = row < J.rows && kb < ke;
+            float acc[NB][R];
 #pragma unroll
-                for (int s = 0; s < NB; s++) { acc[s][0] = a2[s][0]; acc[s][1] = a2[s][1]; }
-            } else {
-                float a1[NB][1];
-                rs_row_unit<TYPE, (TYPE == G4_Q6_K ? 4 : 10), 1, NB>(J, A, nbc, row, valid, a1, c);
+            for (int s = 0; s < NB; s++)
 #pragma unroll
-                for (int s = 0; s < NB; s++) { acc[s][0] = a1[s][0]; acc[s][1] = 0.0f; }
+                for (int r = 0; r < R; r++) acc[s][r] = 0.0f;
+            for (int k0 = kb; k0 < ke; k0 += KU) {
+                if (!(round == 0 && k0 == kb)) {
+                    if (valid) rs_load<TYPE, KU, R>(w, J, row, k0, ke, c);
+                }
+                if (valid) rs_compute<TYPE, KU, R, NB>(w, J, A, nbc, k0, ke, acc, c);
             }
 #pragma unroll
             for (int s = 0; s < NB; s++)
 #pragma unroll
-                for (int r = 0; r < 2; r++)
-#pragma unroll
-                    for (int o = 4; o > 0; o >>= 1) acc[s][r] += __shfl_xor_sync(0xffffffffu, acc[s][r], o, 8);
-            if (c == 0 && valid) {
+                for (int r = 0; r < R; r++) {
+                    float v = acc[s][r];
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    if (GPR >= 2) v += __shfl_xor_sync(0xffffffffu, v, 8);
+                    if (GPR >= 4) v += __shfl_xor_sync(0xffffffffu, v, 16);
+                    acc[s][r] = v;
+                }
+            if (c == 0 && part == 0 && row < J.rows) {
 #pragma unroll
                 for (int s = 0; s < NB; s++) {
                     if (s >= nbc) break;
                     float a = acc[s][0];
                     float *out = J.out ? J.out + (size_t)(s0 + s) * J.out_stride : nullptr;
                     if (J.epi == EPI_GELU_MUL) {
-                        out[row] = rs_gelu(a) * acc[s][1];
+                        out[row] = rs_gelu(a) * acc[s][R - 1];
                     } else if (J.epi == EPI_SOFTCAP_ARGMAX) {
                         if (J.cap > 0.0f) a = J.cap * tanhf(a * (1.0f / J.cap));
                         if (out) out[row] = a;
@@ -311,7 +342,6 @@ __global__ void __launch_bounds__(kRsThreads, 1) gemv_rs_kernel(GemvJobs jobs, i
                 }
             }
         }
-        (void)R;
         if (J.epi == EPI_SOFTCAP_ARGMAX) {
 #pragma unroll
             for (int s = 0; s < NB; s++) {
@@ -340,7 +370,8 @@ static size_t rs_smem(int nb_seq, int n) {
 
 template <int TYPE, int NB>
 static void rs_launch(GemvJobs &jobs, int ctas, size_t smem, int B, cudaStream_t st) {
-    gemv_rs_kernel<TYPE, NB><<<ctas, kRsThreads, smem, st>>>(jobs, B);
+    if (jobs.j[0].w2) gemv_rs_kernel<TYPE, NB, 2><<<ctas, kRsThreads, smem, st>>>(jobs, B);
+    else gemv_rs_kernel<TYPE, NB, 1><<<ctas, kRsThreads, smem, st>>>(jobs, B);
 }
 
 template <int TYPE>
@@ -380,8 +411,8 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
         set_error(G4_ERR_ARG, "gemv: fused prologue needs batch <= %d and dim %% 256 == 0", kFusedMaxBatch);
         return G4_ERR_ARG;
     }
-    long total_rows = 0;
-    for (int i = 0; i < jobs.njobs; i++) total_rows += jobs.j[i].rows;
+    long total_work = 0;
+    for (int i = 0; i < jobs.njobs; i++) total_work += (long)jobs.j[i].rows * (jobs.j[i].n / G4_QK);
     int ctas = 0;
     for (int i = 0; i < jobs.njobs; i++) {
         GemvJob &J = jobs.j[i];
@@ -398,10 +429,16 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
             set_error(G4_ERR_ARG, "gemv: fused prologue dim %d != n %d", jobs.pro.dim, J.n);
             return G4_ERR_ARG;
         }
-        // CTAs in proportion to the job's rows; a group handles whole rows
-        const long grid = (long)g_rs_sms;
-        long cj = (grid * J.rows + total_rows - 1) / total_rows;
-        const long need = (J.rows + kRsGroups - 1) / kRsGroups;
+        // lane groups per row: enough that a group holds about one load chunk
+        const int nbj = J.n / G4_QK;
+        const int ku = type == G4_Q6_K ? 3 : type == G4_Q5_K ? 4 : 5;
+        J.rt = nbj <= ku ? 1 : nbj <= 2 * ku ? 2 : 4;
+        if (J.w2 && J.rt < 4 && nbj > 3) J.rt *= 2;
+        // CTAs in proportion to the job's bytes (rows x super-blocks)
+        const long grid = 2L * g_rs_sms;
+        long cj = (grid * J.rows * nbj + total_work - 1) / total_work;
+        const long warp_rounds = ((long)J.rows * J.rt + 3) / 4;
+        const long need = (warp_rounds + 9) / 10;
         if (cj > need) cj = need;
         if (cj < 1) cj = 1;
         J.ctas = (int)cj;
@@ -420,13 +457,18 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
     return G4_OK;
 }
 
+template <int TYPE, int R>
+static int rs_prime_r() {
+    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 1, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 2, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 4, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 8, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return G4_OK;
+}
 template <int TYPE>
 static int rs_prime() {
-    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_rs_kernel<TYPE, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    return G4_OK;
+    int rc = rs_prime_r<TYPE, 1>();
+    return rc ? rc : rs_prime_r<TYPE, 2>();
 }
 
 int prime_gemv_ks_attrs() {
