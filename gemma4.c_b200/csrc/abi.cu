@@ -489,7 +489,8 @@ int g4_attn_decode(float *out, const float *q, const float *k, const float *v, i
     const size_t qn = (size_t)n_heads * hd;
     Carve cv;
     const size_t oqd = cv.take(qn * 4), ok = cv.take(kk.size() * 4), ov = cv.take(vv.size() * 4),
-                 op = cv.take((size_t)n_heads * max_chunks * (hd + 2) * 4), oo = cv.take(qn * 4), opos = cv.take(4);
+                 op = cv.take((size_t)n_heads * max_chunks * (hd + 2) * 4), oo = cv.take(qn * 4), opos = cv.take(4),
+                 octr = cv.take((size_t)n_kv_heads * 4);
     G4_TRY(scratch_reserve(cv.off));
     uint8_t *s = g_ctx.scratch;
     const int pos = nwin - 1;
@@ -497,12 +498,14 @@ int g4_attn_decode(float *out, const float *q, const float *k, const float *v, i
     G4_CUDA(cudaMemcpyAsync(s + ok, kk.data(), kk.size() * 4, cudaMemcpyHostToDevice, g_ctx.st));
     G4_CUDA(cudaMemcpyAsync(s + ov, vv.data(), vv.size() * 4, cudaMemcpyHostToDevice, g_ctx.st));
     G4_CUDA(cudaMemcpyAsync(s + opos, &pos, 4, cudaMemcpyHostToDevice, g_ctx.st));
+    G4_CUDA(cudaMemsetAsync(s + octr, 0, (size_t)n_kv_heads * 4, g_ctx.st));
     AttnLayer L{};
     L.hd = hd; L.n_rot = 0; L.n_heads = n_heads; L.n_kv = n_kv_heads;
+    L.q = (const float *)(s + oqd); L.prep = 0;
     L.append = 0; L.ring = nwin; L.src_kc = (const float *)(s + ok); L.src_vc = (const float *)(s + ov);
     L.src_ring = nwin; L.window = 0; L.eps = 0.0f;
-    G4_TRY(launch_attn_decode(L, (const float *)(s + oqd), (float *)(s + op), (float *)(s + oo), 1,
-                              (const int *)(s + opos), max_chunks, nwin, g_ctx.st));
+    L.qo = (float *)(s + oo); L.part = (float *)(s + op); L.counters = (int *)(s + octr); L.max_chunks = max_chunks;
+    G4_TRY(launch_attention(L, 1, (const int *)(s + opos), nwin, g_ctx.st));
     G4_CUDA(cudaMemcpyAsync(out, s + oo, qn * 4, cudaMemcpyDeviceToHost, g_ctx.st));
     return sync_ctx();
 }

@@ -58,21 +58,23 @@ struct g4_engine {
     const void *embd = nullptr, *ple_tok = nullptr, *ple_proj = nullptr;
     int embd_t = 0, ple_tok_t = 0, ple_proj_t = 0;
     const float *ple_proj_norm = nullptr, *norm_out = nullptr;
+    float *hidden_src = nullptr;  // buffer holding the State.x view after the last step
     float2 *rope_swa = nullptr, *rope_full = nullptr;
     // state
-    float *x = nullptr, *xn = nullptr, *xf = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qn = nullptr,
+    float *x = nullptr, *x2 = nullptr, *xn = nullptr, *xf = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qn = nullptr,
           *qo = nullptr, *o_raw = nullptr, *hb = nullptr, *hb2 = nullptr, *d_raw = nullptr, *g = nullptr,
           *p_raw = nullptr, *ple_tokb = nullptr, *ple_ctx = nullptr, *ple = nullptr, *logits = nullptr,
           *attn_part = nullptr;
     uint8_t *q8 = nullptr;
     int q8_blocks = 0, max_chunks = 0;
     unsigned long long *keys = nullptr;
-    int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr;
+    int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr, *attn_ctr = nullptr;
     int *h_pos = nullptr, *h_tok = nullptr;
     std::vector<void *> allocs;
     size_t dev_bytes = 0;
     std::map<long, cudaGraphExec_t> graphs;
     std::map<long, int> graph_kernels;  // kernel nodes per captured step
+    std::map<long, float *> graph_hidden;  // where each step leaves State.x
     int last_lm_mode = 0, last_step_kernels = 0;
     std::mutex mu;
 };
@@ -170,7 +172,7 @@ int gemv(g4_engine *e, const void *w, int type, int n, int rows, const float *ac
     return launch_gemv_kquant(jobs, B, e->st);
 }
 
-int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
                        e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
@@ -218,8 +220,9 @@ int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_log
         A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
         A.window = ly.swa ? e->window : 0;
         A.eps = e->eps;
-        TRY(launch_attn_prep(A, e->q, e->k, e->v, e->qn, B, e->d_pos, e->max_seq, e->st));
-        TRY(launch_attn_decode(A, e->qn, e->attn_part, e->qo, B, e->d_pos, e->max_chunks, e->max_seq, e->st));
+        A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
+        A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
+        TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
 
         // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
         TRY(gemv(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
@@ -271,6 +274,163 @@ int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_log
     return G4_OK;
 }
 
+bool is_dense(int t) { return t == G4_F32 || t == G4_F16 || t == G4_BF16; }
+
+// One GEMV whose activation is either computed by a fused prologue (pro != null)
+// or read from act (fp32 [B][ld]; quantized to Q8_K first for Q4_K/Q5_K).
+int gemv_p(g4_engine *e, const void *w, int type, int n, int rows, const Prologue *pro, int writer, const float *act,
+           int ld, float *out, int ldo, int B, int epi = EPI_STORE, const float *evec = nullptr, int ld_evec = 0,
+           unsigned long long *keys = nullptr, float cap = 0.0f) {
+    if (is_dense(type)) {
+        TRY(launch_gemv_dense(w, type, n, rows, act, ld, out, ldo, B, epi == EPI_SOFTCAP_ARGMAX ? EPI_STORE : epi,
+                              evec, ld_evec, e->st, pro, writer));
+        if (epi == EPI_SOFTCAP_ARGMAX) TRY(launch_softcap_argmax(out, rows, ldo, cap, keys, B, e->st));
+        return G4_OK;
+    }
+    GemvJobs jobs{};
+    jobs.njobs = 1;
+    GemvJob &J = jobs.j[0];
+    J.w = w; J.type = type; J.n = n; J.rows = rows;
+    J.out = out; J.out_stride = ldo; J.epi = epi; J.evec = evec; J.ld_evec = ld_evec; J.amax = keys; J.cap = cap;
+    if (pro) {
+        jobs.has_pro = 1;
+        jobs.pro = *pro;
+        jobs.pro_writer = writer;
+    } else if (is_q8_type(type)) {
+        TRY(launch_quantize_q8k(act, ld, e->q8, n, B, e->st));
+        J.act = e->q8;
+    } else {
+        J.act = act;
+        J.act_stride = ld;
+    }
+    return launch_gemv_kquant(jobs, B, e->st);
+}
+
+// The decode step for B <= 8: every residual/norm/quantize step runs as the
+// prologue of the GEMV that consumes it (8 launches per layer).
+int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+    const int dim = e->dim, L = e->L, pd = e->pd;
+    TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
+                       e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
+    TRY(gemv_p(e, e->ple_proj, e->ple_proj_t, dim, pd * L, nullptr, 0, e->x, dim, e->ple_ctx, pd * L, B));
+    TRY(launch_ple_mix(e->ple_tokb, e->ple_ctx, e->ple_proj_norm, pd, L, e->ctx_scale, e->mix_scale, e->eps, e->ple,
+                       B, e->st));
+    float *cur = e->x, *nxt = e->x2;
+    auto flip = [&]() { float *t = cur; cur = nxt; nxt = t; };
+    for (int l = 0; l < L; l++) {
+        const LayerDev &ly = e->layers[l];
+        const LayerDev *prev = l > 0 ? &e->layers[l - 1] : nullptr;
+        const bool has_kv = l < G4_N_LAYER_KV;
+        // x = (x + rms(p_raw)*post_norm[l-1]) * out_scale[l-1]; act = rms(x)*attn_norm[l]
+        Prologue pa{};
+        pa.x_in = cur; pa.delta = prev ? e->p_raw : nullptr; pa.post_w = prev ? prev->post_norm : nullptr;
+        pa.scale = prev ? prev->out_scale : nullptr; pa.x_out = nxt; pa.pre_w = ly.attn_norm; pa.dim = dim;
+        pa.eps = e->eps;
+        struct Proj { const void *w; int t; int rows; float *out; };
+        Proj pr[3] = {{ly.wq, ly.wq_t, ly.qd, e->q}, {ly.wk, ly.wk_t, ly.kvd, e->k}, {ly.wv, ly.wv_t, ly.kvd, e->v}};
+        const int np = has_kv ? 3 : 1;
+        int writer = 1;
+        const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
+        for (int kt : ktypes) {
+            GemvJobs jobs{};
+            for (int i = 0; i < np; i++) {
+                if (pr[i].t != kt) continue;
+                GemvJob &J = jobs.j[jobs.njobs++];
+                J.w = pr[i].w; J.type = kt; J.n = dim; J.rows = pr[i].rows; J.out = pr[i].out;
+                J.out_stride = pr[i].rows; J.epi = EPI_STORE;
+            }
+            if (!jobs.njobs) continue;
+            jobs.has_pro = 1; jobs.pro = pa; jobs.pro_writer = writer;
+            writer = 0;
+            TRY(launch_gemv_kquant(jobs, B, e->st));
+        }
+        for (int i = 0; i < np; i++)
+            if (is_dense(pr[i].t)) {
+                TRY(gemv_p(e, pr[i].w, pr[i].t, dim, pr[i].rows, &pa, writer, nullptr, dim, pr[i].out, pr[i].rows, B));
+                writer = 0;
+            }
+        flip();  // cur = x after the PLE residual of layer l-1
+
+        AttnLayer A{};
+        A.hd = ly.hd; A.n_rot = ly.n_rot; A.n_heads = e->nh; A.n_kv = e->nkv;
+        A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
+        A.q_norm = ly.q_norm; A.k_norm = ly.k_norm;
+        A.rope = ly.swa ? e->rope_swa : e->rope_full;
+        A.append = has_kv; A.kc = ly.kc; A.vc = ly.vc; A.ring = ly.ring;
+        const LayerDev &src = e->layers[ly.src];
+        A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
+        A.window = ly.swa ? e->window : 0;
+        A.eps = e->eps;
+        A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
+        TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
+
+        // O projection: the Q8_K quantization of qo is its prologue
+        Prologue po{};
+        po.x_in = e->qo; po.dim = ly.qd; po.eps = e->eps;
+        TRY(gemv_p(e, ly.wo, ly.wo_t, ly.qd, dim, is_q8_type(ly.wo_t) ? &po : nullptr, 0, e->qo, ly.qd, e->o_raw, dim, B));
+
+        // x += rms(o_raw)*post_attn_norm; act = rms(x)*ffn_norm; gelu(gate)*up
+        Prologue pf{};
+        pf.x_in = cur; pf.delta = e->o_raw; pf.post_w = ly.post_attn_norm; pf.x_out = nxt; pf.pre_w = ly.ffn_norm;
+        pf.dim = dim; pf.eps = e->eps;
+        if (!is_dense(ly.gate_t) && ly.gate_t == ly.up_t) {
+            GemvJobs fj{};
+            fj.njobs = 1;
+            GemvJob &J = fj.j[0];
+            J.w = ly.gate; J.w2 = ly.up; J.type = ly.gate_t; J.n = dim; J.rows = e->hidden;
+            J.out = e->hb; J.out_stride = e->hidden; J.epi = EPI_GELU_MUL;
+            fj.has_pro = 1; fj.pro = pf; fj.pro_writer = 1;
+            TRY(launch_gemv_kquant(fj, B, e->st));
+        } else {
+            TRY(gemv_p(e, ly.gate, ly.gate_t, dim, e->hidden, &pf, 1, nullptr, dim, e->hb, e->hidden, B));
+            TRY(gemv_p(e, ly.up, ly.up_t, dim, e->hidden, &pf, 0, nullptr, dim, e->hb2, e->hidden, B));
+            TRY(launch_gelu_mul(e->hb, e->hb2, (size_t)B * e->hidden, e->st));
+        }
+        flip();
+
+        // down projection (Q8_K quantization of hb as the prologue when needed)
+        Prologue pd_{};
+        pd_.x_in = e->hb; pd_.dim = e->hidden; pd_.eps = e->eps;
+        TRY(gemv_p(e, ly.down, ly.down_t, e->hidden, dim, is_q8_type(ly.down_t) ? &pd_ : nullptr, 0, e->hb,
+                   e->hidden, e->d_raw, dim, B));
+
+        // x += rms(d_raw)*post_ffw_norm; g = gelu(inp_gate.x) * ple[l]; p_raw = proj.g
+        Prologue pg{};
+        pg.x_in = cur; pg.delta = e->d_raw; pg.post_w = ly.post_ffw_norm; pg.x_out = nxt; pg.dim = dim; pg.eps = e->eps;
+        TRY(gemv_p(e, ly.inp_gate, ly.inp_gate_t, dim, pd, &pg, 1, nullptr, dim, e->g, pd, B, EPI_GELU_SCALE,
+                   e->ple + (size_t)l * pd, pd * L));
+        flip();
+        Prologue pp{};
+        pp.x_in = e->g; pp.dim = pd; pp.eps = e->eps;
+        TRY(gemv_p(e, ly.proj, ly.proj_t, pd, dim, is_q8_type(ly.proj_t) ? &pp : nullptr, 0, e->g, pd, e->p_raw, dim, B));
+    }
+    const LayerDev &last = e->layers[L - 1];
+    Prologue pl{};
+    pl.x_in = cur; pl.delta = e->p_raw; pl.post_w = last.post_norm; pl.scale = last.out_scale; pl.x_out = nxt;
+    pl.pre_w = e->norm_out; pl.xn_out = e->xf; pl.dim = dim; pl.eps = e->eps;
+    if (!lm_mode) {  // residual only (State.x after a prefill forward)
+        ResNorm rf{};
+        rf.x_in = cur; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = nxt;
+        rf.dim = dim; rf.eps = e->eps;
+        TRY(launch_resnorm(rf, B, e->st));
+        e->hidden_src = nxt;
+        return G4_OK;
+    }
+    e->hidden_src = e->xf;
+    G4_CUDA(cudaMemsetAsync(e->keys, 0, sizeof(unsigned long long) * B, e->st));
+    const bool dense = is_dense(e->embd_t);
+    TRY(gemv_p(e, e->embd, e->embd_t, dim, e->vocab, &pl, 1, nullptr, dim, (want_logits || dense) ? e->logits : nullptr,
+               e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
+    TRY(launch_keys_to_tokens(e->keys, e->d_next, B, e->st));
+    return G4_OK;
+}
+
+int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+    if (B <= kFusedMaxBatch && e->dim % G4_QK == 0) return enqueue_step_fused(e, B, lm_mode, from_keys, want_logits);
+    e->hidden_src = lm_mode ? e->xf : e->x;
+    return enqueue_step_unfused(e, B, lm_mode, from_keys, want_logits);
+}
+
 int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const long key = ((long)B << 8) | ((long)lm_mode << 2) | ((long)from_keys << 1) | (long)want_logits;
     auto it = e->graphs.find(key);
@@ -292,6 +452,7 @@ int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits)
                 }
         }
         e->graph_kernels[key] = nk;
+        e->graph_hidden[key] = e->hidden_src;
         cudaGraphExec_t ge = nullptr;
         ce = cudaGraphInstantiate(&ge, g, 0);
         cudaGraphDestroy(g);
@@ -301,6 +462,7 @@ int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits)
     G4_CUDA(cudaGraphLaunch(it->second, e->st));
     e->last_lm_mode = lm_mode;
     e->last_step_kernels = e->graph_kernels[key];
+    e->hidden_src = e->graph_hidden[key];
     return G4_OK;
 }
 
@@ -439,7 +601,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     }
     // activations
     const size_t B = max_batch;
-    TRY(dalloc_t(e, &e->x, B * dim)); TRY(dalloc_t(e, &e->xn, B * dim)); TRY(dalloc_t(e, &e->xf, B * dim));
+    TRY(dalloc_t(e, &e->x, B * dim)); TRY(dalloc_t(e, &e->x2, B * dim)); TRY(dalloc_t(e, &e->xn, B * dim)); TRY(dalloc_t(e, &e->xf, B * dim));
     TRY(dalloc_t(e, &e->q, B * e->qd_max)); TRY(dalloc_t(e, &e->qn, B * e->qd_max)); TRY(dalloc_t(e, &e->qo, B * e->qd_max));
     TRY(dalloc_t(e, &e->k, B * e->kvd_max)); TRY(dalloc_t(e, &e->v, B * e->kvd_max));
     TRY(dalloc_t(e, &e->o_raw, B * dim)); TRY(dalloc_t(e, &e->d_raw, B * dim)); TRY(dalloc_t(e, &e->p_raw, B * dim));
@@ -455,6 +617,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     e->max_chunks = (max_seq + attn_chunk_size() - 1) / attn_chunk_size();
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
+    TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
     TRY(dalloc_t(e, &e->d_tokens, B)); TRY(dalloc_t(e, &e->d_next, B)); TRY(dalloc_t(e, &e->d_pos, 1));
     TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * B));
     G4_CUDA(cudaMallocHost((void **)&e->h_pos, sizeof(int) * (size_t)max_seq));
@@ -586,7 +749,7 @@ int g4_engine_get_hidden(g4_engine *e, int b, float *x) {
     std::lock_guard<std::mutex> lk(e->mu);
     G4_CUDA(cudaSetDevice(e->device));
     // after an LM-head step the reference's State.x holds the output-normed vector (main.c:2021)
-    const float *src = (e->last_lm_mode ? e->xf : e->x) + (size_t)b * e->dim;
+    const float *src = (e->hidden_src ? e->hidden_src : e->x) + (size_t)b * e->dim;
     G4_CUDA(cudaMemcpyAsync(x, src, sizeof(float) * e->dim, cudaMemcpyDeviceToHost, e->st));
     G4_CUDA(cudaStreamSynchronize(e->st));
     return G4_OK;

@@ -47,12 +47,13 @@ int launch_qk_block_sums(const void *w, int type, int n, int rows, const void *q
 
 // ---- attention (k_attn.cu)
 
-// Neox RoPE cos/sin table: cs[pos][j] = (cos, sin) of the reference angle
-// for pair j < n_rot/2 (computed on the host, see rope_table_host).
+// One attention layer for the fused decode-attention kernel.
 struct AttnLayer {
     int hd, n_rot, n_heads, n_kv;
+    const float *q, *k, *v;         // raw projections [B][n_heads*hd], [B][n_kv*hd]
+    int prep;                       // 1: q-norm + RoPE here (0: q is ready)
     const float *q_norm, *k_norm;   // device [hd]
-    const float2 *rope;             // device [max_seq][n_rot/2]
+    const float2 *rope;             // device [max_seq][n_rot/2] (cos, sin) or null
     int append;                     // 1: this layer stores K/V (l < 24)
     float *kc, *vc;                 // cache of THIS layer (append target)
     int ring;                       // slots of this layer's cache (window ring or max_seq)
@@ -60,11 +61,12 @@ struct AttnLayer {
     int src_ring;                   // slots of the source cache
     int window;                     // 0: full causal, else sliding window
     float eps;
+    float *qo;                      // output [B][n_heads*hd]
+    float *part;                    // scratch [B][n_heads][max_chunks][hd+2]
+    int *counters;                  // [B][n_kv] zero-initialised tickets
+    int max_chunks;
 };
-int launch_attn_prep(const AttnLayer &L, const float *q, const float *k, const float *v, float *qn, int B,
-                     const int *pos_dev, int max_seq, cudaStream_t st);
-int launch_attn_decode(const AttnLayer &L, const float *qn, float *part, float *qo, int B, const int *pos_dev,
-                       int max_chunks, int max_seq, cudaStream_t st);
+int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq, cudaStream_t st);
 int attn_chunk_size();
 // Host: reference-exact RoPE table for positions [0, npos).
 void rope_table_host(float2 *out, int npos, int n_rot, float base, float freq_scale, const float *ff);

@@ -20,6 +20,7 @@ struct Prologue {
     const float *scale;   // layer_output_scale (1 float) or null
     float *x_out;         // [B][dim] x' (written by the writer CTA) or null
     const float *pre_w;   // [dim] pre-norm weight, or null: act = x'
+    float *xn_out;        // [B][dim] the normalised activation (writer CTA) or null
     int dim;
     float eps;
 };
@@ -68,6 +69,7 @@ __device__ __forceinline__ void prologue_run(const Prologue &P, int B, float *xs
             for (int i = tid; i < dim; i += nt) {  // same thread owns element i in every loop
                 if (writer && P.x_out) P.x_out[(size_t)s * dim + i] = xs[i];
                 xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), P.pre_w[i]);
+                if (writer && P.xn_out) P.xn_out[(size_t)s * dim + i] = xs[i];
             }
         } else if (writer && P.x_out) {
             for (int i = tid; i < dim; i += nt) P.x_out[(size_t)s * dim + i] = xs[i];

@@ -14,13 +14,11 @@
 // layers and max_seq (slot = pos) for global ones.  A ring reads the same
 // logical rows in the same logical order as the reference's linear cache.
 //
-// Kernels:
-//   attn_prep     per (head, sequence): q-norm + RoPE into qn; for layers
-//                 that store KV, k-norm + RoPE and v-norm into the cache slot.
-//   attn_decode   split-K flash-decoding: a CTA owns (chunk of 64 positions,
-//                 kv head, sequence) and all G query heads of that kv head,
-//                 so each K/V row is read from HBM once per step.
-//   attn_combine  merges the chunk partials (max, sum, unnormalised output).
+// One kernel, attn_fused_kernel: split-K flash-decoding where a CTA owns
+// (chunk of 64 positions, kv head, sequence) and all G query heads of that
+// kv head, so each K/V row is read from HBM once per step; the q/k norms,
+// RoPE and the KV append run in the same CTA, and the chunk partials (max,
+// sum, unnormalised output) are merged by the last CTA to finish.
 // The position is read from device memory so one CUDA graph serves all
 // positions; the grid covers the largest window and idle chunks exit.
 #include <math.h>
@@ -51,128 +49,128 @@ void rope_table_host(float2 *out, int npos, int n_rot, float base, float freq_sc
     }
 }
 
-// Sum over the whole CTA (any blockDim.x that is a multiple of 32, <= 1024).
-__device__ __forceinline__ float block_sum(float v, float *red) {
-    v = warp_sum(v);
-    const int nw = blockDim.x >> 5;
-    if (nw == 1) return v;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) red[w] = v;
-    __syncthreads();
-    float t = 0.0f;
-    for (int i = 0; i < nw; i++) t += red[i];
-    return t;
-}
-
-// One CTA per (head, sequence); thread j owns the RoPE pair (j, j + hd/2).
-__global__ void attn_prep_kernel(AttnLayer L, const float *__restrict__ q, const float *__restrict__ k,
-                                 const float *__restrict__ v, float *__restrict__ qn, const int *__restrict__ pos_dev) {
-    __shared__ float red[32];
-    const int hd = L.hd, half = hd / 2, j = threadIdx.x;
-    const int head = blockIdx.x, b = blockIdx.y;
-    const int pos = *pos_dev;
-    const bool is_q = head < L.n_heads;
-    const int kvh = head - L.n_heads;
-    const int qd = L.n_heads * hd, kvd = L.n_kv * hd;
-    const float *src = is_q ? q + (size_t)b * qd + (size_t)head * hd : k + (size_t)b * kvd + (size_t)kvh * hd;
-    float v0 = src[j], v1 = src[j + half];
-    // per-head RMSNorm, seg[i] *= ss * w[i] (main.c:1458-1466)
-    const float ss = block_sum(v0 * v0 + v1 * v1, red);
-    const float inv = 1.0f / sqrtf(ss / (float)hd + L.eps);
-    const float *w = is_q ? L.q_norm : L.k_norm;
-    v0 = v0 * (inv * w[j]);
-    v1 = v1 * (inv * w[j + half]);
-    if (j < L.n_rot / 2) {  // Neox rotation, products rounded separately like the reference
-        const float2 cs = L.rope[(size_t)pos * (L.n_rot / 2) + j];
-        const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-        const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
-        v0 = r0;
-        v1 = r1;
-    }
-    if (is_q) {
-        float *dst = qn + (size_t)b * qd + (size_t)head * hd;
-        dst[j] = v0;
-        dst[j + half] = v1;
-        return;
-    }
-    // K row, then the V row normalised without weight (main.c:1468-1476)
-    const int slot = pos % L.ring;
-    const size_t row = (((size_t)b * L.n_kv + kvh) * L.ring + slot) * hd;
-    L.kc[row + j] = v0;
-    L.kc[row + j + half] = v1;
-    const float *vs = v + (size_t)b * kvd + (size_t)kvh * hd;
-    float u0 = vs[j], u1 = vs[j + half];
-    const float vss = block_sum(u0 * u0 + u1 * u1, red);
-    const float vinv = 1.0f / sqrtf(vss / (float)hd + L.eps);
-    L.vc[row + j] = u0 * vinv;
-    L.vc[row + j + half] = u1 * vinv;
-}
-
-int launch_attn_prep(const AttnLayer &L, const float *q, const float *k, const float *v, float *qn, int B,
-                     const int *pos_dev, int max_seq, cudaStream_t st) {
-    (void)max_seq;
-    if (L.hd % 64 || L.hd > 512) { set_error(G4_ERR_ARG, "attention: head_dim %d unsupported", L.hd); return G4_ERR_ARG; }
-    const int heads = L.n_heads + (L.append ? L.n_kv : 0);
-    attn_prep_kernel<<<dim3(heads, B), L.hd / 2, 0, st>>>(L, q, k, v, qn, pos_dev);
-    G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
-    return G4_OK;
-}
-
-// Partial record of one (sequence, q head, chunk): m, l, o[hd].
-__host__ __device__ inline size_t part_stride(int hd) { return (size_t)hd + 2; }
-
 template <int EPL>
 __device__ __forceinline__ void load_row(float (&dst)[EPL], const float *src) {
     if constexpr (EPL % 4 == 0) {
 #pragma unroll
         for (int e = 0; e < EPL; e += 4) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(src + e));
+            const float4 a = *reinterpret_cast<const float4 *>(src + e);
             dst[e] = a.x; dst[e + 1] = a.y; dst[e + 2] = a.z; dst[e + 3] = a.w;
         }
     } else {
 #pragma unroll
         for (int e = 0; e < EPL; e += 2) {
-            const float2 a = __ldg(reinterpret_cast<const float2 *>(src + e));
+            const float2 a = *reinterpret_cast<const float2 *>(src + e);
             dst[e] = a.x; dst[e + 1] = a.y;
         }
     }
 }
 
-template <int EPL, int G>
-constexpr size_t decode_smem_bytes() {
-    return sizeof(float) * ((size_t)8 * G * EPL * 32 + (size_t)G * kChunk + 2 * G);
+// Per-head RMSNorm (+ weight) and Neox RoPE of one head vector by one warp
+// (main.c:1458-1476, 1725-1745).  Lane l holds elements l + 32 i, so the RoPE
+// partner j + hd/2 of element j sits in the same lane.  Writes dst[hd].
+template <int EPL>
+__device__ __forceinline__ void warp_norm_rope(const float *src, const float *w, const float2 *cs, int n_rot, float eps,
+                                               float *dst, float *dst2) {
+    constexpr int HD = EPL * 32;
+    const int lane = threadIdx.x & 31;
+    float v[EPL];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; i++) {
+        v[i] = src[lane + 32 * i];
+        ss = fmaf(v[i], v[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)HD + eps);
+#pragma unroll
+    for (int i = 0; i < EPL; i++) v[i] = w ? v[i] * (inv * w[lane + 32 * i]) : v[i] * inv;
+    if (cs) {
+#pragma unroll
+        for (int i = 0; i < EPL / 2; i++) {
+            const int j = lane + 32 * i;
+            if (j < n_rot / 2) {  // products rounded separately like the reference
+                const float2 c = cs[j];
+                const float v0 = v[i], v1 = v[i + EPL / 2];
+                v[i] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+                v[i + EPL / 2] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < EPL; i++) {
+        dst[lane + 32 * i] = v[i];
+        if (dst2) dst2[lane + 32 * i] = v[i];
+    }
 }
 
 template <int EPL, int G>
-__global__ void __launch_bounds__(256) attn_decode_kernel(AttnLayer L, const float *__restrict__ qn,
-                                                          float *__restrict__ part, int max_chunks,
-                                                          const int *__restrict__ pos_dev) {
+constexpr size_t attn_smem_bytes() {
+    return sizeof(float) * ((size_t)G * EPL * 32 + (size_t)8 * G * EPL * 32 + (size_t)G * kChunk + 2 * G +
+                            2 * (size_t)EPL * 32 + (size_t)G * 128);
+}
+
+// One CTA per (chunk of 64 positions, kv head, sequence), all G query heads
+// of the kv head: q-norm + RoPE of the G heads; on the chunk holding `pos`
+// of a layer that stores KV, k-norm + RoPE and v-norm of the new row, written
+// to the cache slot; scores, chunk softmax statistics and the unnormalised
+// P.V; then the last CTA of the (kv head, sequence) to finish (atomic ticket,
+// no waiting) merges the chunk partials into qo.
+template <int EPL, int G>
+__global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int *__restrict__ pos_dev) {
     constexpr int HD = EPL * 32;
     extern __shared__ __align__(16) float dsm[];
-    float(*red)[G][HD] = reinterpret_cast<float(*)[G][HD]>(dsm);           // [8][G][HD]
-    float(*sc)[kChunk] = reinterpret_cast<float(*)[kChunk]>(dsm + 8 * G * HD);  // [G][kChunk]
-    float(*ml)[2] = reinterpret_cast<float(*)[2]>(dsm + 8 * G * HD + G * kChunk);
+    float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(dsm);                       // [G][HD]
+    float(*red)[G][HD] = reinterpret_cast<float(*)[G][HD]>(dsm + G * HD);       // [8][G][HD]
+    float(*sc)[kChunk] = reinterpret_cast<float(*)[kChunk]>(dsm + 9 * G * HD);  // [G][kChunk]
+    float(*ml)[2] = reinterpret_cast<float(*)[2]>(dsm + 9 * G * HD + G * kChunk);
+    float *knew = dsm + 9 * G * HD + G * kChunk + 2 * G;                        // [HD]
+    float *vnew = knew + HD;                                                    // [HD]
+    float *wts = vnew + HD;                                                     // [G][128] combine weights
+    __shared__ int ticket;
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *pos_dev;
     int t0 = 0;
     if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
     const int nwin = pos + 1 - t0;
+    const int nch = (nwin + kChunk - 1) / kChunk;
+    if (c >= nch) return;
     const int cbeg = c * kChunk;
-    if (cbeg >= nwin) return;
     const int cnt = min(kChunk, nwin - cbeg);
+    const bool last_chunk = c == nch - 1;
+    const bool new_row = L.append && last_chunk;  // this CTA owns row `pos`
+    const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
+    const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
 
+    // 1. query heads (and the new K/V row) into shared memory
+    if (warp < G) {
+        const float *src = L.q + (size_t)b * qd + (size_t)(h * G + warp) * HD;
+        if (L.prep) {
+            warp_norm_rope<EPL>(src, L.q_norm, cs, L.n_rot, L.eps, qs[warp], nullptr);
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i++) qs[warp][lane + 32 * i] = src[lane + 32 * i];
+        }
+    } else if (new_row && warp == G) {
+        const int slot = pos % L.ring;
+        float *kdst = L.kc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        warp_norm_rope<EPL>(L.k + (size_t)b * kvd + (size_t)h * HD, L.k_norm, cs, L.n_rot, L.eps, knew, kdst);
+    } else if (new_row && warp == G + 1) {
+        const int slot = pos % L.ring;
+        float *vdst = L.vc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        warp_norm_rope<EPL>(L.v + (size_t)b * kvd + (size_t)h * HD, nullptr, nullptr, 0, L.eps, vnew, vdst);
+    }
+    __syncthreads();
     float qv[G][EPL];
 #pragma unroll
-    for (int g = 0; g < G; g++)
-        load_row<EPL>(qv[g], qn + ((size_t)b * L.n_heads + (size_t)h * G + g) * HD + lane * EPL);
+    for (int g = 0; g < G; g++) load_row<EPL>(qv[g], qs[g] + lane * EPL);
     const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
-    // scores: one warp per cached row
+    // 2. scores: one warp per cached row
     for (int tl = warp; tl < cnt; tl += 8) {
         const int t = t0 + cbeg + tl;
-        const float *kr = L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+        const float *kr = (new_row && t == pos) ? knew + lane * EPL
+                                                : L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
         float kv[EPL];
         load_row<EPL>(kv, kr);
 #pragma unroll
@@ -185,7 +183,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnLayer L, const flo
         }
     }
     __syncthreads();
-    // chunk softmax statistics, one warp per query head
+    // 3. chunk softmax statistics, one warp per query head
     if (warp < G) {
         float m = -INFINITY;
         for (int tl = lane; tl < cnt; tl += 32) m = fmaxf(m, sc[warp][tl]);
@@ -193,15 +191,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnLayer L, const flo
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.0f;
         for (int tl = lane; tl < cnt; tl += 32) {
-            const float p = expf(sc[warp][tl] - m);
-            sc[warp][tl] = p;
-            l += p;
+            const float pr = expf(sc[warp][tl] - m);
+            sc[warp][tl] = pr;
+            l += pr;
         }
         l = warp_sum(l);
         if (lane == 0) { ml[warp][0] = m; ml[warp][1] = l; }
     }
     __syncthreads();
-    // unnormalised P.V over the chunk
+    // 4. unnormalised P.V over the chunk
     float acc[G][EPL];
 #pragma unroll
     for (int g = 0; g < G; g++)
@@ -209,14 +207,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnLayer L, const flo
         for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
     for (int tl = warp; tl < cnt; tl += 8) {
         const int t = t0 + cbeg + tl;
-        const float *vr = L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+        const float *vr = (new_row && t == pos) ? vnew + lane * EPL
+                                                : L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
         float vv[EPL];
         load_row<EPL>(vv, vr);
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            const float p = sc[g][tl];
+            const float pr = sc[g][tl];
 #pragma unroll
-            for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(p, vv[e], acc[g][e]);
+            for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(pr, vv[e], acc[g][e]);
         }
     }
 #pragma unroll
@@ -224,99 +223,95 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnLayer L, const flo
 #pragma unroll
         for (int e = 0; e < EPL; e++) red[warp][g][lane * EPL + e] = acc[g][e];
     __syncthreads();
+    // 5. chunk partial -> scratch; the last CTA to finish merges
+    const size_t ps = (size_t)HD + 2;
     for (int i = threadIdx.x; i < G * HD; i += 256) {
         const int g = i / HD, d = i % HD;
         float o = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; w++) o += red[w][g][d];
-        float *pr = part + (((size_t)b * L.n_heads + (size_t)h * G + g) * max_chunks + c) * part_stride(HD);
+        float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + c) * ps;
         pr[2 + d] = o;
         if (d == 0) { pr[0] = ml[g][0]; pr[1] = ml[g][1]; }
     }
-}
-
-// One CTA per (q head, sequence): merge the chunk partials.
-__global__ void attn_combine_kernel(AttnLayer L, const float *__restrict__ part, float *__restrict__ qo,
-                                    int max_chunks, const int *__restrict__ pos_dev) {
-    extern __shared__ float wts[];  // [max_chunks]
-    __shared__ float invL;
-    const int h = blockIdx.x, b = blockIdx.y, hd = L.hd;
-    const int pos = *pos_dev;
-    int t0 = 0;
-    if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
-    const int nwin = pos + 1 - t0;
-    const int nch = (nwin + kChunk - 1) / kChunk;
-    const float *base = part + ((size_t)b * L.n_heads + h) * max_chunks * part_stride(hd);
-    if (threadIdx.x == 0) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ticket = atomicAdd(L.counters + (size_t)b * L.n_kv + h, 1);
+    __syncthreads();
+    if (ticket != nch - 1) return;
+    __threadfence();
+    // merge: M = max_c m_c; out = sum_c e^(m_c-M) o_c / sum_c e^(m_c-M) l_c
+    if (warp < G) {
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + warp) * L.max_chunks * ps;
         float M = -INFINITY;
-        for (int c = 0; c < nch; c++) M = fmaxf(M, base[c * part_stride(hd)]);
+        for (int cc = lane; cc < nch; cc += 32) M = fmaxf(M, __ldcg(base + cc * ps));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float S = 0.0f;
-        for (int c = 0; c < nch; c++) {
-            const float w = expf(base[c * part_stride(hd)] - M);
-            wts[c] = w;
-            S = fmaf(w, base[c * part_stride(hd) + 1], S);
+        for (int cc = lane; cc < nch; cc += 32) {
+            const float wgt = expf(__ldcg(base + cc * ps) - M);
+            if (cc < 128) wts[warp * 128 + cc] = wgt;
+            S = fmaf(wgt, __ldcg(base + cc * ps + 1), S);
         }
-        invL = 1.0f / S;
+        S = warp_sum(S);
+        if (lane == 0) { ml[warp][0] = M; ml[warp][1] = 1.0f / S; }
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    for (int i = threadIdx.x; i < G * HD; i += 256) {
+        const int g = i / HD, d = i % HD;
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps;
         float o = 0.0f;
-        for (int c = 0; c < nch; c++) o = fmaf(wts[c], base[c * part_stride(hd) + 2 + d], o);
-        qo[(size_t)b * L.n_heads * hd + (size_t)h * hd + d] = o * invL;
+        for (int cc = 0; cc < nch; cc++) {
+            const float wgt = cc < 128 ? wts[g * 128 + cc] : expf(__ldcg(base + cc * ps) - ml[g][0]);
+            o = fmaf(wgt, __ldcg(base + cc * ps + 2 + d), o);
+        }
+        L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * ml[g][1];
     }
+    if (threadIdx.x == 0) L.counters[(size_t)b * L.n_kv + h] = 0;  // ready for the next launch
 }
 
 template <int EPL, int G>
-static int launch_decode_eg(dim3 grid, const AttnLayer &L, const float *qn, float *part, int max_chunks,
-                            const int *pos_dev, cudaStream_t st) {
-    const size_t smem = decode_smem_bytes<EPL, G>();
-    attn_decode_kernel<EPL, G><<<grid, 256, smem, st>>>(L, qn, part, max_chunks, pos_dev);
+static int launch_fused_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, cudaStream_t st) {
+    attn_fused_kernel<EPL, G><<<grid, 256, attn_smem_bytes<EPL, G>(), st>>>(L, pos_dev);
     return G4_OK;
 }
 
 template <int EPL>
-static int launch_decode_g(const AttnLayer &L, int G, dim3 grid, const float *qn, float *part, int max_chunks,
-                           const int *pos_dev, cudaStream_t st) {
+static int launch_fused_g(const AttnLayer &L, int G, dim3 grid, const int *pos_dev, cudaStream_t st) {
     switch (G) {
-    case 1: return launch_decode_eg<EPL, 1>(grid, L, qn, part, max_chunks, pos_dev, st);
-    case 2: return launch_decode_eg<EPL, 2>(grid, L, qn, part, max_chunks, pos_dev, st);
-    case 4: return launch_decode_eg<EPL, 4>(grid, L, qn, part, max_chunks, pos_dev, st);
+    case 1: return launch_fused_eg<EPL, 1>(grid, L, pos_dev, st);
+    case 2: return launch_fused_eg<EPL, 2>(grid, L, pos_dev, st);
+    case 4: return launch_fused_eg<EPL, 4>(grid, L, pos_dev, st);
     default: set_error(G4_ERR_ARG, "attention: GQA group %d unsupported", G); return G4_ERR_ARG;
     }
 }
 
-int launch_attn_decode(const AttnLayer &L, const float *qn, float *part, float *qo, int B, const int *pos_dev,
-                       int max_chunks, int max_seq, cudaStream_t st) {
+int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq, cudaStream_t st) {
     const int G = L.n_heads / L.n_kv;
-    if (L.n_heads % L.n_kv) { set_error(G4_ERR_ARG, "attention: n_heads %% n_kv != 0"); return G4_ERR_ARG; }
+    if (L.n_kv <= 0 || L.n_heads % L.n_kv) { set_error(G4_ERR_ARG, "attention: n_heads %% n_kv != 0"); return G4_ERR_ARG; }
     const int span = L.window > 0 ? (L.window < max_seq ? L.window : max_seq) : max_seq;
     const int nch = (span + kChunk - 1) / kChunk;
-    if (nch > max_chunks) { set_error(G4_ERR_ARG, "attention: %d chunks > scratch %d", nch, max_chunks); return G4_ERR_ARG; }
+    if (nch > L.max_chunks) { set_error(G4_ERR_ARG, "attention: %d chunks > scratch %d", nch, L.max_chunks); return G4_ERR_ARG; }
+    if (L.append && G + 2 > 8) { set_error(G4_ERR_ARG, "attention: GQA group %d too large", G); return G4_ERR_ARG; }
     dim3 grid(nch, L.n_kv, B);
     int rc;
     switch (L.hd) {
-    case 64: rc = launch_decode_g<2>(L, G, grid, qn, part, max_chunks, pos_dev, st); break;
-    case 128: rc = launch_decode_g<4>(L, G, grid, qn, part, max_chunks, pos_dev, st); break;
-    case 256: rc = launch_decode_g<8>(L, G, grid, qn, part, max_chunks, pos_dev, st); break;
-    case 512: rc = launch_decode_g<16>(L, G, grid, qn, part, max_chunks, pos_dev, st); break;
+    case 64: rc = launch_fused_g<2>(L, G, grid, pos_dev, st); break;
+    case 128: rc = launch_fused_g<4>(L, G, grid, pos_dev, st); break;
+    case 256: rc = launch_fused_g<8>(L, G, grid, pos_dev, st); break;
+    case 512: rc = launch_fused_g<16>(L, G, grid, pos_dev, st); break;
     default: set_error(G4_ERR_ARG, "attention: head_dim %d unsupported", L.hd); return G4_ERR_ARG;
     }
     if (rc) return rc;
     G4_LAUNCHED();
     G4_CUDA(cudaGetLastError());
-    attn_combine_kernel<<<dim3(L.n_heads, B), 128, (size_t)max_chunks * 4, st>>>(L, part, qo, max_chunks, pos_dev);
-    G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
-}  // namespace g4
-
-namespace g4 {
 template <int EPL, int G>
 static int prime_one() {
-    G4_CUDA(cudaFuncSetAttribute(attn_decode_kernel<EPL, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)decode_smem_bytes<EPL, G>()));
+    G4_CUDA(cudaFuncSetAttribute(attn_fused_kernel<EPL, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attn_smem_bytes<EPL, G>()));
     return G4_OK;
 }
 int prime_attn_attrs() {
@@ -327,4 +322,5 @@ int prime_attn_attrs() {
     rc |= prime_one<16, 1>(); rc |= prime_one<16, 2>(); rc |= prime_one<16, 4>();
     return rc ? G4_ERR_CUDA : G4_OK;
 }
+
 }  // namespace g4

@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
         P.x_in += (size_t)s * P.dim;
         if (P.delta) P.delta += (size_t)s * P.dim;
         if (P.x_out) P.x_out += (size_t)s * P.dim;
+        if (P.xn_out) P.xn_out += (size_t)s * P.dim;
         prologue_run(P, 1, xs, nullptr, pro_writer && blockIdx.x == 0, pred);
     } else {
         for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[(size_t)s * ldx + i];

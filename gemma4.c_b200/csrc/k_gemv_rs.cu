@@ -202,6 +202,7 @@ __device__ __forceinline__ void rs_stage(const GemvJobs &jobs, const GemvJob &J,
         P.x_in += (size_t)s0 * P.dim;
         if (P.delta) P.delta += (size_t)s0 * P.dim;
         if (P.x_out) P.x_out += (size_t)s0 * P.dim;
+        if (P.xn_out) P.xn_out += (size_t)s0 * P.dim;
         float *xs = TYPE == G4_Q6_K ? A.x : pro_x;
         prologue_run(P, nbc, xs, nullptr, writer, pred);
         if (TYPE != G4_Q6_K) {  // quantize into planes
