@@ -46,7 +46,7 @@ int upload_tensor(void *dst, const void *src, int type, int n, int rows, cudaStr
         G4_CUDA(cudaStreamSynchronize(st));
         return G4_OK;
     }
-    // Q6_K: raw blocks through a bounded staging buffer, then split into planes.
+    // Q6_K: raw blocks through a bounded staging buffer, then split into per-row planes.
     const size_t total = (size_t)rows * (n / G4_QK);
     const size_t chunk = total < (size_t)(1 << 20) ? total : (size_t)(1 << 20);  // 1M blocks = 210 MB
     void *tmp = nullptr;
@@ -56,7 +56,7 @@ int upload_tensor(void *dst, const void *src, int type, int n, int rows, cudaStr
         const size_t nb = total - off < chunk ? total - off : chunk;
         cudaError_t e = cudaMemcpyAsync(tmp, (const uint8_t *)src + off * 210, nb * 210, cudaMemcpyHostToDevice, st);
         if (e != cudaSuccess) { rc = cuda_fail(e, "cudaMemcpyAsync", __FILE__, __LINE__); break; }
-        rc = launch_repack_q6(tmp, nb, off, dst, total, st);
+        rc = launch_repack_q6(tmp, nb, off, dst, n / G4_QK, st);
         if (rc == G4_OK) {
             e = cudaStreamSynchronize(st);
             if (e != cudaSuccess) rc = cuda_fail(e, "cudaStreamSynchronize", __FILE__, __LINE__);
@@ -96,6 +96,7 @@ struct Ctx {
     size_t reg_bytes = 0;
     uint8_t *scratch = nullptr;
     size_t scratch_bytes = 0;
+    int *err = nullptr;  // device status word of bounded waits
 };
 
 static std::mutex g_mu;
@@ -125,6 +126,7 @@ static int ctx_ready() {
         cudaSetDevice(g_ctx.device);
         reg_release(g_ctx);
         cudaFree(g_ctx.scratch);
+        cudaFree(g_ctx.err);
         cudaStreamDestroy(g_ctx.st);
         g_ctx = Ctx();
     }
@@ -140,6 +142,8 @@ static int ctx_ready() {
         if (rc) return rc;
     }
     G4_CUDA(cudaStreamCreateWithFlags(&g_ctx.st, cudaStreamNonBlocking));
+    G4_CUDA(cudaMalloc(&g_ctx.err, sizeof(int)));
+    G4_CUDA(cudaMemset(g_ctx.err, 0, sizeof(int)));
     g_ctx.device = dev;
     return G4_OK;
 }
@@ -205,6 +209,7 @@ static int gemv_any(float *o_dev, const float *x_dev, const void *wd, int n, int
         J.w = wd; J.type = type; J.n = n; J.rows = d;
         J.act = (type == G4_Q6_K) ? (const void *)x_dev : q8_dev;
         J.act_stride = n; J.out = o_dev; J.out_stride = d; J.epi = epi; J.amax = keys; J.cap = cap;
+        jobs.err = g_ctx.err;
         return launch_gemv_kquant(jobs, 1, g_ctx.st);
     }
     G4_TRY(launch_gemv_dense(wd, type, n, d, x_dev, n, o_dev, d, 1, EPI_STORE, nullptr, 0, g_ctx.st));
@@ -213,7 +218,14 @@ static int gemv_any(float *o_dev, const float *x_dev, const void *wd, int n, int
 }
 
 static int sync_ctx() {
+    int h = 0;
+    G4_CUDA(cudaMemcpyAsync(&h, g_ctx.err, sizeof(int), cudaMemcpyDeviceToHost, g_ctx.st));
     G4_CUDA(cudaStreamSynchronize(g_ctx.st));
+    if (h) {
+        G4_CUDA(cudaMemset(g_ctx.err, 0, sizeof(int)));
+        set_error(h, "a device-side wait gave up (bounded wait timeout); results are invalid");
+        return h;
+    }
     return G4_OK;
 }
 

@@ -69,7 +69,8 @@ struct g4_engine {
     int q8_blocks = 0, max_chunks = 0;
     unsigned long long *keys = nullptr;
     int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr, *attn_ctr = nullptr;
-    int *h_pos = nullptr, *h_tok = nullptr;
+    int *h_pos = nullptr, *h_tok = nullptr, *h_err = nullptr;
+    int *d_err = nullptr;  // bounded-wait status word written by the kernels
     std::vector<void *> allocs;
     size_t dev_bytes = 0;
     std::map<long, cudaGraphExec_t> graphs;
@@ -144,6 +145,7 @@ void destroy(g4_engine *e) {
     for (void *p : e->allocs) cudaFree(p);
     if (e->h_pos) cudaFreeHost(e->h_pos);
     if (e->h_tok) cudaFreeHost(e->h_tok);
+    if (e->h_err) cudaFreeHost(e->h_err);
     if (e->st) cudaStreamDestroy(e->st);
     delete e;
 }
@@ -169,6 +171,7 @@ int gemv(g4_engine *e, const void *w, int type, int n, int rows, const float *ac
     J.act = is_q8_type(type) ? (const void *)e->q8 : (const void *)act;
     J.act_stride = ld; J.out = out; J.out_stride = ldo; J.epi = epi; J.evec = evec; J.ld_evec = ld_evec;
     J.amax = keys; J.cap = cap;
+    jobs.err = e->d_err;
     return launch_gemv_kquant(jobs, B, e->st);
 }
 
@@ -204,6 +207,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                 J.act = is_q8_type(pr[i].t) ? (const void *)e->q8 : (const void *)e->xn;
                 J.act_stride = dim; J.out = pr[i].out; J.out_stride = pr[i].rows; J.epi = EPI_STORE;
             }
+            jobs.err = e->d_err;
             if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
         }
         for (int i = 0; i < np; i++)
@@ -241,6 +245,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
             J.w = ly.gate; J.w2 = ly.up; J.type = ly.gate_t; J.n = dim; J.rows = e->hidden;
             J.act = is_q8_type(ly.gate_t) ? (const void *)e->q8 : (const void *)e->xn;
             J.act_stride = dim; J.out = e->hb; J.out_stride = e->hidden; J.epi = EPI_GELU_MUL;
+            fj.err = e->d_err;
             TRY(launch_gemv_kquant(fj, B, e->st));
         } else {
             TRY(gemv(e, ly.gate, ly.gate_t, dim, e->hidden, e->xn, dim, is_q8_type(ly.gate_t), e->hb, e->hidden, B));
@@ -303,6 +308,7 @@ int gemv_p(g4_engine *e, const void *w, int type, int n, int rows, const Prologu
         J.act = act;
         J.act_stride = ld;
     }
+    jobs.err = e->d_err;
     return launch_gemv_kquant(jobs, B, e->st);
 }
 
@@ -340,7 +346,7 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
                 J.out_stride = pr[i].rows; J.epi = EPI_STORE;
             }
             if (!jobs.njobs) continue;
-            jobs.has_pro = 1; jobs.pro = pa; jobs.pro_writer = writer;
+            jobs.has_pro = 1; jobs.pro = pa; jobs.pro_writer = writer; jobs.err = e->d_err;
             writer = 0;
             TRY(launch_gemv_kquant(jobs, B, e->st));
         }
@@ -379,7 +385,7 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
             GemvJob &J = fj.j[0];
             J.w = ly.gate; J.w2 = ly.up; J.type = ly.gate_t; J.n = dim; J.rows = e->hidden;
             J.out = e->hb; J.out_stride = e->hidden; J.epi = EPI_GELU_MUL;
-            fj.has_pro = 1; fj.pro = pf; fj.pro_writer = 1;
+            fj.has_pro = 1; fj.pro = pf; fj.pro_writer = 1; fj.err = e->d_err;
             TRY(launch_gemv_kquant(fj, B, e->st));
         } else {
             TRY(gemv_p(e, ly.gate, ly.gate_t, dim, e->hidden, &pf, 1, nullptr, dim, e->hb, e->hidden, B));
@@ -463,6 +469,22 @@ int run_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits)
     e->last_lm_mode = lm_mode;
     e->last_step_kernels = e->graph_kernels[key];
     e->hidden_src = e->graph_hidden[key];
+    return G4_OK;
+}
+
+// Read back the kernels' status word (enqueue before the stream sync).
+int enqueue_err_check(g4_engine *e) {
+    G4_CUDA(cudaMemcpyAsync(e->h_err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->st));
+    return G4_OK;
+}
+int err_after_sync(g4_engine *e) {
+    if (*e->h_err) {
+        const int code = *e->h_err;
+        *e->h_err = 0;
+        cudaMemsetAsync(e->d_err, 0, sizeof(int), e->st);
+        set_error(code, "a device-side wait gave up (bounded wait timeout); results are invalid");
+        return code;
+    }
     return G4_OK;
 }
 
@@ -618,6 +640,9 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
     TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
+    TRY(dalloc_t(e, &e->d_err, 1));
+    G4_CUDA(cudaMallocHost((void **)&e->h_err, sizeof(int)));
+    *e->h_err = 0;
     TRY(dalloc_t(e, &e->d_tokens, B)); TRY(dalloc_t(e, &e->d_next, B)); TRY(dalloc_t(e, &e->d_pos, 1));
     TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * B));
     G4_CUDA(cudaMallocHost((void **)&e->h_pos, sizeof(int) * (size_t)max_seq));
@@ -661,8 +686,9 @@ void *g4_engine_stream(g4_engine *e) { return e ? (void *)e->st : nullptr; }
 int g4_engine_sync(g4_engine *e) {
     if (!e) { set_error(G4_ERR_ARG, "engine is NULL"); return G4_ERR_ARG; }
     G4_CUDA(cudaSetDevice(e->device));
+    TRY(enqueue_err_check(e));
     G4_CUDA(cudaStreamSynchronize(e->st));
-    return G4_OK;
+    return err_after_sync(e);
 }
 
 int g4_forward(g4_engine *e, int token, int pos, int lm_mode, float *logits) {
@@ -679,8 +705,10 @@ int g4_forward(g4_engine *e, int token, int pos, int lm_mode, float *logits) {
             return -1;
         }
     }
+    if (enqueue_err_check(e)) return -1;
     cudaError_t ce = cudaStreamSynchronize(e->st);
     if (ce != cudaSuccess) { cuda_fail(ce, "forward", __FILE__, __LINE__); return -1; }
+    if (err_after_sync(e)) return -1;
     return next;
 }
 
@@ -712,8 +740,10 @@ int g4_generate_greedy(g4_engine *e, const int *prompt, int n_prompt, int max_ne
         set_error(G4_ERR_CUDA, "history readback failed");
         return -1;
     }
+    if (enqueue_err_check(e)) return -1;
     cudaError_t ce = cudaStreamSynchronize(e->st);
     if (ce != cudaSuccess) { cuda_fail(ce, "generate", __FILE__, __LINE__); return -1; }
+    if (err_after_sync(e)) return -1;
     for (int i = 0; i < ngen; i++)
         if (out_tokens[i] == eos) return i;  // the reference stops before emitting eos (main.c:2435)
     return ngen;
@@ -728,8 +758,9 @@ int g4_decode_batch(g4_engine *e, int B, const int *tokens, int pos, int lm_mode
     TRY(stage_tokens(e, tokens, B, pos));
     TRY(run_step(e, B, lm_mode, false, false));
     if (lm_mode) G4_CUDA(cudaMemcpyAsync(next, e->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, e->st));
+    TRY(enqueue_err_check(e));
     G4_CUDA(cudaStreamSynchronize(e->st));
-    return G4_OK;
+    return err_after_sync(e);
 }
 
 int g4_decode_batch_device(g4_engine *e, int B, const int *tokens_dev, int pos, int lm_mode, int *next_dev) {

@@ -2,10 +2,9 @@
 //
 // Weight tensors keep the GGUF super-block layouts of
 // gemma4-4b/cpu-blas/main.c:95-115 in HBM (Q4_K 144 B and Q5_K 176 B blocks
-// are multiples of 16 B, so a row is read with 128-bit loads), except Q6_K:
-// its 210-byte blocks are not 16-byte aligned, so the device copy of a Q6_K
-// tensor is split into four planes (ql 128 B, qh 64 B, scales 16 B per block,
-// then the fp16 d of every block) — same bytes, 16-byte aligned vector loads.
+// are multiples of 16 B, so rows are 16-byte aligned), except Q6_K: its
+// 210-byte blocks are not, so each row of a Q6_K tensor is stored as four
+// planes (ql, qh, scales, d) padded to a multiple of 16 B (see q6_row_bytes).
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,31 +43,42 @@ inline bool type_known(int t) {
 }
 inline bool is_q8_type(int t) { return t == G4_Q4_K || t == G4_Q5_K; }  // is_q8_mm_type, main.c:615-617
 
-// Device copy of a Q6_K tensor with R rows of nb blocks (NB = R*nb blocks):
-//   ql plane NB*128 | qh plane NB*64 | sc plane NB*16 | d plane NB*2 (+pad)
-struct Q6Planes {
+// Device copy of a Q6_K tensor: each row of nb super-blocks is stored as four
+// planes, ql[nb][128] | qh[nb][64] | scales[nb][16] | d[nb] (padded to 16 B),
+// the same bytes as the GGUF blocks but with every row contiguous and 16-byte
+// aligned, so a tile of rows moves with one bulk copy and 128-bit loads.
+__host__ __device__ inline size_t q6_row_bytes(int nb) {
+    return (size_t)nb * 208 + (((size_t)nb * 2 + 15) & ~(size_t)15);
+}
+struct Q6Row {
     const uint4 *ql;
     const uint4 *qh;
     const uint4 *sc;
     const uint16_t *d;
 };
-inline size_t q6_device_bytes(size_t nblocks) { return nblocks * 208 + ((nblocks * 2 + 15) & ~(size_t)15); }
-__host__ __device__ inline Q6Planes q6_planes(const void *base, size_t nblocks) {
-    const uint8_t *b = (const uint8_t *)base;
-    Q6Planes p;
-    p.ql = (const uint4 *)b;
-    p.qh = (const uint4 *)(b + nblocks * 128);
-    p.sc = (const uint4 *)(b + nblocks * 192);
-    p.d = (const uint16_t *)(b + nblocks * 208);
-    return p;
+__host__ __device__ inline Q6Row q6_row_at(const void *row_base, int nb) {
+    const uint8_t *r = (const uint8_t *)row_base;
+    Q6Row q;
+    q.ql = (const uint4 *)r;
+    q.qh = (const uint4 *)(r + (size_t)nb * 128);
+    q.sc = (const uint4 *)(r + (size_t)nb * 192);
+    q.d = (const uint16_t *)(r + (size_t)nb * 208);
+    return q;
 }
 // Device byte size of a weight tensor of `rows` rows of `n` elements.
 inline size_t device_tensor_bytes(int type, int n, int rows) {
-    if (type == G4_Q6_K) return q6_device_bytes((size_t)rows * (n / G4_QK));
+    if (type == G4_Q6_K) return q6_row_bytes(n / G4_QK) * (size_t)rows;
     return row_bytes(type, n) * (size_t)rows;
 }
+// Device bytes of one row (the stride between rows on the device).
+__host__ __device__ inline size_t device_row_bytes(int type, int n) {
+    if (type == G4_Q6_K) return q6_row_bytes(n / G4_QK);
+    if (type == G4_F32) return (size_t)n * 4;
+    if (type == G4_F16 || type == G4_BF16) return (size_t)n * 2;
+    return (size_t)(n / G4_QK) * (type == G4_Q4_K ? 144 : 176);
+}
 
-// Host -> device upload of one weight tensor (Q6_K is split into planes).
+// Host -> device upload of one weight tensor (Q6_K rows split into planes).
 int upload_tensor(void *dst_dev, const void *src_host, int type, int n, int rows, cudaStream_t st);
 
 // ---------------------------------------------------------------- device helpers

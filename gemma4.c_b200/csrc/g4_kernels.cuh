@@ -34,6 +34,7 @@ struct GemvJobs {
     int has_pro;     // 1: run `pro`; jobs' act/act_stride are ignored
     int pro_writer;  // 1: CTA 0 of this launch stores x' (pro.x_out)
     int red_floats;  // set by the launcher: offset of the prologue area in shared memory
+    int *err;        // device status word: a bounded wait that gave up stores G4_ERR_TIMEOUT
 };
 constexpr int kFusedMaxBatch = 8;
 
@@ -91,7 +92,7 @@ int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float em
 int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st);
 int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned long long *keys, int B,
                           cudaStream_t st);
-int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, size_t nblk_total,
+int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, int nb,
                      cudaStream_t st);
 int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, int pd, int L, float ctx_scale,
                    float mix_scale, float eps, float *ple_out, int B, cudaStream_t st);

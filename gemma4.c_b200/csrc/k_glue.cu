@@ -94,16 +94,15 @@ __device__ __forceinline__ float weight_elem(const void *w, int type, int ncols,
     if (type == G4_BF16) return bf16_to_f32(((const uint16_t *)w)[(size_t)row * ncols + e]);
     const int nb = ncols / G4_QK, k = e / G4_QK, i = e % G4_QK;
     if (type == G4_Q6_K) {
-        const Q6Planes P = q6_planes(w, nrows_total * nb);
-        const size_t bi = (size_t)row * nb + k;
-        const uint8_t *ql = (const uint8_t *)(P.ql + bi * 8);
-        const uint8_t *qh = (const uint8_t *)(P.qh + bi * 4);
-        const int8_t *sc = (const int8_t *)(P.sc + bi);
+        const Q6Row P = q6_row_at((const uint8_t *)w + (size_t)row * q6_row_bytes(nb), nb);
+        const uint8_t *ql = (const uint8_t *)(P.ql + (size_t)k * 8);
+        const uint8_t *qh = (const uint8_t *)(P.qh + (size_t)k * 4);
+        const int8_t *sc = (const int8_t *)(P.sc + k);
         const int n6 = i / 128, r = i % 128, qd = r / 32, l = r % 32;
         const int qlb = ql[64 * n6 + (qd & 1) * 32 + l];
         const int lo = (qd >= 2) ? (qlb >> 4) : (qlb & 15);
         const int q = (lo | (((qh[32 * n6 + l] >> (2 * qd)) & 3) << 4)) - 32;
-        const float d = f16_to_f32(P.d[bi]);
+        const float d = f16_to_f32(P.d[k]);
         return __fmul_rn(__fmul_rn(d, (float)sc[8 * n6 + l / 16 + 2 * qd]), (float)q);
     }
     const size_t bb = type == G4_Q4_K ? 144 : 176;
@@ -234,25 +233,27 @@ int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned 
     return G4_OK;
 }
 
-// GGUF Q6_K blocks (210 B) -> device planes (ql | qh | scales | d).
-__global__ void repack_q6_kernel(const uint8_t *raw, size_t nblk, size_t off, uint8_t *planes, size_t total) {
+// GGUF Q6_K blocks (210 B) -> device rows (ql | qh | scales | d planes per row).
+__global__ void repack_q6_kernel(const uint8_t *raw, size_t nblk, size_t off, uint8_t *dst, int nb) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nblk) return;
     const uint8_t *b = raw + i * 210;
-    const size_t gi = off + i;
-    uint8_t *ql = planes + gi * 128, *qh = planes + total * 128 + gi * 64, *sc = planes + total * 192 + gi * 16;
-    uint16_t *d = reinterpret_cast<uint16_t *>(planes + total * 208) + gi;
+    const size_t gi = off + i, row = gi / nb;
+    const int k = (int)(gi % nb);
+    uint8_t *r = dst + row * q6_row_bytes(nb);
+    uint8_t *ql = r + (size_t)k * 128, *qh = r + (size_t)nb * 128 + (size_t)k * 64, *sc = r + (size_t)nb * 192 + (size_t)k * 16;
+    uint16_t *d = reinterpret_cast<uint16_t *>(r + (size_t)nb * 208) + k;
     for (int j = 0; j < 128; j++) ql[j] = b[j];
     for (int j = 0; j < 64; j++) qh[j] = b[128 + j];
     for (int j = 0; j < 16; j++) sc[j] = b[192 + j];
     *d = (uint16_t)(b[208] | (b[209] << 8));
 }
 
-int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, size_t nblk_total,
+int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *planes_dev, int nb,
                      cudaStream_t st) {
     if (!nblk) return G4_OK;
     repack_q6_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>((const uint8_t *)raw_dev, nblk, blk_offset,
-                                                                     (uint8_t *)planes_dev, nblk_total);
+                                                                     (uint8_t *)planes_dev, nb);
     G4_LAUNCHED();
     G4_CUDA(cudaGetLastError());
     return G4_OK;
