@@ -234,29 +234,30 @@ def gemv_roofline(g4, B: int, reps: int = 10):
     return res
 
 
-def config0_gemv(g4, reps: int = 20):
+def config0_gemv(g4, reps: int = 20, rows: int = 10240):
     """Q4_K 10240 x 2560 GEMV at batch 1 (activation
-    quantized to Q8_K once), weights rotated over 20 copies (295 MB > L2),
-    timed as CUDA-graph replays with CUDA events."""
+    quantized to Q8_K once), weights rotated over enough copies to exceed L2
+    (20 copies = 295 MB), timed as CUDA-graph replays with CUDA events.
+    `rows` > 10240 times the same kernel on a taller matrix."""
     import torch
     S = g4.synth
-    copies = 20
+    copies = max(2, 20 * 10240 // rows)
     ws = []
     for c in range(copies):
-        w, xh = S.config0_weights(seed=c)
-        ws.append(g4.weight_upload(w, S.Q4_K, 2560, 10240))
+        w, xh = S.config0_weights(seed=c, rows=rows)
+        ws.append(g4.weight_upload(w, S.Q4_K, 2560, rows))
     x = torch.from_numpy(xh).cuda()
-    o = torch.empty(10240, device="cuda", dtype=torch.float32)
+    o = torch.empty(rows, device="cuda", dtype=torch.float32)
     q8 = torch.empty(10 * 292, device="cuda", dtype=torch.uint8)
     g4.lib().g4d_quantize_row_q8_K(x.data_ptr(), q8.data_ptr(), 2560, 1, None)
     torch.cuda.synchronize()
 
     def run(stream):
         for w in ws:
-            g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, 10240, S.Q4_K, q8.data_ptr(), 1, 1, stream)
+            g4.mm_device(o.data_ptr(), x.data_ptr(), w, 2560, rows, S.Q4_K, q8.data_ptr(), 1, 1, stream)
 
     ms = _graph_time(run, reps, None) / copies
-    byts = 14745600 + 2920 + 40960
+    byts = 1440 * rows + 2920 + 4 * rows
     for w in ws:
         g4.free(w)
     return {"us_per_gemv": ms * 1e3, "gbs": byts / (ms * 1e-3) / 1e9, "bytes": byts}
@@ -274,6 +275,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--gemv-rows", type=int, default=10240, help="gemv0 workload: matrix rows")
     a = ap.parse_args()
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -292,12 +294,12 @@ def main():
     if a.workload == "gemv0":  # BASELINE config 0 alone (used for kernel profiling)
         import torch
         torch.cuda.set_device(0)
-        r = config0_gemv(g4, reps=max(a.steps, 1))
+        r = config0_gemv(g4, reps=max(a.steps, 1), rows=a.gemv_rows)
         hbm_peak, _, kind = measured_peaks()
         print(json.dumps({"metric": "Q4_K GEMV HBM GB/s", "value": r["gbs"], "unit": "GB/s", "n_gpus": 1,
                           "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["us_per_gemv"] / 1e3,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4",
-                          "data": "synthetic", "config": {"workload": "config0 Q4_K 10240x2560 GEMV"},
+                          "data": "synthetic", "config": {"workload": "config0 Q4_K %dx2560 GEMV" % a.gemv_rows},
                           "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": hbm_peak, "unit": "GB/s",
                                        "frac": r["gbs"] / hbm_peak, "peak_kind": kind, "traffic": None}}))
         return

@@ -271,7 +271,6 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     TRY(launch_resnorm(rf, B, e->st));
     if (!lm_mode) return G4_OK;
     // tied LM head + softcap + first-max argmax (1780-1796, 2045-2050)
-    G4_CUDA(cudaMemsetAsync(e->keys, 0, sizeof(unsigned long long) * B, e->st));
     const bool dense = e->embd_t == G4_F32 || e->embd_t == G4_F16 || e->embd_t == G4_BF16;
     TRY(gemv(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, (want_logits || dense) ? e->logits : nullptr,
              e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
@@ -423,7 +422,6 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
         return G4_OK;
     }
     e->hidden_src = e->xf;
-    G4_CUDA(cudaMemsetAsync(e->keys, 0, sizeof(unsigned long long) * B, e->st));
     const bool dense = is_dense(e->embd_t);
     TRY(gemv_p(e, e->embd, e->embd_t, dim, e->vocab, &pl, 1, nullptr, dim, (want_logits || dense) ? e->logits : nullptr,
                e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));

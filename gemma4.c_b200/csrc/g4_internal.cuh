@@ -81,6 +81,32 @@ __host__ __device__ inline size_t device_row_bytes(int type, int n) {
 // Host -> device upload of one weight tensor (Q6_K rows split into planes).
 int upload_tensor(void *dst_dev, const void *src_host, int type, int n, int rows, cudaStream_t st);
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the decode step is launched with programmatic stream
+// serialization: it lets the next kernel be scheduled as soon as all of its
+// own CTAs are running (pdl_trigger at entry), and waits for the previous
+// kernel's results (pdl_wait) only before its first dependent global access.
+// Work that reads nothing produced upstream (weight prefetch, barrier setup)
+// runs before the wait and overlaps the previous kernel's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ float f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }

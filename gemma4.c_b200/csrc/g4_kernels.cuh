@@ -87,7 +87,7 @@ struct ResNorm {
 };
 int launch_resnorm(const ResNorm &r, int B, cudaStream_t st);
 int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
-                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, const unsigned long long *keys,
+                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, unsigned long long *keys,
                    float *x, float *ple_out, int B, cudaStream_t st);
 int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st);
 int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned long long *keys, int B,

@@ -128,6 +128,8 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     float *vnew = knew + HD;                                                    // [HD]
     float *wts = vnew + HD;                                                     // [G][128] combine weights
     __shared__ int ticket;
+    pdl_trigger();
+    pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *pos_dev;
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
 
 template <int EPL, int G>
 static int launch_fused_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, cudaStream_t st) {
-    attn_fused_kernel<EPL, G><<<grid, 256, attn_smem_bytes<EPL, G>(), st>>>(L, pos_dev);
+    G4_CUDA(launch_pdl(attn_fused_kernel<EPL, G>, grid, dim3(256), attn_smem_bytes<EPL, G>(), st, L, pos_dev));
     return G4_OK;
 }
 

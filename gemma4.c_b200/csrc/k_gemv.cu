@@ -18,6 +18,8 @@ namespace g4 {
 
 // x: [B][ldx] floats, y: [B][nb] BlockQ8_K.  grid (nb, B), block 32.
 __global__ void quantize_q8k_kernel(const float *__restrict__ x, int ldx, uint8_t *__restrict__ y, int nb) {
+    pdl_trigger();
+    pdl_wait();
     const int k = blockIdx.x, s = blockIdx.y, lane = threadIdx.x;
     uint32_t q[2];
     float d;
@@ -29,9 +31,8 @@ __global__ void quantize_q8k_kernel(const float *__restrict__ x, int ldx, uint8_
 int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStream_t st) {
     if (n % G4_QK) { set_error(G4_ERR_ARG, "quantize_q8K: k=%d not a multiple of 256", n); return G4_ERR_ARG; }
     if (n == 0 || B == 0) return G4_OK;
-    quantize_q8k_kernel<<<dim3(n / G4_QK, B), 32, 0, st>>>(x, ldx, (uint8_t *)y, n / G4_QK);
+    G4_CUDA(launch_pdl(quantize_q8k_kernel, dim3(n / G4_QK, B), dim3(32), 0, st, x, ldx, (uint8_t *)y, n / G4_QK));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
@@ -54,6 +55,8 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
                                                          int has_pro, int pro_writer) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ float pred[8];
+    pdl_trigger();
+    pdl_wait();
     float *xs = (float *)smem_raw;
     const int s = blockIdx.y;
     if (has_pro) {  // x' = x + rmsnorm(delta)*w (per sequence), computed by every CTA
@@ -124,10 +127,9 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
     if (pro && pro->dim != n) { set_error(G4_ERR_ARG, "gemv_dense: prologue dim %d != n %d", pro->dim, n); return G4_ERR_ARG; }
     Prologue P{};
     if (pro) P = *pro;
-    gemv_dense_kernel<<<dim3((rows + 7) / 8, B), 256, smem, st>>>(w, type, n, rows, x, ldx, out, ldo, epi, evec, ld_evec,
-                                                                  P, pro ? 1 : 0, pro_writer);
+    G4_CUDA(launch_pdl(gemv_dense_kernel, dim3((rows + 7) / 8, B), dim3(256), smem, st, w, type, n, rows, x, ldx, out,
+                       ldo, epi, evec, ld_evec, P, pro ? 1 : 0, pro_writer));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 

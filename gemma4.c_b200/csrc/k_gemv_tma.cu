@@ -1,6 +1,6 @@
 // k_gemv_tma.cu — K-quant GEMV for decode (batch 1..8 per pass): weight tiles
 // streamed into shared memory by bulk asynchronous copies (the TMA engine,
-// cp.async.bulk) through an mbarrier ring, consumed by 8 warps.
+// cp.async.bulk) through an mbarrier ring, consumed by 16 warps.
 //
 // Computes, per activation vector s and output row r of a K-quant matrix W
 // (rows of n/256 super-blocks in the GGUF layouts of main.c:95-115):
@@ -13,7 +13,7 @@
 // Batch-1 decode is a pure weight stream (0.5625 B/weight for Q4_K), so the
 // kernel is built to keep HBM busy: one persistent CTA per SM; warp 8 is the
 // producer and keeps S tiles (each TR contiguous rows, one bulk copy) in
-// flight; warps 0-7 hold 32 lane groups of 8 lanes.  GPR groups (1, 2, 4) of
+// flight; warps 0-15 hold 64 lane groups of 8 lanes.  GPR groups (1, 2, 4) of
 // one warp own a row of the tile and each sums a contiguous run of its
 // super-blocks: the 8 lanes split a 256-weight super-block (16 bytes of
 // quants each), so the reduction is 3-5 shuffles and there is no CTA barrier
@@ -31,7 +31,8 @@
 
 namespace g4 {
 
-constexpr int kTmConsumerWarps = 8;
+constexpr int kTmConsumerWarps = 16;
+constexpr int kTmGroups = kTmConsumerWarps * 4;       // consumer lane groups
 constexpr int kTmThreads = (kTmConsumerWarps + 1) * 32;  // + producer warp
 constexpr int kTmMaxStages = 6;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -250,7 +251,7 @@ __device__ __forceinline__ void tm_stage(const GemvJobs &jobs, const GemvJob &J,
 
 struct TmPlan {   // per launch, computed on the host
     int gpr;      // lane groups per row (1, 2, 4)
-    int tr;       // rows per tile = 32 / gpr
+    int tr;       // rows per tile (<= 64 / gpr)
     int stages;   // ring depth
     int row_bytes;
     int stage_bytes;  // R * tr * row_bytes, 128-aligned
@@ -275,6 +276,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
     const size_t rb = (size_t)plan.row_bytes;
     uint8_t *ring = smem + plan.act_bytes;
     const bool producer = warp == kTmConsumerWarps;
+    pdl_trigger();
 
     TmAct A;
     {
@@ -318,6 +320,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
         const int my_tiles = cta < ntiles ? (ntiles - cta + nctas - 1) / nctas : 0;
         if (producer && lane == 0)
             for (; issued < my_tiles && issued < S; issued++) issue(issued);
+        pdl_wait();  // activation / residual from the previous kernel; weights above do not depend on it
         tm_stage<TYPE>(jobs, J, A, pro_x, s0, nbc, jobs.pro_writer && bx == 0, pred);
 
         if (producer) {
@@ -342,10 +345,11 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
             unsigned long long mykey[NB];
 #pragma unroll
             for (int s = 0; s < NB; s++) mykey[s] = 0ull;
-            const int g = warp * 4 + q;               // consumer lane group 0..31
+            const int g = warp * 4 + q;               // consumer lane group
             const int rl = g / GPR, part = g % GPR;  // tile row, block run
             const int bpg = (nb + GPR - 1) / GPR;
             const int kb = min(part * bpg, nb), ke = min(kb + bpg, nb);
+            const bool grp_on = rl < TR;             // long rows: fewer tile rows than groups
             for (int i = 0; i < my_tiles; i++) {
                 const int tile = cta + i * nctas, st = i % S;
                 if (!mbar_wait(&full[st], (i / S) & 1)) {
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                 }
                 const uint8_t *stage = ring + (size_t)st * plan.stage_bytes;
                 const int row = tile * TR + rl;
-                const bool valid = row < J.rows;
+                const bool valid = grp_on && row < J.rows;
                 float acc[R][NB];
 #pragma unroll
                 for (int r = 0; r < R; r++)
@@ -440,7 +444,7 @@ static size_t tm_act_bytes(int nbs, int n) {
 
 template <int TYPE, int NB, int R>
 static void tm_launch(GemvJobs &jobs, int ctas, size_t smem, int B, const TmPlan &plan, cudaStream_t st) {
-    gemv_tma_kernel<TYPE, NB, R><<<ctas, kTmThreads, smem, st>>>(jobs, B, plan);
+    (void)launch_pdl(gemv_tma_kernel<TYPE, NB, R>, dim3(ctas), dim3(kTmThreads), smem, st, jobs, B, plan);
 }
 
 template <int TYPE, int NB>
@@ -460,12 +464,16 @@ static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st) {
         }
     TmPlan plan{};
     plan.gpr = nb <= 6 ? 1 : nb <= 12 ? 2 : 4;
-    plan.tr = 32 / plan.gpr;
     plan.row_bytes = (int)device_row_bytes(TYPE, n);
-    plan.stage_bytes = (int)(((size_t)R * plan.tr * plan.row_bytes + 127) & ~(size_t)127);
     int nbs = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
-    while (nbs > 1 && tm_act_bytes<TYPE>(nbs, n) + 2 * (size_t)plan.stage_bytes > (size_t)kTmSmemBudget) nbs /= 2;
+    while (nbs > 1 && tm_act_bytes<TYPE>(nbs, n) > (size_t)kTmSmemBudget / 3) nbs /= 2;
     plan.act_bytes = (int)((tm_act_bytes<TYPE>(nbs, n) + 127) & ~(size_t)127);
+    // rows per tile: one row per GPR groups, at most what lets >= 3 stages fit
+    int tr = kTmGroups / plan.gpr;
+    const int fit = (kTmSmemBudget - plan.act_bytes) / (3 * R * plan.row_bytes);
+    if (tr > fit) tr = fit > 1 ? fit : 1;
+    plan.tr = tr;
+    plan.stage_bytes = (int)(((size_t)R * plan.tr * plan.row_bytes + 127) & ~(size_t)127);
     int stages = (kTmSmemBudget - plan.act_bytes) / plan.stage_bytes;
     if (stages > kTmMaxStages) stages = kTmMaxStages;
     if (stages < 2) {
@@ -524,7 +532,7 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
         // persistent CTAs (1 per SM) shared out in proportion to the job's bytes
         const int nbj = J.n / G4_QK;
         const int gpr = nbj <= 6 ? 1 : nbj <= 12 ? 2 : 4;
-        const long tiles = (J.rows + 32 / gpr - 1) / (32 / gpr);
+        const long tiles = (J.rows + kTmGroups / gpr - 1) / (kTmGroups / gpr);
         long cj = ((long)g_tm_sms * J.rows * nbj + total_work - 1) / total_work;
         if (cj > tiles) cj = tiles;
         if (cj < 1) cj = 1;

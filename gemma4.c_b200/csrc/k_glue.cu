@@ -34,6 +34,8 @@ __device__ __forceinline__ float cta_sum(float v, float *red) {
 __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
     extern __shared__ __align__(16) float xs[];  // [dim] x, then [dim] xn
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x, dim = r.dim, tid = threadIdx.x;
     float *xn = xs + dim;
     const float *xi = r.x_in + (size_t)b * dim;
@@ -79,9 +81,8 @@ int launch_resnorm(const ResNorm &r, int B, cudaStream_t st) {
     if (r.q8_out && r.dim % G4_QK) { set_error(G4_ERR_ARG, "resnorm: dim %d not a multiple of 256", r.dim); return G4_ERR_ARG; }
     const size_t smem = (size_t)r.dim * 8;
     if (smem > 100 * 1024) { set_error(G4_ERR_ARG, "resnorm: dim %d too large", r.dim); return G4_ERR_ARG; }
-    resnorm_kernel<<<B, 512, smem, st>>>(r);
+    G4_CUDA(launch_pdl(resnorm_kernel, dim3(B), dim3(512), smem, st, r));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
@@ -122,10 +123,14 @@ __device__ __forceinline__ float weight_elem(const void *w, int type, int ncols,
 
 __global__ void embed_kernel(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
                              int ple_tok_t, int ple_row, float ple_scale, const int *tokens,
-                             const unsigned long long *keys, float *x, float *ple_out) {
+                             unsigned long long *keys, float *x, float *ple_out) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x;
     int tok = tokens ? tokens[b] : argmax_key_index(keys[b]);
     if (tok < 0 || (size_t)tok >= vocab) tok = 0;  // no LM-head result yet: never index out of the table
+    __syncthreads();
+    if (threadIdx.x == 0) keys[b] = 0ull;  // reset for this step's LM-head argmax
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
         x[(size_t)b * dim + i] = __fmul_rn(weight_elem(embd, embd_t, dim, vocab, tok, i), emb_scale);
     if (ple_out)
@@ -134,12 +139,11 @@ __global__ void embed_kernel(const void *embd, int embd_t, int dim, size_t vocab
 }
 
 int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,
-                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, const unsigned long long *keys,
+                   int ple_tok_t, int ple_row, float ple_scale, const int *tokens, unsigned long long *keys,
                    float *x, float *ple_out, int B, cudaStream_t st) {
-    embed_kernel<<<B, 512, 0, st>>>(embd, embd_t, dim, vocab, emb_scale, ple_tok, ple_tok_t, ple_row, ple_scale, tokens,
-                                    keys, x, ple_out);
+    G4_CUDA(launch_pdl(embed_kernel, dim3(B), dim3(512), 0, st, embd, embd_t, dim, vocab, emb_scale, ple_tok, ple_tok_t,
+                       ple_row, ple_scale, tokens, keys, x, ple_out));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
@@ -148,6 +152,8 @@ __global__ void ple_mix_kernel(const float *ple_tok, const float *ple_ctx, const
                                float ctx_scale, float mix_scale, float eps, float *ple_out) {
     __shared__ float red[32];
     __shared__ float cs[1024];
+    pdl_trigger();
+    pdl_wait();
     const int l = blockIdx.x, b = blockIdx.y;
     const size_t off = (size_t)b * L * pd + (size_t)l * pd;
     float ss = 0.0f;
@@ -167,21 +173,22 @@ __global__ void ple_mix_kernel(const float *ple_tok, const float *ple_ctx, const
 int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, int pd, int L, float ctx_scale,
                    float mix_scale, float eps, float *ple_out, int B, cudaStream_t st) {
     if (pd > 1024) { set_error(G4_ERR_ARG, "ple_dim %d > 1024", pd); return G4_ERR_ARG; }
-    ple_mix_kernel<<<dim3(L, B), 256, 0, st>>>(ple_tok, ple_ctx, norm_w, pd, L, ctx_scale, mix_scale, eps, ple_out);
+    G4_CUDA(launch_pdl(ple_mix_kernel, dim3(L, B), dim3(256), 0, st, ple_tok, (const float *)ple_ctx, norm_w, pd, L,
+                       ctx_scale, mix_scale, eps, ple_out));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
 __global__ void keys_to_tokens_kernel(const unsigned long long *keys, int *tokens, int B) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) tokens[b] = argmax_key_index(keys[b]);
 }
 
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st) {
-    keys_to_tokens_kernel<<<(B + 127) / 128, 128, 0, st>>>(keys, tokens, B);
+    G4_CUDA(launch_pdl(keys_to_tokens_kernel, dim3((B + 127) / 128), dim3(128), 0, st, keys, tokens, B));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
@@ -194,20 +201,23 @@ __device__ __forceinline__ float gelu_ref(float x) {  // gelu_f32, main.c:1490-1
 }
 
 __global__ void gelu_mul_kernel(float *a, const float *b, size_t n) {
+    pdl_trigger();
+    pdl_wait();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) a[i] = gelu_ref(a[i]) * b[i];
 }
 
 int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st) {
-    gelu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, b, n);
+    G4_CUDA(launch_pdl(gelu_mul_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a, b, n));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
 // Softcap in place (main.c:1790-1795) and first-max argmax per sequence
 // (sample_token temp <= 0, main.c:2045-2050) for LM heads of dense types.
 __global__ void softcap_argmax_kernel(float *logits, int vocab, int ld, float cap, unsigned long long *keys) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.y;
     float *lg = logits + (size_t)b * ld;
     unsigned long long best = 0ull;
@@ -227,9 +237,8 @@ __global__ void softcap_argmax_kernel(float *logits, int vocab, int ld, float ca
 
 int launch_softcap_argmax(float *logits, int vocab, int ld, float cap, unsigned long long *keys, int B,
                           cudaStream_t st) {
-    softcap_argmax_kernel<<<dim3(148, B), 256, 0, st>>>(logits, vocab, ld, cap, keys);
+    G4_CUDA(launch_pdl(softcap_argmax_kernel, dim3(148, B), dim3(256), 0, st, logits, vocab, ld, cap, keys));
     G4_LAUNCHED();
-    G4_CUDA(cudaGetLastError());
     return G4_OK;
 }
 
