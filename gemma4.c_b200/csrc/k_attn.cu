@@ -15,7 +15,7 @@
 // logical rows in the same logical order as the reference's linear cache.
 //
 // One kernel, attn_fused_kernel: split-K flash-decoding where a CTA owns
-// (chunk of 64 positions, kv head, sequence) and all G query heads of that
+// (chunk of 32 positions, kv head, sequence) and all G query heads of that
 // kv head, so each K/V row is read from HBM once per step; the q/k norms,
 // RoPE and the KV append run in the same CTA, and the chunk partials (max,
 // sum, unnormalised output) are merged by the last CTA to finish.
@@ -28,7 +28,8 @@
 
 namespace g4 {
 
-constexpr int kChunk = 64;
+constexpr int kChunk = 32;  // positions per CTA (8 warps x 4 rows, loads issued together)
+constexpr int kMaxWts = 512;  // chunk weights kept in shared memory by the merging CTA
 int attn_chunk_size() { return kChunk; }
 
 // Reference-exact RoPE angles (apply_rope_neox, main.c:1725-1745): theta
@@ -107,10 +108,10 @@ __device__ __forceinline__ void warp_norm_rope(const float *src, const float *w,
 template <int EPL, int G>
 constexpr size_t attn_smem_bytes() {
     return sizeof(float) * ((size_t)G * EPL * 32 + (size_t)8 * G * EPL * 32 + (size_t)G * kChunk + 2 * G +
-                            2 * (size_t)EPL * 32 + (size_t)G * 128);
+                            2 * (size_t)EPL * 32 + (size_t)G * kMaxWts);
 }
 
-// One CTA per (chunk of 64 positions, kv head, sequence), all G query heads
+// One CTA per (chunk of 32 positions, kv head, sequence), all G query heads
 // of the kv head: q-norm + RoPE of the G heads; on the chunk holding `pos`
 // of a layer that stores KV, k-norm + RoPE and v-norm of the new row, written
 // to the cache slot; scores, chunk softmax statistics and the unnormalised
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     float(*ml)[2] = reinterpret_cast<float(*)[2]>(dsm + 9 * G * HD + G * kChunk);
     float *knew = dsm + 9 * G * HD + G * kChunk + 2 * G;                        // [HD]
     float *vnew = knew + HD;                                                    // [HD]
-    float *wts = vnew + HD;                                                     // [G][128] combine weights
+    float *wts = vnew + HD;                                                     // [G][kMaxWts] combine weights
     __shared__ int ticket;
     pdl_trigger();
     pdl_wait();
@@ -168,20 +169,29 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
 #pragma unroll
     for (int g = 0; g < G; g++) load_row<EPL>(qv[g], qs[g] + lane * EPL);
     const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
-    // 2. scores: one warp per cached row
-    for (int tl = warp; tl < cnt; tl += 8) {
-        const int t = t0 + cbeg + tl;
-        const float *kr = (new_row && t == pos) ? knew + lane * EPL
-                                                : L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
-        float kv[EPL];
-        load_row<EPL>(kv, kr);
+    // 2. scores: warp w owns rows w, w+8, ...; all its row loads are issued first
+    constexpr int RPW = kChunk / 8;
+    {
+        float kv[RPW][EPL];
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float s = 0.0f;
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+            const int t = t0 + cbeg + min(tl, cnt - 1);
+            const float *kr = (new_row && t == pos) ? knew + lane * EPL
+                                                    : L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+            load_row<EPL>(kv[r], kr);
+        }
 #pragma unroll
-            for (int e = 0; e < EPL; e++) s = fmaf(kv[e], qv[g][e], s);
-            s = warp_sum(s);
-            if (lane == 0) sc[g][tl] = s;
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float sv = 0.0f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) sv = fmaf(kv[r][e], qv[g][e], sv);
+                sv = warp_sum(sv);
+                if (lane == 0 && tl < cnt) sc[g][tl] = sv;
+            }
         }
     }
     __syncthreads();
@@ -207,17 +217,26 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
-    for (int tl = warp; tl < cnt; tl += 8) {
-        const int t = t0 + cbeg + tl;
-        const float *vr = (new_row && t == pos) ? vnew + lane * EPL
-                                                : L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
-        float vv[EPL];
-        load_row<EPL>(vv, vr);
+    {
+        float vv[RPW][EPL];
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float pr = sc[g][tl];
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+            const int t = t0 + cbeg + min(tl, cnt - 1);
+            const float *vr = (new_row && t == pos) ? vnew + lane * EPL
+                                                    : L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+            load_row<EPL>(vv[r], vr);
+        }
 #pragma unroll
-            for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(pr, vv[e], acc[g][e]);
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+            if (tl >= cnt) break;
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float pr = sc[g][tl];
+#pragma unroll
+                for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(pr, vv[r][e], acc[g][e]);
+            }
         }
     }
 #pragma unroll
@@ -252,7 +271,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
         float S = 0.0f;
         for (int cc = lane; cc < nch; cc += 32) {
             const float wgt = expf(__ldcg(base + cc * ps) - M);
-            if (cc < 128) wts[warp * 128 + cc] = wgt;
+            if (cc < kMaxWts) wts[warp * kMaxWts + cc] = wgt;
             S = fmaf(wgt, __ldcg(base + cc * ps + 1), S);
         }
         S = warp_sum(S);
@@ -264,7 +283,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
         const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps;
         float o = 0.0f;
         for (int cc = 0; cc < nch; cc++) {
-            const float wgt = cc < 128 ? wts[g * 128 + cc] : expf(__ldcg(base + cc * ps) - ml[g][0]);
+            const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps) - ml[g][0]);
             o = fmaf(wgt, __ldcg(base + cc * ps + 2 + d), o);
         }
         L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * ml[g][1];

@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
     if (type == G4_F32) {
         const float *r = (const float *)w + (size_t)row * n;
         if (vec) {
+#pragma unroll 5
             for (int j = lane * 4; j < n; j += 128) {
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(r + j));
                 acc = fmaf(a.x, xs[j], acc); acc = fmaf(a.y, xs[j + 1], acc);
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
         const uint16_t *r = (const uint16_t *)w + (size_t)row * n;
         const bool bf = type == G4_BF16;
         if (vec) {
+#pragma unroll 5
             for (int j = lane * 8; j < n; j += 256) {
                 const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + j));
                 const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
