@@ -68,6 +68,7 @@ SIGNATURES = [
     ("g4d_free", ip, [vp]),
     ("g4d_quantize_row_q8_K", ip, [vp, vp, ip, ip, vp]),
     ("g4d_mm", ip, [vp, vp, vp, ip, ip, ip, vp, ip, ip, vp]),
+    ("g4d_attn_decode_noalloc", ip, [vp, vp, vp, vp, ip, ip, ip, ip, vp]),
     ("g4_model_desc_bytes", C.c_size_t, []),
     ("g4_engine_create", vp, [vp, ip, ip, ip]),
     ("g4_engine_destroy", ip, [vp]),

@@ -157,6 +157,19 @@ int g4d_quantize_row_q8_K(const float *x, g4_block_q8_K *y, int k, int batch, vo
 int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_block_q8_K *q8, int q8_ready,
            int batch, void *stream);
 
+/* Decode attention (the result of g4_attn_decode) on DEVICE pointers, for
+ * callers that cannot let the library allocate device memory.  This entry
+ * point has no counterpart in the reference.  It calls no cudaMalloc/cudaFree:
+ * its scratch is a 4 MiB array compiled into the library (held on every GPU
+ * that loads it), so n_heads * ceil(nwin/32) * (hd + 2) * 4 bytes plus about
+ * 512 must fit in 4 MiB, else G4_ERR_ARG.  k and v are [n_kv_heads][nwin][hd]
+ * (each kv head's rows contiguous), q [n_heads * hd], out [n_heads * hd].
+ * The first call on a device looks the array up and should precede any
+ * stream capture; calls that may overlap on the GPU share the array and must
+ * be serialised by the caller. */
+int g4d_attn_decode_noalloc(float *out, const float *q, const float *k, const float *v, int nwin, int n_heads,
+                            int n_kv_heads, int hd, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* 2. Device-resident engine                                           */
 /* ------------------------------------------------------------------ */
