@@ -6,10 +6,13 @@ HBM GB/s vs peak).
 
 Workloads (seeded synthetic data with the reference configurations' shapes;
 random-init Gemma-4-E4B-shaped Q4_K_M model, no network, no real GGUF):
-  batch64  BASELINE config 4: 64 independent sequences, each prefilled with a
-           seeded random prompt (4096 tokens), then greedy decode.  The 64
-           sequences are sharded over the N ranks (one process per GPU, no
-           collective on the data path) -> "scaling": "strong".
+  batch64  BASELINE config 4: 64 independent sequences with a 4096-token
+           context, then greedy decode.  The prompt's KV rows are filled from a
+           seed (--prefill fill; a decode step's work does not depend on them)
+           and the last prompt token runs through the model; --prefill run
+           decodes the whole prompt.  The 64 sequences are sharded over the N
+           ranks (one process per GPU, no collective on the data path) ->
+           "scaling": "strong".
   batch1   BASELINE config 3: one sequence, 512-token prompt, greedy decode.
 A step is one decode position for all local sequences.  `value` is whole-job
 tokens/s with token ids and weights already in HBM (greedy feedback on the
@@ -274,6 +277,9 @@ def main():
     ap.add_argument("--seqs", type=int, default=None, help="total sequences (default 64 / 1)")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--prefill", default=None, choices=["run", "fill"],
+                    help="run: decode the prompt position by position; fill: seeded KV rows for the prompt "
+                         "(default: fill for batch64, run for batch1)")
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--gemv-rows", type=int, default=10240, help="gemv0 workload: matrix rows")
     a = ap.parse_args()
@@ -342,10 +348,16 @@ def main():
     allp = rng.integers(0, S.E4B.vocab_size, size=(seqs, prompt), dtype=np.int32)
     mine = allp[dist.rank * B:(dist.rank + 1) * B]
     prompts_dev = torch.from_numpy(np.ascontiguousarray(mine.T)).cuda()  # [prompt][B]
+    prefill = a.prefill or ("fill" if a.workload == "batch64" else "run")
+    cfg["prefill"] = prefill
     t0 = time.perf_counter()
-    for pos in range(prompt):
-        lm = 1 if pos == prompt - 1 else 0
-        eng.decode_batch_device(B, prompts_dev.data_ptr() + pos * B * 4, pos, lm, None)
+    if prefill == "fill":  # KV rows of the prompt from a seed; the last prompt token runs for real
+        eng.fill_kv(prompt - 1, seed=1234 + dist.rank)
+        eng.decode_batch_device(B, prompts_dev.data_ptr() + (prompt - 1) * B * 4, prompt - 1, 1, None)
+    else:
+        for pos in range(prompt):
+            lm = 1 if pos == prompt - 1 else 0
+            eng.decode_batch_device(B, prompts_dev.data_ptr() + pos * B * 4, pos, lm, None)
     eng.sync()
     prefill_s = time.perf_counter() - t0
     pos = prompt

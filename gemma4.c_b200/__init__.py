@@ -82,6 +82,7 @@ SIGNATURES = [
     ("g4_engine_get_hidden", ip, [vp, ip, vp]),
     ("g4_engine_get_kv", ip, [vp, ip, ip, ip, vp, vp]),
     ("g4_engine_last_step_kernels", ip, [vp]),
+    ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
 ]
 
 _lib = None
@@ -273,6 +274,9 @@ class Engine:
         v = np.zeros(n, np.float32)
         _check(lib().g4_engine_get_kv(self.h, b, layer, pos, _p(k), _p(v)))
         return k, v
+
+    def fill_kv(self, npos: int, seed: int = 1):
+        _check(lib().g4_engine_fill_kv(self.h, npos, seed))
 
     def last_step_kernels(self) -> int:
         return int(lib().g4_engine_last_step_kernels(self.h))

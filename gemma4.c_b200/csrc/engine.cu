@@ -773,6 +773,19 @@ int g4_decode_batch_device(g4_engine *e, int B, const int *tokens_dev, int pos, 
     return G4_OK;
 }
 
+int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed) {
+    if (!e || npos < 0 || npos > e->max_seq) { set_error(G4_ERR_ARG, "fill_kv: bad arguments"); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    G4_CUDA(cudaSetDevice(e->device));
+    for (int l = 0; l < e->L && l < G4_N_LAYER_KV; l++) {
+        const LayerDev &ly = e->layers[l];
+        TRY(launch_fill_kv(ly.kc, e->max_batch, e->nkv, ly.ring, ly.hd, npos, seed + 2 * (uint64_t)l, e->st));
+        TRY(launch_fill_kv(ly.vc, e->max_batch, e->nkv, ly.ring, ly.hd, npos, seed + 2 * (uint64_t)l + 1, e->st));
+    }
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
 int g4_engine_get_hidden(g4_engine *e, int b, float *x) {
     if (!e || !x || b < 0 || b >= e->max_batch) { set_error(G4_ERR_ARG, "get_hidden: bad arguments"); return G4_ERR_ARG; }
     std::lock_guard<std::mutex> lk(e->mu);

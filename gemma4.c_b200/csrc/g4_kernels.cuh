@@ -97,5 +97,6 @@ int launch_repack_q6(const void *raw_dev, size_t nblk, size_t blk_offset, void *
 int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, int pd, int L, float ctx_scale,
                    float mix_scale, float eps, float *ple_out, int B, cudaStream_t st);
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
+int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st);
 
 }  // namespace g4

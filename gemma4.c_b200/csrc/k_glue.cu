@@ -322,3 +322,34 @@ int prime_kernel_attrs() {
     return prime_attn_attrs();
 }
 }  // namespace g4
+
+namespace g4 {
+
+// Seeded values in [-1, 1) for KV rows [0, npos) of one cache (a splitmix64
+// hash of the element index), so a benchmark can start decoding at a long
+// context without running the prefill; a decode step's cost does not depend
+// on the cached values.
+__global__ void fill_kv_kernel(float *c, size_t rows_per_head, int ring, int hd, int npos, size_t total, uint64_t seed) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const size_t head_row = i / hd;                 // (b, h, slot) row index
+    const int slot = (int)(head_row % ring);
+    if (slot >= npos && npos < ring) return;
+    uint64_t z = seed + 0x9E3779B97F4A7C15ull * (i + 1);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    c[i] = (float)(z >> 40) * (2.0f / 16777216.0f) - 1.0f;
+    (void)rows_per_head;
+}
+
+int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st) {
+    const size_t total = (size_t)B * n_kv * ring * hd;
+    if (!total) return G4_OK;
+    fill_kv_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(c, (size_t)ring, ring, hd, npos, total, seed);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
+}  // namespace g4

@@ -251,6 +251,12 @@ int g4_engine_sync(g4_engine *e);
 /* The engine's CUDA stream (cudaStream_t as void*) for event timing. */
 void *g4_engine_stream(g4_engine *e);
 
+/* Benchmark helper: fill the KV rows of positions [0, npos) of every KV layer
+ * and sequence with seeded values in [-1, 1), so decoding can start at a long
+ * context without a prefill (a decode step's work does not depend on the
+ * cached values).  Not part of the reference interface. */
+int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed);
+
 /* Number of kernels in the most recent step (the nodes of its CUDA graph). */
 int g4_engine_last_step_kernels(const g4_engine *e);
 
