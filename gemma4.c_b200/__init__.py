@@ -83,6 +83,7 @@ SIGNATURES = [
     ("g4_engine_get_kv", ip, [vp, ip, ip, ip, vp, vp]),
     ("g4_engine_last_step_kernels", ip, [vp]),
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
+    ("g4_set_tc_min_batch", ip, [ip]),
 ]
 
 _lib = None
@@ -209,6 +210,14 @@ def free(dev: int):
 def mm_device(o, x, w, n, d, t, q8, q8_ready, batch, stream):
     """g4d_mm on raw device pointers (ints)."""
     _check(lib().g4d_mm(o, x, w, n, d, t, q8, q8_ready, batch, stream))
+
+
+def set_tc_min_batch(b: int) -> int:
+    """Batch size from which g4d_mm runs Q4_K/Q5_K on the tensor cores; returns the previous value."""
+    r = lib().g4_set_tc_min_batch(b)
+    if r < 0:
+        _check(G4_ERR_ARG)
+    return r
 
 
 def registry_clear():

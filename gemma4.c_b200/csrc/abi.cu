@@ -550,6 +550,84 @@ int g4d_quantize_row_q8_K(const float *x, g4_block_q8_K *y, int k, int batch, vo
     return launch_quantize_q8k(x, k, y, k, batch, (cudaStream_t)stream);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- tensor-core batch path of g4d_mm
+
+static std::atomic<int> g_tc_min_batch{16};
+
+struct TcScratchDev {  // per device; calls that use it must be ordered on the GPU
+    uint8_t *bq = nullptr;
+    size_t bq_bytes = 0;
+    float *part = nullptr;
+    size_t part_bytes = 0;
+    int *tickets = nullptr;
+    int n_tickets = 0;
+    int nsm = 0;
+};
+static TcScratchDev g_tcs[64];
+static std::mutex g_tcs_mu;
+
+static int tc_scratch(int n, int d, TcScratchDev **out) {
+    int dev = 0;
+    G4_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) { set_error(G4_ERR_NO_DEVICE, "device ordinal %d out of range", dev); return G4_ERR_NO_DEVICE; }
+    std::lock_guard<std::mutex> lk(g_tcs_mu);
+    TcScratchDev &S = g_tcs[dev];
+    if (!S.nsm) G4_CUDA(cudaDeviceGetAttribute(&S.nsm, cudaDevAttrMultiProcessorCount, dev));
+    const size_t bq = tc_operand_bytes(n), part = tc_part_bytes(d, n, S.nsm);
+    const int nt = tc_tickets(d);
+    if (bq > S.bq_bytes || part > S.part_bytes || nt > S.n_tickets) {
+        G4_CUDA(cudaDeviceSynchronize());  // earlier calls may still use the old buffers
+        if (bq > S.bq_bytes) {
+            cudaFree(S.bq);
+            S.bq = nullptr; S.bq_bytes = 0;
+            G4_CUDA(cudaMalloc(&S.bq, bq));
+            S.bq_bytes = bq;
+        }
+        if (part > S.part_bytes) {
+            cudaFree(S.part);
+            S.part = nullptr; S.part_bytes = 0;
+            G4_CUDA(cudaMalloc(&S.part, part));
+            S.part_bytes = part;
+        }
+        if (nt > S.n_tickets) {
+            cudaFree(S.tickets);
+            S.tickets = nullptr; S.n_tickets = 0;
+            G4_CUDA(cudaMalloc(&S.tickets, sizeof(int) * (size_t)nt));
+            G4_CUDA(cudaMemset(S.tickets, 0, sizeof(int) * (size_t)nt));
+            S.n_tickets = nt;
+        }
+    }
+    *out = &S;
+    return G4_OK;
+}
+
+// Q4_K/Q5_K rows against `batch` Q8_K activations (already in q8) on the
+// tensor cores, in groups of up to 64 sequences.
+static int mm_tc(float *o, const void *w, int n, int d, int type, const g4_block_q8_K *q8, int batch, cudaStream_t st) {
+    TcScratchDev *S = nullptr;
+    G4_TRY(tc_scratch(n, d, &S));
+    CUtensorMap tm;
+    G4_TRY(tc_weight_map(&tm, w, type, n, d));
+    const int nb = n / G4_QK;
+    float *yd = (float *)(S->bq + (size_t)nb * 320 * 64);
+    for (int g0 = 0; g0 < batch; g0 += 64) {
+        const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
+        G4_TRY(launch_tc_from_q8((const uint8_t *)q8 + (size_t)g0 * nb * G4_Q8_BYTES, gb, n, np, S->bq, yd, st));
+        G4_TRY(launch_gemm_tc(&tm, type, n, d, S->bq, yd, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
+                              S->tickets, nullptr, S->nsm, st));
+    }
+    return G4_OK;
+}
+
+extern "C" {
+
+int g4_set_tc_min_batch(int b) {
+    if (b < 1) { set_error(G4_ERR_ARG, "tc min batch %d", b); return -1; }
+    return g_tc_min_batch.exchange(b);
+}
+
 int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_block_q8_K *q8, int q8_ready,
            int batch, void *stream) {
     G4_TRY(check_mm_args(o, w, n, d, type));
@@ -564,6 +642,7 @@ int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_b
     }
     if (type == G4_F32 || type == G4_F16 || type == G4_BF16)
         return launch_gemv_dense(w, type, n, d, x, n, o, d, batch, EPI_STORE, nullptr, 0, st);
+    if (is_q8_type(type) && batch >= g_tc_min_batch.load()) return mm_tc(o, w, n, d, type, q8, batch, st);
     GemvJobs jobs{};
     jobs.njobs = 1;
     GemvJob &J = jobs.j[0];

@@ -1,5 +1,7 @@
 // g4_kernels.cuh — launchers of the sm_100a kernels (internal to libg4b200).
 #pragma once
+#include <cuda.h>  // CUtensorMap
+
 #include "g4_internal.cuh"
 #include "g4_prologue.cuh"
 
@@ -98,5 +100,21 @@ int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, in
                    float mix_scale, float eps, float *ple_out, int B, cudaStream_t st);
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
 int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st);
+
+// ---- batched K-quant GEMM on tcgen05 (k_gemm_tc.cu), 16..64 sequences
+struct TcPlan {
+    int ksplit, kslice, units, grid;  // K-slices per 128-row tile, blocks per slice, work units, CTAs
+};
+int tc_np(int B);                    // padded sequence count: 16, 32 or 64
+size_t tc_operand_bytes(int n);      // B operand + block scales of one activation (NP = 64)
+TcPlan tc_plan(int rows, int nb, int nsm);
+size_t tc_part_bytes(int rows, int n, int nsm);
+int tc_tickets(int rows);
+int tc_weight_map(CUtensorMap *m, const void *w, int type, int n, int rows);
+int launch_tc_quant(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
+int launch_tc_from_q8(const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
+int launch_gemm_tc(const CUtensorMap *tm, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
+                   float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                   cudaStream_t st);
 
 }  // namespace g4

@@ -26,6 +26,7 @@
 // CTA returns instead of hanging the GPU.
 #include <math.h>
 
+#include "g4_async.cuh"
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
 
@@ -35,56 +36,12 @@ constexpr int kTmConsumerWarps = 16;
 constexpr int kTmGroups = kTmConsumerWarps * 4;       // consumer lane groups
 constexpr int kTmThreads = (kTmConsumerWarps + 1) * 32;  // + producer warp
 constexpr int kTmMaxStages = 6;
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ float tm_gelu(float x) {  // gelu_f32, main.c:1490-1492
     return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
 }
 __device__ __forceinline__ float tm_q6(uint32_t w, int i) {  // byte i (0..63) -> q - 32, exact
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + i)) - 8388640.0f;
-}
-
-// ---------------------------------------------------------------- mbarrier / bulk copy
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    uint64_t st;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
-                 : "=l"(st) : "r"(smem_u32(bar)), "r"(bytes) : "memory");
-    (void)st;
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    uint64_t st;
-    asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(st) : "r"(smem_u32(bar)) : "memory");
-    (void)st;
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Wait for phase `parity` of `bar`; false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        for (int i = 0; i < 64; i++)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) return false;
-    }
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
 // ---------------------------------------------------------------- activation

@@ -1,0 +1,93 @@
+"""Batched Q4_K/Q5_K x Q8_K GEMM on the tensor cores (tcgen05, k_gemm_tc.cu)
+through the C ABI (g4d_mm with batch >= the tensor-core threshold), against
+the oracle per sequence and against the streaming GEMV on the same inputs.
+
+The reference computes one activation at a time (mm_quant_dot_rows,
+gemma4-4b/cpu-blas/main.c:1558-1566); a batch of B activations must give, for
+every sequence, the same result as B separate calls within the K-quant
+tolerance (integer block sums exact, float sum order free).
+"""
+import numpy as np
+import pytest
+
+from _tol import assert_close, kquant_term_scale
+
+pytestmark = pytest.mark.gpu
+
+Q4, Q5 = 12, 13
+
+
+def _run(g4, torch, w, x, t, n, rows, tc_min):
+    B = x.shape[0]
+    dev = torch.device("cuda:0")
+    wd = g4.weight_upload(w, t, n, rows)
+    try:
+        xd = torch.from_numpy(x).to(dev)
+        q8 = torch.zeros(B * (n // 256) * 292, dtype=torch.uint8, device=dev)
+        o = torch.full((B, rows), float("nan"), dtype=torch.float32, device=dev)
+        prev = g4.set_tc_min_batch(tc_min)
+        try:
+            g4.mm_device(o.data_ptr(), xd.data_ptr(), wd, n, rows, t, q8.data_ptr(), 0, B,
+                         torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+        finally:
+            g4.set_tc_min_batch(prev)
+        return o.cpu().numpy(), q8.cpu().numpy().reshape(B, -1)
+    finally:
+        g4.free(wd)
+
+
+@pytest.fixture
+def torch_cuda(gpu):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("torch sees no CUDA device")
+    return torch
+
+
+@pytest.mark.parametrize("t,rows,n,B", [
+    (Q4, 300, 2560, 16),     # one ragged row tile, NP = 16
+    (Q4, 2048, 2560, 20),    # NP = 32 with padding sequences
+    (Q4, 2560, 2048, 64),    # O-projection shape, NP = 64
+    (Q4, 10240, 2560, 64),   # gate/up shape
+    (Q4, 2560, 10240, 33),   # long K: many K-slices per tile
+    (Q5, 1000, 4096, 40),
+    (Q4, 512, 2560, 70),     # two groups (64 + 6)
+])
+def test_tc_gemm_vs_oracle(gpu, torch_cuda, orc, g4, t, rows, n, B):
+    rng = np.random.default_rng(1000 * t + rows + n + B)
+    w = g4.synth.rand_blocks(rng, t, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    x[1] *= 50.0  # per-sequence scales differ
+    o, q8 = _run(g4, torch_cuda, w, x, t, n, rows, tc_min=1)
+    assert np.isfinite(o).all()
+    for s in range(B):
+        q8s = orc.quantize_q8K(x[s])
+        assert (q8[s] == q8s.reshape(-1)).all(), "Q8_K bytes of sequence %d" % s
+        e = orc.mm(x[s], w, n, rows, t)
+        ss, sm = g4.block_sums(w, n, rows, t, q8s)  # exact; pinned against the oracle elsewhere
+        assert_close(o[s], e, kquant_term_scale(w, t, n, q8s, ss, sm), what="TC Q%dK seq %d" % (t - 8, s))
+
+
+@pytest.mark.parametrize("t", [Q4, Q5])
+def test_tc_gemm_vs_gemv(gpu, torch_cuda, g4, t):
+    """Same inputs through the tensor-core GEMM and the streaming GEMV."""
+    rows, n, B = 640, 2560, 24
+    rng = np.random.default_rng(77 + t)
+    w = g4.synth.rand_blocks(rng, t, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    o_tc, _ = _run(g4, torch_cuda, w, x, t, n, rows, tc_min=1)
+    o_sv, _ = _run(g4, torch_cuda, w, x, t, n, rows, tc_min=1 << 30)
+    for s in range(B):
+        assert_close(o_tc[s], o_sv[s], what="TC vs GEMV seq %d" % s)
+
+
+def test_tc_gemm_repeat_deterministic(gpu, torch_cuda, g4):
+    """K-slice partials are summed in a fixed order: repeated calls agree bitwise."""
+    rows, n, B = 2560, 10240, 64
+    rng = np.random.default_rng(5)
+    w = g4.synth.rand_blocks(rng, Q4, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    a, _ = _run(g4, torch_cuda, w, x, Q4, n, rows, tc_min=1)
+    b, _ = _run(g4, torch_cuda, w, x, Q4, n, rows, tc_min=1)
+    assert (a == b).all()
