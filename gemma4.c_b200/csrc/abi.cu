@@ -10,6 +10,7 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <map>
 #include <mutex>
@@ -575,7 +576,7 @@ static int tc_scratch(int n, int d, TcScratchDev **out) {
     std::lock_guard<std::mutex> lk(g_tcs_mu);
     TcScratchDev &S = g_tcs[dev];
     if (!S.nsm) G4_CUDA(cudaDeviceGetAttribute(&S.nsm, cudaDevAttrMultiProcessorCount, dev));
-    const size_t bq = tc_operand_bytes(n), part = tc_part_bytes(d, n, S.nsm);
+    const size_t bq = std::max(tc_operand_bytes(n), tc6_operand_bytes(n)), part = tc_part_bytes(d, n, S.nsm);
     const int nt = tc_tickets(d);
     if (bq > S.bq_bytes || part > S.part_bytes || nt > S.n_tickets) {
         G4_CUDA(cudaDeviceSynchronize());  // earlier calls may still use the old buffers
@@ -611,12 +612,29 @@ static int mm_tc(float *o, const void *w, int n, int d, int type, const g4_block
     CUtensorMap tm;
     G4_TRY(tc_weight_map(&tm, w, type, n, d));
     const int nb = n / G4_QK;
-    float *yd = (float *)(S->bq + (size_t)nb * 320 * 64);
+    float *yd = (float *)(S->bq + tc_yd_offset(n));
     for (int g0 = 0; g0 < batch; g0 += 64) {
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
-        G4_TRY(launch_tc_from_q8((const uint8_t *)q8 + (size_t)g0 * nb * G4_Q8_BYTES, gb, n, np, S->bq, yd, st));
-        G4_TRY(launch_gemm_tc(&tm, type, n, d, S->bq, yd, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
+        G4_TRY(launch_tc_from_q8(type, (const uint8_t *)q8 + (size_t)g0 * nb * G4_Q8_BYTES, gb, n, np, S->bq, yd, st));
+        G4_TRY(launch_gemm_tc(&tm, w, type, n, d, S->bq, yd, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
                               S->tickets, nullptr, S->nsm, st));
+    }
+    return G4_OK;
+}
+
+// Q6_K rows against `batch` fp32 activations on the tensor cores.
+static int mm_tc6(float *o, const float *x, const void *w, int n, int d, int batch, cudaStream_t st) {
+    TcScratchDev *S = nullptr;
+    G4_TRY(tc_scratch(n, d, &S));
+    alignas(64) unsigned char maps[512];
+    if (tc6_maps_bytes() > sizeof(maps)) { set_error(G4_ERR_STATE, "tensor-map bundle size"); return G4_ERR_STATE; }
+    G4_TRY(tc6_weight_maps(maps, w, n, d));
+    float *ys = (float *)(S->bq + tc6_ys_offset(n));
+    for (int g0 = 0; g0 < batch; g0 += 64) {
+        const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
+        G4_TRY(launch_tc6_split(x + (size_t)g0 * n, n, gb, n, np, S->bq, ys, st));
+        G4_TRY(launch_gemm_q6tc(maps, w, n, d, S->bq, ys, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
+                                S->tickets, nullptr, S->nsm, EPI_STORE, 0.0f, nullptr, st));
     }
     return G4_OK;
 }
@@ -643,6 +661,7 @@ int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_b
     if (type == G4_F32 || type == G4_F16 || type == G4_BF16)
         return launch_gemv_dense(w, type, n, d, x, n, o, d, batch, EPI_STORE, nullptr, 0, st);
     if (is_q8_type(type) && batch >= g_tc_min_batch.load()) return mm_tc(o, w, n, d, type, q8, batch, st);
+    if (type == G4_Q6_K && batch >= g_tc_min_batch.load()) return mm_tc6(o, x, w, n, d, batch, st);
     GemvJobs jobs{};
     jobs.njobs = 1;
     GemvJob &J = jobs.j[0];

@@ -101,19 +101,30 @@ int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, in
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
 int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st);
 
+// ---- batched Q6_K GEMM on tcgen05 (k_gemm_q6tc.cu), 16..64 sequences
+size_t tc6_operand_bytes(int n);     // x1/x2 operand + scales of one activation (NP = 64)
+size_t tc6_ys_offset(int n);
+size_t tc6_maps_bytes();             // bytes of the opaque tensor-map bundle
+int tc6_weight_maps(void *maps_out, const void *w, int n, int rows);
+int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *ys, cudaStream_t st);
+int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
+                     int np, float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                     int epi, float cap, unsigned long long *keys, cudaStream_t st);
+
 // ---- batched K-quant GEMM on tcgen05 (k_gemm_tc.cu), 16..64 sequences
 struct TcPlan {
     int ksplit, kslice, units, grid;  // K-slices per 128-row tile, blocks per slice, work units, CTAs
 };
 int tc_np(int B);                    // padded sequence count: 16, 32 or 64
 size_t tc_operand_bytes(int n);      // B operand + block scales of one activation (NP = 64)
+size_t tc_yd_offset(int n);          // where the block scales start inside that buffer
 TcPlan tc_plan(int rows, int nb, int nsm);
 size_t tc_part_bytes(int rows, int n, int nsm);
 int tc_tickets(int rows);
 int tc_weight_map(CUtensorMap *m, const void *w, int type, int n, int rows);
-int launch_tc_quant(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
-int launch_tc_from_q8(const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
-int launch_gemm_tc(const CUtensorMap *tm, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
+int launch_tc_quant(int type, const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
+int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
+int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
                    float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
                    cudaStream_t st);
 

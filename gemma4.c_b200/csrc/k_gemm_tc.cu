@@ -43,6 +43,7 @@
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
 #include "g4_quant.cuh"
+#include "g4_tc.cuh"
 
 namespace g4 {
 
@@ -93,23 +94,12 @@ __device__ __forceinline__ bool tc_wait(TcState &S, uint64_t *bar, uint32_t pari
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     for (;;) {
-        for (int i = 0; i < 32; i++)
-            if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
         if (S.abort) return false;
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
 }
 
-struct TcArgs {
-    const uint8_t *bq;  // [nb][320*NP]: q8 quants (core-matrix layout) then the bsum operand
-    const float *yd;    // [nb][NP] Q8_K block scales (0 for padding sequences)
-    float *out;         // [B][ldo]
-    float *part;        // [ksplit][NP][rows] slice partials (ksplit > 1)
-    int *tickets;       // [row_tiles][8], zero between launches
-    int *err;
-    int nb, rows, B, ldo;
-    int ksplit, kslice, units;
-};
 
 template <int TYPE, int NP>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmw, TcArgs a) {
@@ -465,6 +455,444 @@ __global__ void tc_from_q8_kernel(const uint8_t *__restrict__ q8, int nb, int B,
     tc_store_q8(bq + (size_t)k * 320 * NP, yd + (size_t)k * NP, NP, s, lane, q, d, ls);
 }
 
+// ---------------------------------------------------------------- Q4_K: fp16 MMA, A operand in TMEM
+//
+// The same products for Q4_K with kind::f16 operands that hold exact small
+// integers: A = sc_j * q (<= 63*15 = 945) and mins mn_j, B = q8 and the
+// 16-element sums bsums[k] of Q8_K (|.| <= 2048).  Every product is exact in
+// fp32 and every partial sum is an integer below 2^24 in magnitude as long
+// as it spans at most 128 weights (945*128*128 < 2^24), so the fp32
+// accumulators hold the exact integers: S0 (weights 0..127), S1 (128..255)
+// and M.  S0 + S1 rounds once, exactly like (float)sumi in the reference.
+// The expanded weights go straight from registers into TMEM (tcgen05.st) and
+// the MMA reads A from there, so shared memory only carries the raw weight
+// tile and the B operand.
+//
+// K order inside each group of 4 weights is (0, 2, 1, 3): two nibbles of
+// one 16-bit lane pair become one 32-bit TMEM column with one mask.  The B
+// operand is written in the same order, so the dot product is unchanged.
+
+constexpr int kQ4Threads = 576;  // warp 0 producer, warp 1 MMA, warps 2..17 expand + epilogue
+constexpr int kQ4RawStages = 5;
+
+template <int NP>
+struct Q4Smem {
+    static constexpr int raw = 128 * 144;
+    static constexpr int bst = 544 * NP;  // 256*NP fp16 quants + 16*NP fp16 bsums
+    static constexpr int bstages = NP == 64 ? 3 : 4;
+    static constexpr int b_off = kQ4RawStages * raw;
+    static constexpr int total = b_off + bstages * bst + 1024;
+};
+// TMEM columns: [D_s0 | D_s1] for two blocks in flight, D_m, the four
+// 64-weight quarters of A (32 columns each), the mins of two blocks (8 each).
+template <int NP>
+struct Q4Tmem {
+    static constexpr uint32_t dm = 4 * NP, a = 5 * NP, mins = 5 * NP + 128;
+    static_assert(mins + 16 <= 512, "TMEM columns");
+};
+
+struct Q4State {
+    uint64_t raw_full[kQ4RawStages], raw_empty[kQ4RawStages], b_full[4], b_empty[4];
+    uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], dm_empty, mma_done;
+    uint32_t tmem_base;
+    volatile int abort;
+    float yd[8][2][32];  // per epilogue warp: block scales of its sequences, by block parity
+};
+
+// Waiting warps sleep in the barrier (1 ms suspend hint) instead of
+// spinning, so they leave the issue slots of their SMSP to working warps.
+__device__ __forceinline__ bool q4_wait(Q4State &S, uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (S.abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+__device__ __forceinline__ void q4_fail(Q4State &S, int *err) {
+    S.abort = 1;
+    if (err) atomicExch(err, G4_ERR_TIMEOUT);
+}
+// Warp roles.  Warps 2..17 work on TMEM lane quadrant (warp & 3), i.e. 32
+// weight rows each (a warp may only touch its own quadrant):
+//   warps 2..9   expand: warp-group e = (warp-2)/4 expands the quarters 2e
+//                and 2e+1 (weights 128e .. 128e+127) of every super-block;
+//   warps 10..17 epilogue: group p = (warp-10)/4 owns sequences
+//                [p*NP/2, (p+1)*NP/2) and runs the per-block float epilogue.
+// Expansion of block i+1 and the epilogue of block i then run concurrently
+// on every SMSP.
+template <int NP>
+__global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_constant__ CUtensorMap tmw, TcArgs a) {
+    constexpr int RAW = Q4Smem<NP>::raw, BST = Q4Smem<NP>::bst, BS = Q4Smem<NP>::bstages, RS = kQ4RawStages;
+    constexpr int SP = NP / 2;  // sequences per epilogue warp
+    using TM = Q4Tmem<NP>;
+    extern __shared__ uint8_t smem_dyn[];
+    __shared__ Q4State S;
+    uint8_t *smem = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
+    uint8_t *raw = smem, *bst = smem + Q4Smem<NP>::b_off;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    if (tid == 0) {
+        for (int i = 0; i < RS; i++) {
+            mbar_init(&S.raw_full[i], 1);
+            mbar_init(&S.raw_empty[i], 8);  // expand warps
+        }
+        for (int i = 0; i < BS; i++) {
+            mbar_init(&S.b_full[i], 1);
+            mbar_init(&S.b_empty[i], 1);
+        }
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&S.a_full[i], 4);  // the four lane quadrants of quarter i
+            mbar_init(&S.a_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&S.acc_full[i], 1);
+            mbar_init(&S.acc_empty[i], 8);  // epilogue warps
+        }
+        mbar_init(&S.dm_empty, 8);
+        mbar_init(&S.mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.abort = 0;
+    }
+    if (warp == 1) tc_alloc(&S.tmem_base, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = S.tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int i = 0, nb_issued = 0;
+            bool ok = true, dep = false;
+            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const int rt = u / a.ksplit, b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
+                for (int b = b0; b < b1; b++, i++) {
+                    const int rs = i % RS;
+                    if (!q4_wait(S, &S.raw_empty[rs], ((i / RS) & 1) ^ 1)) { ok = false; break; }
+                    mbar_expect_tx(&S.raw_full[rs], RAW);
+                    tma_load_2d(raw + rs * RAW, &tmw, b * 144, rt * 128, &S.raw_full[rs]);
+                    if (!dep) { pdl_wait(); dep = true; }
+                    const int bs = i % BS;
+                    if (!q4_wait(S, &S.b_empty[bs], ((i / BS) & 1) ^ 1)) { ok = false; i++; break; }
+                    mbar_expect_tx(&S.b_full[bs], BST);
+                    bulk_g2s(bst + bs * BST, a.bq + (size_t)b * BST, BST, &S.b_full[bs]);
+                    nb_issued = i + 1;
+                }
+            }
+            if (!dep) pdl_wait();
+            if (!ok) {
+                q4_fail(S, a.err);
+                for (int k = max(0, i - RS); k < i; k++) {
+                    const unsigned long long t0 = global_ns();
+                    while (!mbar_try_wait(&S.raw_full[k % RS], (k / RS) & 1) && global_ns() - t0 < kWaitLimitNs) {}
+                }
+                for (int k = max(0, nb_issued - BS); k < nb_issued; k++) {
+                    const unsigned long long t0 = global_ns();
+                    while (!mbar_try_wait(&S.b_full[k % BS], (k / BS) & 1) && global_ns() - t0 < kWaitLimitNs) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc(1, 0, 0, NP);  // f32 += f16 * f16
+            int i = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
+                for (int b = b0; b < b1 && ok; b++, i++) {
+                    const int abuf = i & 1, bs = i % BS;
+                    // Test every barrier this block needs at once (the tests overlap; a test whose
+                    // result is used immediately costs a barrier round trip), then fence once.
+                    {
+                        const uint32_t pa = i & 1;
+                        const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
+                        const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
+                        const bool r2 = mbar_try_wait(&S.a_full[0], pa), r3 = mbar_try_wait(&S.a_full[2], pa);
+                        const bool r4 = mbar_try_wait(&S.a_full[1], pa), r5 = mbar_try_wait(&S.a_full[3], pa);
+                        if (!(r0 && r1 && r2 && r3 && r4 && r5)) {
+                            if (!q4_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) || !q4_wait(S, &S.b_full[bs], (i / BS) & 1) ||
+                                !q4_wait(S, &S.a_full[0], pa) || !q4_wait(S, &S.a_full[2], pa) ||
+                                !q4_wait(S, &S.a_full[1], pa) || !q4_wait(S, &S.a_full[3], pa)) { ok = false; break; }
+                        }
+                    }
+                    tc_fence_after();
+                    const uint32_t bsa = smem_u32(bst + bs * BST);
+                    const uint32_t d0 = tbase + abuf * 2 * NP;
+                    for (int qi = 0; qi < 4; qi++) {
+                        // the two expand warp groups finish quarters 0 and 2 first, then 1 and 3
+                        const int q = ((qi & 1) << 1) | (qi >> 1);
+                        const uint32_t acol = tbase + TM::a + 32 * q;
+                        const uint32_t dq = d0 + (q >> 1) * NP;  // S0: weights 0..127, S1: 128..255
+#pragma unroll
+                        for (int ks = 0; ks < 4; ks++)
+                            tc_mma_f16_ts(dq, acol + 8 * ks, umma_desc(bsa + (8 * q + 2 * ks) * NP * 16, NP * 16, 128),
+                                          idesc, (ks | (q & 1)) != 0);
+                        tc_commit(&S.a_empty[q]);
+                    }
+                    if (!ok) break;
+                    // mins x bsums (K = 16) into the single D_m, once the epilogue of block i-1 has read it.
+                    // The mins of block i sit in slot i&1; the expand warps rewrite that slot for block
+                    // i+2 only after quarter 0 of block i+1 was consumed, i.e. after this MMA completed.
+                    if (i > 0 && !q4_wait(S, &S.dm_empty, (i - 1) & 1)) { ok = false; break; }
+                    tc_fence_after();
+                    tc_mma_f16_ts(tbase + TM::dm, tbase + TM::mins + 8 * (i & 1), umma_desc(bsa + 512 * NP, NP * 16, 128),
+                                  idesc, 0);
+                    tc_commit(&S.b_empty[bs]);
+                    tc_commit(&S.acc_full[abuf]);
+                }
+            }
+            if (!ok) q4_fail(S, a.err);
+            tc_commit(&S.mma_done);
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(&S.mma_done, 0) && global_ns() - t0 < kWaitLimitNs) {}
+        }
+        __syncwarp();
+    } else if (warp < 10) {
+        // ------------------------------------------------------------ expand warps
+        const int quad = warp & 3, e = (warp - 2) >> 2, r = 32 * quad + lane;
+        const uint32_t tl = tbase + ((uint32_t)(32 * quad) << 16);
+        const uint32_t raw_s = smem_u32(raw);
+        int i = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+            const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
+            for (int b = b0; b < b1; b++, i++) {
+                const int rs = i % RS;
+                if (!q4_wait(S, &S.raw_full[rs], (i / RS) & 1)) { ok = false; break; }
+                const uint32_t rw = raw_s + rs * RAW + r * 144;
+                const uint4 meta = lds128(rw);
+                const uint4 qa = lds128(rw + 16 + 64 * e), qb = lds128(rw + 32 + 64 * e);
+                const uint4 qc = lds128(rw + 48 + 64 * e), qd = lds128(rw + 64 + 64 * e);
+                const uint32_t sc03 = meta.y & 0x3f3f3f3fu;
+                const uint32_t sc47 = (meta.w & 0x0f0f0f0fu) | ((meta.y >> 2) & 0x30303030u);
+                uint32_t mc[8];
+                if (e == 0) {  // mins of sub-blocks 0..7, each twice (against the bsums of 16)
+                    const uint32_t mn03 = meta.z & 0x3f3f3f3fu;
+                    const uint32_t mn47 = ((meta.w >> 4) & 0x0f0f0f0fu) | ((meta.z >> 2) & 0x30303030u);
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const uint32_t m = __byte_perm(mn03, mn47, 0x4440 | c) & 0xffu;
+                        mc[c] = hadd2_u(m | (m << 16) | 0x64006400u, 0xE400E400u);  // (1024+m) - 1024
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.raw_empty[rs]);  // everything needed is in registers
+#pragma unroll
+                for (int qq = 0; qq < 2; qq++) {
+                    const int q = 2 * e + qq;  // quarter: 64-weight group q, sub-blocks 2q (low nibbles), 2q+1 (high)
+                    const uint32_t qw[8] = {qq ? qc.x : qa.x, qq ? qc.y : qa.y, qq ? qc.z : qa.z, qq ? qc.w : qa.w,
+                                            qq ? qd.x : qb.x, qq ? qd.y : qb.y, qq ? qd.z : qb.z, qq ? qd.w : qb.w};
+                    if (!q4_wait(S, &S.a_empty[q], (i & 1) ^ 1)) { ok = false; break; }
+                    // low nibble q at bits 0..3 of a 16-bit lane: fp16 bits 0x6400|q = 1024+q, and
+                    //   fma(1024+q, sc, -1024*sc) = sc*q exactly (fused, |sc*q| <= 945);
+                    // high nibble at bits 4..7: 0x6400|16q = 1024+16q, fma(1024+16q, sc/16, -64*sc) = sc*q.
+                    const int scl = (int)(__byte_perm(sc03, sc47, 0x4440 | (2 * q)) & 0xffu);
+                    const int sch = (int)(__byte_perm(sc03, sc47, 0x4440 | (2 * q + 1)) & 0xffu);
+                    uint32_t hl = h_of_int(scl), hlc = h_of_int(-1024 * scl);
+                    uint32_t hh = (uint32_t)__half_as_ushort(__float2half_rn((float)sch * 0.0625f)), hhc = h_of_int(-64 * sch);
+                    const uint32_t sl2 = hl | (hl << 16), cl2 = hlc | (hlc << 16);
+                    const uint32_t sh2 = hh | (hh << 16), ch2 = hhc | (hhc << 16);
+                    uint32_t col[16], coh[16];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        const uint32_t x = qw[k], y = __byte_perm(x, 0u, 0x4341);  // bytes 1, 3 -> lanes 0, 1
+                        col[2 * k] = hfma2_u((x & 0x000F000Fu) | 0x64006400u, sl2, cl2);
+                        col[2 * k + 1] = hfma2_u((y & 0x000F000Fu) | 0x64006400u, sl2, cl2);
+                        coh[2 * k] = hfma2_u((x & 0x00F000F0u) | 0x64006400u, sh2, ch2);
+                        coh[2 * k + 1] = hfma2_u((y & 0x00F000F0u) | 0x64006400u, sh2, ch2);
+                    }
+                    tc_st16(tl + TM::a + 32 * q, col);
+                    tc_st16(tl + TM::a + 32 * q + 16, coh);
+                    if (q == 0) tc_st8(tl + TM::mins + 8 * (i & 1), mc);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.a_full[q]);
+                }
+                if (!ok) break;
+            }
+        }
+        if (!ok) q4_fail(S, a.err);
+    } else {
+        // ------------------------------------------------------------ epilogue warps
+        const int quad = warp & 3, p = (warp - 10) >> 2, pw = warp - 10, r = 32 * quad + lane;
+        const uint32_t tl = tbase + ((uint32_t)(32 * quad) << 16);
+        pdl_wait();
+        unsigned long long acc[SP / 2];
+#pragma unroll
+        for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
+        int i = 0;
+        bool ok = true;
+        // scales of the next block: d, dmin of row r (weights, just streamed through L2) and the
+        // Q8_K d of sequence p*SP + lane, loaded one block ahead
+        auto fetch = [&](int u, int b, float &dw, float &dm, float &yl) {
+            const int row = (u / a.ksplit) * 128 + r;
+            uint32_t m = 0;
+            if (row < a.rows) m = __ldg(reinterpret_cast<const uint32_t *>(a.w + (size_t)row * a.row_bytes + (size_t)b * 144));
+            dw = f16_to_f32((uint16_t)(m & 0xffffu));
+            dm = f16_to_f32((uint16_t)(m >> 16));
+            yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
+        };
+        auto finish = [&](int u) {
+            const int rt = u / a.ksplit, ks = u % a.ksplit, row = rt * 128 + r;
+            float *dst = a.ksplit == 1 ? a.out : a.part + (size_t)ks * NP * a.rows;
+            const size_t ld = a.ksplit == 1 ? (size_t)a.ldo : (size_t)a.rows;
+            if (row < a.rows)
+#pragma unroll
+                for (int s = 0; s < SP / 2; s++) {
+                    const float2 f = f2_unpack(acc[s]);
+                    const int seq = p * SP + 2 * s;
+                    if (seq < a.B) dst[(size_t)seq * ld + row] = f.x;
+                    if (seq + 1 < a.B) dst[(size_t)(seq + 1) * ld + row] = f.y;
+                }
+#pragma unroll
+            for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
+            if (a.ksplit == 1) return;
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&a.tickets[rt * 8 + pw], 1) == a.ksplit - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) return;
+            // the last slice to finish sums all slices of this tile, in slice order
+            __threadfence();
+            if (row < a.rows) {
+                for (int k = 0; k < a.ksplit; k++)
+#pragma unroll
+                    for (int s = 0; s < SP / 2; s++) {
+                        const int seq = p * SP + 2 * s;
+                        const float *src = a.part + ((size_t)k * NP + seq) * a.rows + row;
+                        const float l0 = seq < a.B ? __ldcg(src) : 0.0f;
+                        const float l1 = seq + 1 < a.B ? __ldcg(src + a.rows) : 0.0f;
+                        acc[s] = f2_add(acc[s], f2_pack(l0, l1));
+                    }
+#pragma unroll
+                for (int s = 0; s < SP / 2; s++) {
+                    const float2 f = f2_unpack(acc[s]);
+                    const int seq = p * SP + 2 * s;
+                    if (seq < a.B) a.out[(size_t)seq * a.ldo + row] = f.x;
+                    if (seq + 1 < a.B) a.out[(size_t)(seq + 1) * a.ldo + row] = f.y;
+                    acc[s] = 0ull;
+                }
+            }
+            if (lane == 0) a.tickets[rt * 8 + pw] = 0;
+        };
+        // first block
+        int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
+        float ndw = 0.f, ndm = 0.f, nyl = 0.f;
+        if (u < a.units) fetch(u, b, ndw, ndm, nyl);
+        while (u < a.units && ok) {
+            const int b1 = min(a.nb, (u % a.ksplit) * a.kslice + a.kslice);
+            const float dw = ndw, dm = ndm;
+            if (lane < SP) S.yd[pw][i & 1][lane] = nyl;
+            __syncwarp();
+            // advance to the next block and prefetch its scales
+            int nu = u, nbk = b + 1;
+            if (nbk >= b1) { nu = u + gridDim.x; nbk = nu < a.units ? (nu % a.ksplit) * a.kslice : 0; }
+            if (nu < a.units) fetch(nu, nbk, ndw, ndm, nyl);
+            // ---- epilogue of block i
+            if (!q4_wait(S, &S.acc_full[i & 1], (i >> 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            const float *yv = S.yd[pw][i & 1];
+            const unsigned long long dw2 = f2_pack(dw, dw), ndm2 = f2_pack(-dm, -dm);
+#pragma unroll
+            for (int c = 0; c < SP / 8; c++) {
+                uint32_t v0[8], v1[8], vm[8];
+                tc_ld8(tl + (i & 1) * 2 * NP + p * SP + 8 * c, v0);
+                tc_ld8(tl + (i & 1) * 2 * NP + NP + p * SP + 8 * c, v1);
+                tc_ld8(tl + TM::dm + p * SP + 8 * c, vm);
+                tc_wait_ld();
+                if (c == SP / 8 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&S.acc_empty[i & 1]);
+                        mbar_arrive(&S.dm_empty);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    // t = dw*(S0 + S1) - dm*M; acc += yd*t, two sequences per instruction
+                    const unsigned long long sf = f2_add(f2_pack_u(v0[2 * k], v0[2 * k + 1]), f2_pack_u(v1[2 * k], v1[2 * k + 1]));
+                    const unsigned long long mt = f2_mul(ndm2, f2_pack_u(vm[2 * k], vm[2 * k + 1]));
+                    const unsigned long long t = f2_fma(dw2, sf, mt);
+                    const float2 y = *reinterpret_cast<const float2 *>(yv + 8 * c + 2 * k);
+                    acc[4 * c + k] = f2_fma(f2_pack(y.x, y.y), t, acc[4 * c + k]);
+                }
+            }
+            if (nu != u) finish(u);
+            u = nu; b = nbk; i++;
+        }
+        if (!ok) q4_fail(S, a.err);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tc_dealloc(tbase, 512);
+    }
+}
+
+// B operand of gemm_q4tc for super-block k: q8 as fp16, K-major core
+// matrices (byte (k'/8)*(NP*16) + s*16 + (k'%8)*2, k' = weight index with
+// positions 1 and 2 of every 4 swapped), then bsums[16] as fp16 (byte
+// 512*NP + (t/8)*(NP*16) + s*16 + (t%8)*2).
+__device__ __forceinline__ void tc4_store_q8(uint8_t *blk, float *ydk, int NP, int s, int lane, const uint32_t q[2],
+                                             float d, int ls) {
+    int v[8];
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        v[b] = (int)(int8_t)(q[0] >> (8 * b));
+        v[4 + b] = (int)(int8_t)(q[1] >> (8 * b));
+    }
+    const uint4 o = make_uint4(h_of_int(v[0]) | (h_of_int(v[2]) << 16), h_of_int(v[1]) | (h_of_int(v[3]) << 16),
+                               h_of_int(v[4]) | (h_of_int(v[6]) << 16), h_of_int(v[5]) | (h_of_int(v[7]) << 16));
+    *reinterpret_cast<uint4 *>(blk + (size_t)lane * (NP * 16) + s * 16) = o;
+    const int b16 = ls + __shfl_xor_sync(0xffffffffu, ls, 1);  // lanes 2t, 2t+1: elements 16t..16t+15
+    if ((lane & 1) == 0) {
+        const int t = lane >> 1;
+        *reinterpret_cast<uint16_t *>(blk + 512 * NP + (t >> 3) * (NP * 16) + s * 16 + (t & 7) * 2) =
+            (uint16_t)h_of_int(b16);
+    }
+    if (lane == 0) ydk[s] = d;
+}
+
+__global__ void tc4_quant_kernel(const float *__restrict__ x, int ldx, int B, int NP, uint8_t *__restrict__ bq,
+                                 float *__restrict__ yd) {
+    pdl_trigger();
+    pdl_wait();
+    const int k = blockIdx.x, lane = threadIdx.x & 31, s = blockIdx.y * 8 + (threadIdx.x >> 5);
+    uint32_t q[2] = {0u, 0u};
+    float d = 0.0f;
+    int ls = 0;
+    if (s < B) warp_quant_block(x + (size_t)s * ldx + (size_t)k * G4_QK, lane, q, d, ls);
+    tc4_store_q8(bq + (size_t)k * 544 * NP, yd + (size_t)k * NP, NP, s, lane, q, d, ls);
+}
+
+__global__ void tc4_from_q8_kernel(const uint8_t *__restrict__ q8, int nb, int B, int NP, uint8_t *__restrict__ bq,
+                                   float *__restrict__ yd) {
+    pdl_trigger();
+    pdl_wait();
+    const int k = blockIdx.x, lane = threadIdx.x & 31, s = blockIdx.y * 8 + (threadIdx.x >> 5);
+    uint32_t q[2] = {0u, 0u};
+    float d = 0.0f;
+    int ls = 0;
+    if (s < B) {
+        const uint8_t *blk = q8 + ((size_t)s * nb + k) * G4_Q8_BYTES;
+        d = *reinterpret_cast<const float *>(blk);
+        q[0] = *reinterpret_cast<const uint32_t *>(blk + 4 + 8 * lane);
+        q[1] = *reinterpret_cast<const uint32_t *>(blk + 8 + 8 * lane);
+        for (int b = 0; b < 4; b++) ls += (int)(int8_t)(q[0] >> (8 * b)) + (int)(int8_t)(q[1] >> (8 * b));
+    }
+    tc4_store_q8(bq + (size_t)k * 544 * NP, yd + (size_t)k * NP, NP, s, lane, q, d, ls);
+}
+
+template <int NP>
+void *q4tc_kernel_ptr() { return (void *)gemm_q4tc_kernel<NP>; }
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -491,7 +919,9 @@ void *tc_kernel_ptr() { return (void *)gemm_tc_kernel<TYPE, NP>; }
 
 int tc_np(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : 64; }
 
-size_t tc_operand_bytes(int n) { return (size_t)(n / G4_QK) * (320 * 64 + 64 * 4); }
+// per super-block: the larger (Q4_K fp16) operand layout at NP = 64, then the block scales
+size_t tc_operand_bytes(int n) { return (size_t)(n / G4_QK) * (544 * 64 + 64 * 4); }
+size_t tc_yd_offset(int n) { return (size_t)(n / G4_QK) * 544 * 64; }
 
 // Weight rows as a 2-D byte tensor [rows][row_bytes]; one box = 128 rows x
 // one super-block.
@@ -516,7 +946,8 @@ TcPlan tc_plan(int rows, int nb, int nsm) {
     for (int ks = 1; ks <= nb; ks++) {
         const int ksplit = (nb + ks - 1) / ks;
         const int units = tiles * ksplit, grid = min(units, nsm), waves = (units + grid - 1) / grid;
-        const double cost = waves * (ks + 1.0);  // + per-unit pipeline fill and partial store
+        // per unit: pipeline fill, plus fence/ticket/merge when the tile is split
+        const double cost = waves * (ks + (ksplit > 1 ? 3.0 : 1.0));
         if (cost < best_cost - 1e-9 || (fabs(cost - best_cost) < 1e-9 && ks > best.kslice)) {
             best_cost = cost;
             best = TcPlan{ksplit, ks, units, grid};
@@ -525,14 +956,18 @@ TcPlan tc_plan(int rows, int nb, int nsm) {
     return best;
 }
 
-int launch_tc_quant(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st) {
-    G4_CUDA(launch_pdl(tc_quant_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, x, ldx, B, np, bq, yd));
+int launch_tc_quant(int type, const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st) {
+    if (type == G4_Q4_K) G4_CUDA(launch_pdl(tc4_quant_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, x, ldx, B, np, bq, yd));
+    else G4_CUDA(launch_pdl(tc_quant_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, x, ldx, B, np, bq, yd));
     G4_LAUNCHED();
     return G4_OK;
 }
 
-int launch_tc_from_q8(const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st) {
-    G4_CUDA(launch_pdl(tc_from_q8_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, (const uint8_t *)q8, n / G4_QK,
+int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st) {
+    if (type == G4_Q4_K)
+        G4_CUDA(launch_pdl(tc4_from_q8_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, (const uint8_t *)q8,
+                           n / G4_QK, B, np, bq, yd));
+    else G4_CUDA(launch_pdl(tc_from_q8_kernel, dim3(n / G4_QK, np / 8), dim3(256), 0, st, (const uint8_t *)q8, n / G4_QK,
                        B, np, bq, yd));
     G4_LAUNCHED();
     return G4_OK;
@@ -542,9 +977,9 @@ size_t tc_part_bytes(int rows, int n, int nsm) {
     const TcPlan p = tc_plan(rows, n / G4_QK, nsm);
     return p.ksplit > 1 ? (size_t)p.ksplit * 64 * rows * sizeof(float) : 0;
 }
-int tc_tickets(int rows) { return ((rows + 127) / 128) * kTcMathWarps; }
+int tc_tickets(int rows) { return ((rows + 127) / 128) * 8; }
 
-int launch_gemm_tc(const CUtensorMap *tm, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
+int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
                    float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
                    cudaStream_t st) {
     if (type != G4_Q4_K && type != G4_Q5_K) { set_error(G4_ERR_TYPE, "tc gemm: type %d", type); return G4_ERR_TYPE; }
@@ -555,7 +990,8 @@ int launch_gemm_tc(const CUtensorMap *tm, int type, int n, int rows, const uint8
         set_error(G4_ERR_ARG, "tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
-    TcArgs a{bq, yd, out, part, tickets, err, nb, rows, B, ldo, p.ksplit, p.kslice, p.units};
+    TcArgs a{(const uint8_t *)w, device_row_bytes(type, n), bq, yd, out, part, tickets, err, nb, rows, B, ldo,
+             p.ksplit, p.kslice, p.units, EPI_STORE, 0.0f, nullptr};
     void *k = nullptr;
     size_t smem = 0;
 #define G4_TC_CASE(T, N)                                                          \
@@ -565,9 +1001,17 @@ int launch_gemm_tc(const CUtensorMap *tm, int type, int n, int rows, const uint8
         G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         G4_CUDA(launch_pdl(gemm_tc_kernel<T, N>, dim3(p.grid), dim3(kTcThreads), smem, st, *tm, a)); \
     }
-    G4_TC_CASE(G4_Q4_K, 16) else G4_TC_CASE(G4_Q4_K, 32) else G4_TC_CASE(G4_Q4_K, 64)
+#define G4_Q4TC_CASE(N)                                                           \
+    if (type == G4_Q4_K && np == N) {                                              \
+        k = q4tc_kernel_ptr<N>();                                                  \
+        smem = Q4Smem<N>::total;                                                   \
+        G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        G4_CUDA(launch_pdl(gemm_q4tc_kernel<N>, dim3(p.grid), dim3(kQ4Threads), smem, st, *tm, a)); \
+    }
+    G4_Q4TC_CASE(16) else G4_Q4TC_CASE(32) else G4_Q4TC_CASE(64)
     else G4_TC_CASE(G4_Q5_K, 16) else G4_TC_CASE(G4_Q5_K, 32) else G4_TC_CASE(G4_Q5_K, 64)
 #undef G4_TC_CASE
+#undef G4_Q4TC_CASE
     (void)k;
     G4_LAUNCHED();
     return G4_OK;

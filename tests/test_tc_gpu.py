@@ -91,3 +91,61 @@ def test_tc_gemm_repeat_deterministic(gpu, torch_cuda, g4):
     a, _ = _run(g4, torch_cuda, w, x, Q4, n, rows, tc_min=1)
     b, _ = _run(g4, torch_cuda, w, x, Q4, n, rows, tc_min=1)
     assert (a == b).all()
+
+
+Q6 = 14
+
+
+def _run6(g4, torch, w, x, n, rows, tc_min):
+    B = x.shape[0]
+    dev = torch.device("cuda:0")
+    wd = g4.weight_upload(w, Q6, n, rows)
+    try:
+        xd = torch.from_numpy(x).to(dev)
+        o = torch.full((B, rows), float("nan"), dtype=torch.float32, device=dev)
+        prev = g4.set_tc_min_batch(tc_min)
+        try:
+            g4.mm_device(o.data_ptr(), xd.data_ptr(), wd, n, rows, Q6, 0, 0, B, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+        finally:
+            g4.set_tc_min_batch(prev)
+        return o.cpu().numpy()
+    finally:
+        g4.free(wd)
+
+
+@pytest.mark.parametrize("rows,n,B", [
+    (300, 2560, 16),     # ragged row tile
+    (512, 2560, 20),     # V shape, padding sequences
+    (2560, 10240, 64),   # FFN down shape
+    (4096, 2560, 64),
+    (2560, 2048, 33),
+    (200, 1024, 70),     # two groups
+])
+def test_tc_q6K_vs_oracle(gpu, torch_cuda, orc, g4, rows, n, B):
+    """Q6_K fp32 dequant-dot (mm_quant_rows, main.c:1539-1556) for B activations at once."""
+    from _tol import dense_term_scale
+    rng = np.random.default_rng(7 * rows + n + B)
+    w = g4.synth.rand_blocks(rng, Q6, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    x[1] *= 3e4    # per-sequence magnitudes far apart
+    x[2] *= 1e-4
+    x[3, : n // 2] = 0.0   # all-zero super-blocks
+    x[4, 5] = 1e3          # one outlier in a block
+    o = _run6(g4, torch_cuda, w, x, n, rows, tc_min=1)
+    assert np.isfinite(o).all()
+    deq = np.stack([orc.dequant(w[r].copy(), Q6, n // 256) for r in range(rows)])
+    for s in range(B):
+        e = orc.mm(x[s], w, n, rows, Q6)
+        assert_close(o[s], e, dense_term_scale(deq, x[s]), what="TC Q6K seq %d" % s)
+
+
+def test_tc_q6K_vs_gemv(gpu, torch_cuda, g4):
+    rows, n, B = 640, 2560, 24
+    rng = np.random.default_rng(99)
+    w = g4.synth.rand_blocks(rng, Q6, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    o_tc = _run6(g4, torch_cuda, w, x, n, rows, tc_min=1)
+    o_sv = _run6(g4, torch_cuda, w, x, n, rows, tc_min=1 << 30)
+    for s in range(B):
+        assert_close(o_tc[s], o_sv[s], what="TC vs GEMV Q6K seq %d" % s)
