@@ -575,7 +575,11 @@ static int tc_scratch(int n, int d, TcScratchDev **out) {
     if (dev < 0 || dev >= 64) { set_error(G4_ERR_NO_DEVICE, "device ordinal %d out of range", dev); return G4_ERR_NO_DEVICE; }
     std::lock_guard<std::mutex> lk(g_tcs_mu);
     TcScratchDev &S = g_tcs[dev];
-    if (!S.nsm) G4_CUDA(cudaDeviceGetAttribute(&S.nsm, cudaDevAttrMultiProcessorCount, dev));
+    if (!S.nsm) {  // first use on this device
+        G4_CUDA(cudaDeviceGetAttribute(&S.nsm, cudaDevAttrMultiProcessorCount, dev));
+        G4_TRY(prime_tc_attrs());
+        G4_TRY(prime_tc6_attrs());
+    }
     const size_t bq = std::max(tc_operand_bytes(n), tc6_operand_bytes(n)), part = tc_part_bytes(d, n, S.nsm);
     const int nt = tc_tickets(d);
     if (bq > S.bq_bytes || part > S.part_bytes || nt > S.n_tickets) {

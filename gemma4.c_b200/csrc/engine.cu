@@ -24,6 +24,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <vector>
@@ -77,6 +78,14 @@ struct g4_engine {
     std::map<long, int> graph_kernels;  // kernel nodes per captured step
     std::map<long, float *> graph_hidden;  // where each step leaves State.x
     int last_lm_mode = 0, last_step_kernels = 0;
+    // tensor-core path for the batched step (B >= tc_min_batch)
+    struct alignas(64) MapBuf { unsigned char b[512]; };
+    std::map<const void *, MapBuf> tmaps;  // tensor maps per weight matrix
+    uint8_t *tcq = nullptr, *tc6 = nullptr;  // B operands (Q4_K/Q5_K and Q6_K)
+    float *tc_part = nullptr;
+    size_t tc_part_bytes = 0;
+    int *tc_tickets = nullptr;
+    int nsm = 0, tc_min_batch = 9;
     std::mutex mu;
 };
 
@@ -175,18 +184,73 @@ int gemv(g4_engine *e, const void *w, int type, int n, int rows, const float *ac
     return launch_gemv_kquant(jobs, B, e->st);
 }
 
+bool is_kq(int t) { return t == G4_Q4_K || t == G4_Q5_K || t == G4_Q6_K; }
+
+// Whether a GEMM of this step runs on the tensor cores.
+bool use_tc(const g4_engine *e, int B, int type, int epi) {
+    if (!e->tcq || B < e->tc_min_batch || !is_kq(type)) return false;
+    return epi == EPI_STORE || (epi == EPI_SOFTCAP_ARGMAX && type == G4_Q6_K);
+}
+
+// Tensor maps of a weight matrix, encoded once per engine.
+int tc_maps(g4_engine *e, const void *w, int type, int n, int rows, const void **out) {
+    auto it = e->tmaps.find(w);
+    if (it == e->tmaps.end()) {
+        g4_engine::MapBuf mb{};
+        if (type == G4_Q6_K) {
+            if (tc6_maps_bytes() > sizeof(mb.b)) { set_error(G4_ERR_STATE, "tensor-map bundle size"); return G4_ERR_STATE; }
+            TRY(tc6_weight_maps(mb.b, w, n, rows));
+        } else {
+            TRY(tc_weight_map(reinterpret_cast<CUtensorMap *>(mb.b), w, type, n, rows));
+        }
+        it = e->tmaps.emplace(w, mb).first;
+    }
+    *out = it->second.b;
+    return G4_OK;
+}
+
+// y[B][rows] = W . act (fp32 [B][ld]) on the tensor cores, in groups of up
+// to 64 sequences.  act_ready: the B operand of this activation is already
+// in place (same activation as the previous call of the same type class).
+int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float *act, int ld, bool act_ready,
+            float *out, int ldo, int B, int epi = EPI_STORE, unsigned long long *keys = nullptr, float cap = 0.0f) {
+    const void *maps = nullptr;
+    TRY(tc_maps(e, w, type, n, rows, &maps));
+    if (B > 64) act_ready = false;
+    for (int g0 = 0; g0 < B; g0 += 64) {
+        const int gb = B - g0 < 64 ? B - g0 : 64, np = tc_np(gb);
+        float *o = out ? out + (size_t)g0 * ldo : nullptr;
+        if (type == G4_Q6_K) {
+            float *ys = (float *)(e->tc6 + tc6_ys_offset(n));
+            if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, e->st));
+            TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, e->tc_part, e->tc_part_bytes,
+                                 e->tc_tickets, e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st));
+        } else {
+            float *yd = (float *)(e->tcq + tc_yd_offset(n));
+            if (!act_ready) TRY(launch_tc_quant(type, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
+            TRY(launch_gemm_tc((const CUtensorMap *)maps, w, type, n, rows, e->tcq, yd, gb, np, o, ldo, e->tc_part,
+                               e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, e->st));
+        }
+    }
+    return G4_OK;
+}
+
 int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
                        e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
-    TRY(gemv(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
+    if (use_tc(e, B, e->ple_proj_t, EPI_STORE))
+        TRY(tc_gemm(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
+    else
+        TRY(gemv(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
     TRY(launch_ple_mix(e->ple_tokb, e->ple_ctx, e->ple_proj_norm, pd, L, e->ctx_scale, e->mix_scale, e->eps, e->ple,
                        B, e->st));
     for (int l = 0; l < L; l++) {
         const LayerDev &ly = e->layers[l];
         const LayerDev *prev = l > 0 ? &e->layers[l - 1] : nullptr;
         const bool has_kv = l < G4_N_LAYER_KV;
-        const bool q8_in = is_q8_type(ly.wq_t) || (has_kv && (is_q8_type(ly.wk_t) || is_q8_type(ly.wv_t)));
+        const bool tcq_l = use_tc(e, B, ly.wq_t, EPI_STORE);  // projections of this layer on the tensor cores
+        const bool q8_in = !tcq_l && (is_q8_type(ly.wq_t) || (has_kv && (is_q8_type(ly.wk_t) || is_q8_type(ly.wv_t))));
         ResNorm r{};
         r.x_in = e->x; r.delta = prev ? e->p_raw : nullptr; r.post_w = prev ? prev->post_norm : nullptr;
         r.scale = prev ? prev->out_scale : nullptr; r.x_out = e->x; r.pre_w = ly.attn_norm; r.xn_out = e->xn;
@@ -198,6 +262,21 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         Proj pr[3] = {{ly.wq, ly.wq_t, ly.qd, e->q}, {ly.wk, ly.wk_t, ly.kvd, e->k}, {ly.wv, ly.wv_t, ly.kvd, e->v}};
         const int np = has_kv ? 3 : 1;
         const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
+        if (tcq_l) {
+            bool ready8 = false, ready6 = false;  // operand of xn already laid out (Q4/Q5 class, Q6 class)
+            for (int i = 0; i < np; i++) {
+                if (use_tc(e, B, pr[i].t, EPI_STORE)) {
+                    bool &rdy = pr[i].t == G4_Q6_K ? ready6 : ready8;
+                    // Q4_K and Q5_K operands differ in layout: reuse only within one type
+                    const bool same = rdy && (pr[i].t == G4_Q6_K || i == 0 || pr[i].t == pr[i - 1].t);
+                    TRY(tc_gemm(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, same, pr[i].out, pr[i].rows, B));
+                    rdy = true;
+                } else {
+                    TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
+                }
+            }
+        }
+        if (!tcq_l)
         for (int kt : ktypes) {
             GemvJobs jobs{};
             for (int i = 0; i < np; i++) {
@@ -210,7 +289,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
             jobs.err = e->d_err;
             if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
         }
-        for (int i = 0; i < np; i++)
+        for (int i = 0; i < np && !tcq_l; i++)
             if (pr[i].t == G4_F32 || pr[i].t == G4_F16 || pr[i].t == G4_BF16)
                 TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
 
@@ -229,8 +308,12 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
 
         // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
-        TRY(gemv(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
-        const bool q8_ffn = is_q8_type(ly.gate_t) || is_q8_type(ly.up_t);
+        if (use_tc(e, B, ly.wo_t, EPI_STORE))
+            TRY(tc_gemm(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
+        else
+            TRY(gemv(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
+        const bool tc_ffn = use_tc(e, B, ly.gate_t, EPI_STORE) && use_tc(e, B, ly.up_t, EPI_STORE);
+        const bool q8_ffn = !tc_ffn && (is_q8_type(ly.gate_t) || is_q8_type(ly.up_t));
         ResNorm r2{};
         r2.x_in = e->x; r2.delta = e->o_raw; r2.post_w = ly.post_attn_norm; r2.x_out = e->x; r2.pre_w = ly.ffn_norm;
         r2.xn_out = e->xn; r2.q8_out = q8_ffn ? e->q8 : nullptr; r2.dim = dim; r2.eps = e->eps;
@@ -238,7 +321,11 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
 
         // gate / up with the GELU product fused (1976-1978)
         const bool kq = !(ly.gate_t == G4_F32 || ly.gate_t == G4_F16 || ly.gate_t == G4_BF16);
-        if (kq && ly.gate_t == ly.up_t) {
+        if (tc_ffn) {  // gate and up share the activation operand; GELU product as its own pass
+            TRY(tc_gemm(e, ly.gate, ly.gate_t, dim, e->hidden, e->xn, dim, false, e->hb, e->hidden, B));
+            TRY(tc_gemm(e, ly.up, ly.up_t, dim, e->hidden, e->xn, dim, ly.up_t == ly.gate_t, e->hb2, e->hidden, B));
+            TRY(launch_gelu_mul(e->hb, e->hb2, (size_t)B * e->hidden, e->st));
+        } else if (kq && ly.gate_t == ly.up_t) {
             GemvJobs fj{};
             fj.njobs = 1;
             GemvJob &J = fj.j[0];
@@ -253,7 +340,10 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
             TRY(launch_gelu_mul(e->hb, e->hb2, (size_t)B * e->hidden, e->st));
         }
         // down projection, post-FFN norm + residual (1979-1984)
-        TRY(gemv(e, ly.down, ly.down_t, e->hidden, dim, e->hb, e->hidden, false, e->d_raw, dim, B));
+        if (use_tc(e, B, ly.down_t, EPI_STORE))
+            TRY(tc_gemm(e, ly.down, ly.down_t, e->hidden, dim, e->hb, e->hidden, false, e->d_raw, dim, B));
+        else
+            TRY(gemv(e, ly.down, ly.down_t, e->hidden, dim, e->hb, e->hidden, false, e->d_raw, dim, B));
         ResNorm r3{};
         r3.x_in = e->x; r3.delta = e->d_raw; r3.post_w = ly.post_ffw_norm; r3.x_out = e->x; r3.dim = dim;
         r3.eps = e->eps;
@@ -272,8 +362,12 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     if (!lm_mode) return G4_OK;
     // tied LM head + softcap + first-max argmax (1780-1796, 2045-2050)
     const bool dense = e->embd_t == G4_F32 || e->embd_t == G4_F16 || e->embd_t == G4_BF16;
-    TRY(gemv(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, (want_logits || dense) ? e->logits : nullptr,
-             e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
+    if (use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX))
+        TRY(tc_gemm(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, want_logits ? e->logits : nullptr,
+                    e->vocab, B, EPI_SOFTCAP_ARGMAX, e->keys, e->softcap));
+    else
+        TRY(gemv(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, (want_logits || dense) ? e->logits : nullptr,
+                 e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
     TRY(launch_keys_to_tokens(e->keys, e->d_next, B, e->st));
     return G4_OK;
 }
@@ -637,6 +731,24 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     e->max_chunks = (max_seq + attn_chunk_size() - 1) / attn_chunk_size();
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
+    if (max_batch > kFusedMaxBatch) {  // tensor-core path of the batched step
+        G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
+        int nmax = std::max(std::max(dim, e->hidden), std::max(e->qd_max, pd));
+        size_t part = 0;
+        int rows_max = e->vocab;
+        const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
+                                 {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}};
+        for (auto &sh : shapes) {
+            part = std::max(part, tc_part_bytes(sh[0], sh[1], e->nsm));
+            rows_max = std::max(rows_max, sh[0]);
+        }
+        nmax = (nmax + G4_QK - 1) / G4_QK * G4_QK;
+        TRY(dalloc_t(e, &e->tcq, tc_operand_bytes(nmax)));
+        TRY(dalloc_t(e, &e->tc6, tc6_operand_bytes(nmax)));
+        e->tc_part_bytes = std::max(part, (size_t)16);
+        TRY(dalloc_t(e, &e->tc_part, e->tc_part_bytes / sizeof(float)));
+        TRY(dalloc_t(e, &e->tc_tickets, (size_t)tc_tickets(rows_max)));
+    }
     TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
     TRY(dalloc_t(e, &e->d_err, 1));
     G4_CUDA(cudaMallocHost((void **)&e->h_err, sizeof(int)));

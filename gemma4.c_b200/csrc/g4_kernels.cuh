@@ -106,6 +106,8 @@ size_t tc6_operand_bytes(int n);     // x1/x2 operand + scales of one activation
 size_t tc6_ys_offset(int n);
 size_t tc6_maps_bytes();             // bytes of the opaque tensor-map bundle
 int tc6_weight_maps(void *maps_out, const void *w, int n, int rows);
+int prime_tc6_attrs();
+int prime_tc_attrs();
 int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *ys, cudaStream_t st);
 int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
                      int np, float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,

@@ -546,12 +546,18 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
 #define G4_Q6TC_CASE(N)                                                                             \
     if (np == N) {                                                                                   \
         const size_t smem = Q6Smem<N>::total;                                                        \
-        G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<N>(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         G4_CUDA(launch_pdl(gemm_q6tc_kernel<N>, dim3(p.grid), dim3(kQ6Threads), smem, st, *(const Q6Maps *)maps, a)); \
     }
     G4_Q6TC_CASE(16) else G4_Q6TC_CASE(32) else G4_Q6TC_CASE(64)
 #undef G4_Q6TC_CASE
     G4_LAUNCHED();
+    return G4_OK;
+}
+
+int prime_tc6_attrs() {
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<16>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<16>::total));
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<32>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<32>::total));
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<64>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<64>::total));
     return G4_OK;
 }
 

@@ -998,14 +998,12 @@ int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int ro
     if (type == T && np == N) {                                                    \
         k = tc_kernel_ptr<T, N>();                                                 \
         smem = TcSmem<T, N>::total;                                                \
-        G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         G4_CUDA(launch_pdl(gemm_tc_kernel<T, N>, dim3(p.grid), dim3(kTcThreads), smem, st, *tm, a)); \
     }
 #define G4_Q4TC_CASE(N)                                                           \
     if (type == G4_Q4_K && np == N) {                                              \
         k = q4tc_kernel_ptr<N>();                                                  \
         smem = Q4Smem<N>::total;                                                   \
-        G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         G4_CUDA(launch_pdl(gemm_q4tc_kernel<N>, dim3(p.grid), dim3(kQ4Threads), smem, st, *tm, a)); \
     }
     G4_Q4TC_CASE(16) else G4_Q4TC_CASE(32) else G4_Q4TC_CASE(64)
@@ -1013,7 +1011,23 @@ int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int ro
 #undef G4_TC_CASE
 #undef G4_Q4TC_CASE
     (void)k;
+    (void)smem;
     G4_LAUNCHED();
+    return G4_OK;
+}
+
+// Dynamic shared-memory limits of the tensor-core kernels (once per device,
+// outside any stream capture).
+int prime_tc_attrs() {
+#define G4_PRIME(K, BYTES) G4_CUDA(cudaFuncSetAttribute((const void *)K, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BYTES)))
+    constexpr int s16 = TcSmem<G4_Q5_K, 16>::total, s32 = TcSmem<G4_Q5_K, 32>::total, s64 = TcSmem<G4_Q5_K, 64>::total;
+    G4_PRIME((tc_kernel_ptr<G4_Q5_K, 16>()), s16);
+    G4_PRIME((tc_kernel_ptr<G4_Q5_K, 32>()), s32);
+    G4_PRIME((tc_kernel_ptr<G4_Q5_K, 64>()), s64);
+    G4_PRIME(q4tc_kernel_ptr<16>(), Q4Smem<16>::total);
+    G4_PRIME(q4tc_kernel_ptr<32>(), Q4Smem<32>::total);
+    G4_PRIME(q4tc_kernel_ptr<64>(), Q4Smem<64>::total);
+#undef G4_PRIME
     return G4_OK;
 }
 

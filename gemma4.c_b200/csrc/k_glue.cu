@@ -319,6 +319,8 @@ int prime_kernel_attrs() {
     G4_CUDA(cudaFuncSetAttribute(resnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
     int rc = prime_gemv_attrs();
     if (rc) return rc;
+    if ((rc = prime_tc_attrs())) return rc;
+    if ((rc = prime_tc6_attrs())) return rc;
     return prime_attn_attrs();
 }
 }  // namespace g4
