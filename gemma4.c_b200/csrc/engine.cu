@@ -302,7 +302,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         const LayerDev &src = e->layers[ly.src];
         A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
         A.window = ly.swa ? e->window : 0;
-        A.eps = e->eps;
+        A.eps = e->eps; A.err = e->d_err;
         A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
         A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
         TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
@@ -459,7 +459,7 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
         const LayerDev &src = e->layers[ly.src];
         A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
         A.window = ly.swa ? e->window : 0;
-        A.eps = e->eps;
+        A.eps = e->eps; A.err = e->d_err;
         A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
         TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
 

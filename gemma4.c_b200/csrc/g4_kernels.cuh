@@ -64,6 +64,7 @@ struct AttnLayer {
     int src_ring;                   // slots of the source cache
     int window;                     // 0: full causal, else sliding window
     float eps;
+    int *err;                       // status word for bounded waits (may be null)
     float *qo;                      // output [B][n_heads*hd]
     float *part;                    // scratch [B][n_heads][max_chunks][hd+2]
     int *counters;                  // [B][n_kv] zero-initialised tickets

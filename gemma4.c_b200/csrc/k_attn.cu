@@ -23,6 +23,7 @@
 // positions; the grid covers the largest window and idle chunks exit.
 #include <math.h>
 
+#include "g4_async.cuh"
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
 
@@ -105,10 +106,17 @@ __device__ __forceinline__ void warp_norm_rope(const float *src, const float *w,
     }
 }
 
+// Head dims up to 256 stage the chunk's K and V rows in shared memory with
+// bulk copies (TMA) issued at CTA start, so the score and P.V phases do not
+// each wait for HBM; head dim 512 loads rows into registers.
+template <int EPL>
+constexpr bool attn_tma() { return EPL <= 8; }
+
 template <int EPL, int G>
 constexpr size_t attn_smem_bytes() {
     return sizeof(float) * ((size_t)G * EPL * 32 + (size_t)8 * G * EPL * 32 + (size_t)G * kChunk + 2 * G +
-                            2 * (size_t)EPL * 32 + (size_t)G * kMaxWts);
+                            2 * (size_t)EPL * 32 + (size_t)G * kMaxWts +
+                            (attn_tma<EPL>() ? (size_t)2 * kChunk * EPL * 32 : 0));
 }
 
 // One CTA per (chunk of 32 positions, kv head, sequence), all G query heads
@@ -128,7 +136,10 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     float *knew = dsm + 9 * G * HD + G * kChunk + 2 * G;                        // [HD]
     float *vnew = knew + HD;                                                    // [HD]
     float *wts = vnew + HD;                                                     // [G][kMaxWts] combine weights
+    float *kbuf = wts + G * kMaxWts;                                            // [kChunk][HD] (TMA staging)
+    float *vbuf = kbuf + kChunk * HD;                                           // [kChunk][HD]
     __shared__ int ticket;
+    __shared__ __align__(8) uint64_t kvbar;
     pdl_trigger();
     pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -144,6 +155,24 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     const bool last_chunk = c == nch - 1;
     const bool new_row = L.append && last_chunk;  // this CTA owns row `pos`
     const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
+    const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
+    if constexpr (attn_tma<EPL>()) {
+        // 0. the chunk's rows in ring order: slots s_a.. (and 0.. after a wrap) -> kbuf/vbuf rows 0..cnt-1.
+        // Row `pos` of a layer that appends is (re)written below; its stale slot is read here and ignored.
+        if (threadIdx.x == 0) {
+            mbar_init(&kvbar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            const int s_a = (t0 + cbeg) % L.src_ring, n1 = min(cnt, L.src_ring - s_a);
+            const uint32_t rb = HD * sizeof(float);
+            mbar_expect_tx(&kvbar, 2u * (uint32_t)cnt * rb);
+            bulk_g2s(kbuf, L.src_kc + (head_base + s_a) * HD, (uint32_t)n1 * rb, &kvbar);
+            bulk_g2s(vbuf, L.src_vc + (head_base + s_a) * HD, (uint32_t)n1 * rb, &kvbar);
+            if (n1 < cnt) {
+                bulk_g2s(kbuf + n1 * HD, L.src_kc + head_base * HD, (uint32_t)(cnt - n1) * rb, &kvbar);
+                bulk_g2s(vbuf + n1 * HD, L.src_vc + head_base * HD, (uint32_t)(cnt - n1) * rb, &kvbar);
+            }
+        }
+    }
     const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
 
     // 1. query heads (and the new K/V row) into shared memory
@@ -168,7 +197,10 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     float qv[G][EPL];
 #pragma unroll
     for (int g = 0; g < G; g++) load_row<EPL>(qv[g], qs[g] + lane * EPL);
-    const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
+    if constexpr (attn_tma<EPL>()) {
+        // bounded: on expiry record the status and go on (no thread leaves before the barriers below)
+        if (!mbar_wait(&kvbar, 0) && L.err) atomicExch(L.err, G4_ERR_TIMEOUT);
+    }
     // 2. scores: warp w owns rows w, w+8, ...; all its row loads are issued first
     constexpr int RPW = kChunk / 8;
     {
@@ -178,7 +210,8 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
             const int tl = warp + 8 * r;
             const int t = t0 + cbeg + min(tl, cnt - 1);
             const float *kr = (new_row && t == pos) ? knew + lane * EPL
-                                                    : L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+                              : attn_tma<EPL>() ? kbuf + min(tl, cnt - 1) * HD + lane * EPL
+                                                : L.src_kc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
             load_row<EPL>(kv[r], kr);
         }
 #pragma unroll
@@ -224,7 +257,8 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
             const int tl = warp + 8 * r;
             const int t = t0 + cbeg + min(tl, cnt - 1);
             const float *vr = (new_row && t == pos) ? vnew + lane * EPL
-                                                    : L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
+                              : attn_tma<EPL>() ? vbuf + min(tl, cnt - 1) * HD + lane * EPL
+                                                : L.src_vc + (head_base + (size_t)(t % L.src_ring)) * HD + lane * EPL;
             load_row<EPL>(vv[r], vr);
         }
 #pragma unroll
@@ -282,6 +316,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
         const int g = i / HD, d = i % HD;
         const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps;
         float o = 0.0f;
+#pragma unroll 8
         for (int cc = 0; cc < nch; cc++) {
             const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps) - ml[g][0]);
             o = fmaf(wgt, __ldcg(base + cc * ps + 2 + d), o);
@@ -289,6 +324,250 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
         L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * ml[g][1];
     }
     if (threadIdx.x == 0) L.counters[(size_t)b * L.n_kv + h] = 0;  // ready for the next launch
+}
+
+// ---------------------------------------------------------------- streaming variant (head dim <= 256)
+//
+// One CTA per (split of `span` positions, kv head, sequence), span a multiple
+// of 32 chosen so that the grid is about two waves: the split is streamed in
+// sub-chunks of 32 rows through a two-stage shared-memory ring filled by bulk
+// copies (TMA), so the copy of sub-chunk j+1 overlaps the arithmetic of j.
+// Each warp keeps an online softmax state (max, sum, unnormalised P.V) per
+// query head over the rows it owns; the 8 warp states are combined once at
+// the end, then the split partials are merged by the last CTA of the (kv
+// head, sequence) as in attn_fused_kernel.
+constexpr int kSub = 32;
+
+template <int EPL, int G>
+constexpr size_t attn_stream_smem() {
+    return sizeof(float) * ((size_t)G * EPL * 32 + 2 * (size_t)EPL * 32 + 4 * (size_t)kSub * EPL * 32 +
+                            (size_t)8 * G * 2 + (size_t)G * kMaxWts);
+}
+
+template <int EPL, int G>
+__global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
+    constexpr int HD = EPL * 32, RPW = kSub / 8;
+    extern __shared__ __align__(16) float dsm[];
+    float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(dsm);  // [G][HD]
+    float *knew = dsm + G * HD, *vnew = knew + HD;          // [HD] each
+    float *ring = vnew + HD;                                // [2 stages][K, V][kSub][HD]
+    float(*wml)[G][2] = reinterpret_cast<float(*)[G][2]>(ring + 4 * kSub * HD);  // [8][G] (max, sum)
+    float *wts = reinterpret_cast<float *>(wml + 8);        // [G][kMaxWts] merge weights
+    __shared__ __align__(8) uint64_t full[2];
+    __shared__ int ticket;
+    __shared__ float mlf[G][2];
+    pdl_trigger();
+    pdl_wait();
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos = *pos_dev;
+    int t0 = 0;
+    if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
+    const int nwin = pos + 1 - t0;
+    const int nsplit = (nwin + span - 1) / span;
+    if (c >= nsplit) return;
+    const int beg = c * span, ctot = min(span, nwin - beg), nsub = (ctot + kSub - 1) / kSub;
+    const bool new_row = L.append && c == nsplit - 1;  // this CTA owns row `pos`
+    const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
+    const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
+    const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
+
+    // rows [beg + 32j, +cnt) of the split (ring slots, split at a wrap) -> stage j&1.  Row `pos` of a
+    // layer that appends is (re)written below; its stale slot may be read here and is ignored.
+    auto issue = [&](int j) {
+        const int st = j & 1, cnt = min(kSub, ctot - j * kSub);
+        float *kb = ring + (size_t)st * 2 * kSub * HD, *vb = kb + kSub * HD;
+        const int s_a = (t0 + beg + j * kSub) % L.src_ring, n1 = min(cnt, L.src_ring - s_a);
+        const uint32_t rb = HD * sizeof(float);
+        mbar_expect_tx(&full[st], 2u * (uint32_t)cnt * rb);
+        bulk_g2s(kb, L.src_kc + (head_base + s_a) * HD, (uint32_t)n1 * rb, &full[st]);
+        bulk_g2s(vb, L.src_vc + (head_base + s_a) * HD, (uint32_t)n1 * rb, &full[st]);
+        if (n1 < cnt) {
+            bulk_g2s(kb + n1 * HD, L.src_kc + head_base * HD, (uint32_t)(cnt - n1) * rb, &full[st]);
+            bulk_g2s(vb + n1 * HD, L.src_vc + head_base * HD, (uint32_t)(cnt - n1) * rb, &full[st]);
+        }
+    };
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        issue(0);
+        if (nsub > 1) issue(1);
+    }
+    // query heads (and the new K/V row) into shared memory
+    if (warp < G) {
+        const float *src = L.q + (size_t)b * qd + (size_t)(h * G + warp) * HD;
+        if (L.prep) {
+            warp_norm_rope<EPL>(src, L.q_norm, cs, L.n_rot, L.eps, qs[warp], nullptr);
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i++) qs[warp][lane + 32 * i] = src[lane + 32 * i];
+        }
+    } else if (new_row && warp == G) {
+        const int slot = pos % L.ring;
+        float *kdst = L.kc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        warp_norm_rope<EPL>(L.k + (size_t)b * kvd + (size_t)h * HD, L.k_norm, cs, L.n_rot, L.eps, knew, kdst);
+    } else if (new_row && warp == G + 1) {
+        const int slot = pos % L.ring;
+        float *vdst = L.vc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        warp_norm_rope<EPL>(L.v + (size_t)b * kvd + (size_t)h * HD, nullptr, nullptr, 0, L.eps, vnew, vdst);
+    }
+    __syncthreads();
+    float qv[G][EPL];
+#pragma unroll
+    for (int g = 0; g < G; g++) load_row<EPL>(qv[g], qs[g] + lane * EPL);
+    float m[G], l[G], acc[G][EPL];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
+    }
+    for (int j = 0; j < nsub; j++) {
+        const int st = j & 1, cnt = min(kSub, ctot - j * kSub);
+        // bounded: on expiry record the status and go on (every thread still reaches the barriers)
+        if (!mbar_wait(&full[st], (j >> 1) & 1) && L.err) atomicExch(L.err, G4_ERR_TIMEOUT);
+        const float *kb = ring + (size_t)st * 2 * kSub * HD, *vb = kb + kSub * HD;
+        float sv[RPW][G];
+#pragma unroll
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+            const int t = t0 + beg + j * kSub + tl;
+            float kr[EPL];
+            load_row<EPL>(kr, ((new_row && t == pos) ? knew : kb + min(tl, cnt - 1) * HD) + lane * EPL);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float d = 0.0f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) d = fmaf(kr[e], qv[g][e], d);
+                d = warp_sum(d);
+                sv[r][g] = tl < cnt ? d : -INFINITY;
+            }
+        }
+        // online softmax update of this warp's rows
+        float p[RPW][G];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float mx = sv[0][g];
+#pragma unroll
+            for (int r = 1; r < RPW; r++) mx = fmaxf(mx, sv[r][g]);
+            const float mn = fmaxf(m[g], mx);
+            if (mn == -INFINITY) {
+#pragma unroll
+                for (int r = 0; r < RPW; r++) p[r][g] = 0.0f;
+                continue;
+            }
+            const float sc = expf(m[g] - mn);  // 0 when m was -inf
+            l[g] *= sc;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) acc[g][e] *= sc;
+#pragma unroll
+            for (int r = 0; r < RPW; r++) {
+                p[r][g] = sv[r][g] == -INFINITY ? 0.0f : expf(sv[r][g] - mn);
+                l[g] += p[r][g];
+            }
+            m[g] = mn;
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; r++) {
+            const int tl = warp + 8 * r;
+            if (tl >= cnt) break;
+            const int t = t0 + beg + j * kSub + tl;
+            float vr[EPL];
+            load_row<EPL>(vr, ((new_row && t == pos) ? vnew : vb + tl * HD) + lane * EPL);
+#pragma unroll
+            for (int g = 0; g < G; g++)
+#pragma unroll
+                for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(p[r][g], vr[e], acc[g][e]);
+        }
+        __syncthreads();  // stage st consumed by every warp
+        if (tid == 0 && j + 2 < nsub) issue(j + 2);
+    }
+    // combine the 8 warp states (the ring is free now)
+    float *red = ring;  // [8][G][HD]
+    if (lane == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) { wml[warp][g][0] = m[g]; wml[warp][g][1] = l[g]; }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < EPL; e++) red[((size_t)warp * G + g) * HD + lane * EPL + e] = acc[g][e];
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int w = 0; w < 8; w++) M = fmaxf(M, wml[w][tid][0]);
+        float S = 0.0f;
+        for (int w = 0; w < 8; w++) {
+            const float f = wml[w][tid][0] == -INFINITY ? 0.0f : expf(wml[w][tid][0] - M);
+            wml[w][tid][0] = f;  // combine weight of warp w
+            S = fmaf(f, wml[w][tid][1], S);
+        }
+        mlf[tid][0] = M;
+        mlf[tid][1] = S;
+    }
+    __syncthreads();
+    const size_t ps = (size_t)HD + 2;
+    for (int i = tid; i < G * HD; i += 256) {
+        const int g = i / HD, d = i % HD;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) o = fmaf(wml[w][g][0], red[((size_t)w * G + g) * HD + d], o);
+        float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + c) * ps;
+        pr[2 + d] = o;
+        if (d == 0) { pr[0] = mlf[g][0]; pr[1] = mlf[g][1]; }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(L.counters + (size_t)b * L.n_kv + h, 1);
+    __syncthreads();
+    if (ticket != nsplit - 1) return;
+    __threadfence();
+    // merge: M = max_c m_c; out = sum_c e^(m_c-M) o_c / sum_c e^(m_c-M) l_c
+    if (warp < G) {
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + warp) * L.max_chunks * ps;
+        float M = -INFINITY;
+        for (int cc = lane; cc < nsplit; cc += 32) M = fmaxf(M, __ldcg(base + cc * ps));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float S = 0.0f;
+        for (int cc = lane; cc < nsplit; cc += 32) {
+            const float wgt = expf(__ldcg(base + cc * ps) - M);
+            if (cc < kMaxWts) wts[warp * kMaxWts + cc] = wgt;
+            S = fmaf(wgt, __ldcg(base + cc * ps + 1), S);
+        }
+        S = warp_sum(S);
+        if (lane == 0) { mlf[warp][0] = M; mlf[warp][1] = 1.0f / S; }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += 256) {
+        const int g = i / HD, d = i % HD;
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps;
+        float o = 0.0f;
+#pragma unroll 8
+        for (int cc = 0; cc < nsplit; cc++) {
+            const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps) - mlf[g][0]);
+            o = fmaf(wgt, __ldcg(base + cc * ps + 2 + d), o);
+        }
+        L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * mlf[g][1];
+    }
+    if (tid == 0) L.counters[(size_t)b * L.n_kv + h] = 0;  // ready for the next launch
+}
+
+template <int EPL, int G>
+static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, cudaStream_t st) {
+    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(256), attn_stream_smem<EPL, G>(), st, L, pos_dev, span));
+    return G4_OK;
+}
+
+template <int EPL>
+static int launch_stream_g(const AttnLayer &L, int G, dim3 grid, const int *pos_dev, int span, cudaStream_t st) {
+    switch (G) {
+    case 1: return launch_stream_eg<EPL, 1>(grid, L, pos_dev, span, st);
+    case 2: return launch_stream_eg<EPL, 2>(grid, L, pos_dev, span, st);
+    case 4: return launch_stream_eg<EPL, 4>(grid, L, pos_dev, span, st);
+    default: set_error(G4_ERR_ARG, "attention: GQA group %d unsupported", G); return G4_ERR_ARG;
+    }
 }
 
 template <int EPL, int G>
@@ -316,6 +595,24 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     if (L.append && G + 2 > 8) { set_error(G4_ERR_ARG, "attention: GQA group %d too large", G); return G4_ERR_ARG; }
     dim3 grid(nch, L.n_kv, B);
     int rc;
+    if (L.hd <= 256) {
+        // split length: a power-of-two number of 32-row sub-chunks (1..8) so that the grid is about
+        // two CTAs per SM of work
+        long want = ((long)span * B * L.n_kv + (long)kSub * 296 - 1) / ((long)kSub * 296);
+        int k = 1;
+        while (k < want && k < 8) k <<= 1;
+        const int sp = k * kSub;
+        const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
+        switch (L.hd) {
+        case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;
+        case 128: rc = launch_stream_g<4>(L, G, g2, pos_dev, sp, st); break;
+        default: rc = launch_stream_g<8>(L, G, g2, pos_dev, sp, st); break;
+        }
+        if (rc) return rc;
+        G4_LAUNCHED();
+        G4_CUDA(cudaGetLastError());
+        return G4_OK;
+    }
     switch (L.hd) {
     case 64: rc = launch_fused_g<2>(L, G, grid, pos_dev, st); break;
     case 128: rc = launch_fused_g<4>(L, G, grid, pos_dev, st); break;
@@ -335,8 +632,17 @@ static int prime_one() {
                                  (int)attn_smem_bytes<EPL, G>()));
     return G4_OK;
 }
+template <int EPL, int G>
+static int prime_stream() {
+    G4_CUDA(cudaFuncSetAttribute(attn_stream_kernel<EPL, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attn_stream_smem<EPL, G>()));
+    return G4_OK;
+}
 int prime_attn_attrs() {
     int rc = 0;
+    rc |= prime_stream<2, 1>(); rc |= prime_stream<2, 2>(); rc |= prime_stream<2, 4>();
+    rc |= prime_stream<4, 1>(); rc |= prime_stream<4, 2>(); rc |= prime_stream<4, 4>();
+    rc |= prime_stream<8, 1>(); rc |= prime_stream<8, 2>(); rc |= prime_stream<8, 4>();
     rc |= prime_one<2, 1>(); rc |= prime_one<2, 2>(); rc |= prime_one<2, 4>();
     rc |= prime_one<4, 1>(); rc |= prime_one<4, 2>(); rc |= prime_one<4, 4>();
     rc |= prime_one<8, 1>(); rc |= prime_one<8, 2>(); rc |= prime_one<8, 4>();

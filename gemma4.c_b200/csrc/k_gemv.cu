@@ -7,6 +7,8 @@
 // The K-quant GEMV itself lives in k_gemv_ks.cu.
 #include <math.h>
 
+#include <algorithm>
+
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
 #include "g4_prologue.cuh"
@@ -116,9 +118,130 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
     }
 }
 
+// Dense GEMV for many sequences: each weight row is read once per NS
+// sequences (staged in shared memory) instead of once per sequence.  Every
+// accumulator sees exactly the operation order of gemv_dense_kernel, so the
+// result of a sequence does not depend on the batch.
+template <int NS>
+__global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
+                                                            const float *__restrict__ x, int ldx, int B,
+                                                            float *__restrict__ out, int ldo, int epi,
+                                                            const float *__restrict__ evec, int ld_evec) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    pdl_trigger();
+    pdl_wait();
+    float *xs = (float *)smem_raw;  // [NS][n]
+    const int s0 = blockIdx.y * NS, ns = min(NS, B - s0);
+    if ((n % 4) == 0 && (ldx % 4) == 0) {  // 16-byte loads, 8 in flight per thread
+        const int n4 = n / 4, tot = ns * n4;
+        for (int i0 = threadIdx.x; i0 < tot; i0 += 8 * blockDim.x) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < tot) v[u] = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(s0 + i / n4) * ldx) + i % n4);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < tot) reinterpret_cast<float4 *>(xs + (size_t)(i / n4) * n)[i % n4] = v[u];
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < ns * n; i += blockDim.x) {
+            const int s = i / n, j = i % n;
+            xs[(size_t)s * n + j] = x[(size_t)(s0 + s) * ldx + j];
+        }
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the staged activations serve rows blockIdx.x*8 + warp, stepping over the grid
+    for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < rows; row += gridDim.x * (blockDim.x >> 5)) {
+    float acc[NS];
+#pragma unroll
+    for (int s = 0; s < NS; s++) acc[s] = 0.0f;
+    const bool vec = (n % 8) == 0;
+    if (type == G4_F32) {
+        const float *r = (const float *)w + (size_t)row * n;
+        if (vec) {
+            for (int j = lane * 4; j < n; j += 128) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(r + j));
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const float *xv = xs + (size_t)s * n + j;
+                    float t = acc[s];
+                    t = fmaf(a.x, xv[0], t); t = fmaf(a.y, xv[1], t); t = fmaf(a.z, xv[2], t); t = fmaf(a.w, xv[3], t);
+                    acc[s] = t;
+                }
+            }
+        } else {
+            for (int j = lane; j < n; j += 32) {
+                const float a = __ldg(r + j);
+#pragma unroll
+                for (int s = 0; s < NS; s++) acc[s] = fmaf(a, xs[(size_t)s * n + j], acc[s]);
+            }
+        }
+    } else {
+        const uint16_t *r = (const uint16_t *)w + (size_t)row * n;
+        const bool bf = type == G4_BF16;
+        if (vec) {
+            for (int j = lane * 8; j < n; j += 256) {
+                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + j));
+                const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
+                float wf[8];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint16_t l = (uint16_t)(ww[i] & 0xffffu), h = (uint16_t)(ww[i] >> 16);
+                    wf[2 * i] = bf ? bf16_to_f32(l) : f16_to_f32(l);
+                    wf[2 * i + 1] = bf ? bf16_to_f32(h) : f16_to_f32(h);
+                }
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const float4 x0 = *reinterpret_cast<const float4 *>(xs + (size_t)s * n + j);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(xs + (size_t)s * n + j + 4);
+                    float t = acc[s];
+                    t = fmaf(x0.x, wf[0], t); t = fmaf(x0.y, wf[1], t); t = fmaf(x0.z, wf[2], t); t = fmaf(x0.w, wf[3], t);
+                    t = fmaf(x1.x, wf[4], t); t = fmaf(x1.y, wf[5], t); t = fmaf(x1.z, wf[6], t); t = fmaf(x1.w, wf[7], t);
+                    acc[s] = t;
+                }
+            }
+        } else {
+            for (int j = lane; j < n; j += 32) {
+                const uint16_t v = __ldg(r + j);
+                const float wv = bf ? bf16_to_f32(v) : f16_to_f32(v);
+#pragma unroll
+                for (int s = 0; s < NS; s++) acc[s] = fmaf(xs[(size_t)s * n + j], wv, acc[s]);
+            }
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        float a = warp_sum(acc[s]);
+        if (lane == 0 && s < ns) {
+            if (epi == EPI_GELU_SCALE) a = gelu_tanh(a) * evec[(size_t)(s0 + s) * ld_evec + row];
+            out[(size_t)(s0 + s) * ldo + row] = a;
+        }
+    }
+    }
+}
+
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
                       int B, int epi, const float *evec, int ld_evec, cudaStream_t st, const Prologue *pro,
                       int pro_writer) {
+    if (!pro && B > 8 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
+        const size_t per = (size_t)n * 4;
+        // two CTAs per SM (<= 100 KB of staged activations each), about one wave in total
+        const int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : 0;
+        if (NS) {
+            const int gy = (B + NS - 1) / NS, gx = std::max(1, std::min((rows + 7) / 8, 296 / gy));
+            const dim3 grid(gx, gy);
+            if (NS == 16) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<16>, grid, dim3(256), per * 16, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            else if (NS == 8) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<8>, grid, dim3(256), per * 8, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            else G4_CUDA(launch_pdl(gemv_dense_ms_kernel<4>, grid, dim3(256), per * 4, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            G4_LAUNCHED();
+            return G4_OK;
+        }
+    }
     if (type != G4_F32 && type != G4_F16 && type != G4_BF16) {
         set_error(G4_ERR_TYPE, "gemv_dense: unsupported type %d", type);
         return G4_ERR_TYPE;
@@ -200,6 +323,9 @@ namespace g4 {
 int prime_gemv_ks_attrs();
 int prime_gemv_attrs() {
     G4_CUDA(cudaFuncSetAttribute(gemv_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return prime_gemv_ks_attrs();
 }
 }  // namespace g4
