@@ -337,23 +337,48 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
 // the end, then the split partials are merged by the last CTA of the (kv
 // head, sequence) as in attn_fused_kernel.
 constexpr int kSub = 32;
+constexpr int kStages = 3;  // ~128 KB of K/V in flight per SM at head dim 256
 
 template <int EPL, int G>
 constexpr size_t attn_stream_smem() {
-    return sizeof(float) * ((size_t)G * EPL * 32 + 2 * (size_t)EPL * 32 + 4 * (size_t)kSub * EPL * 32 +
-                            (size_t)8 * G * 2 + (size_t)G * kMaxWts);
+    return sizeof(float) * ((size_t)G * EPL * 32 + 2 * (size_t)EPL * 32 + 2 * kStages * (size_t)kSub * EPL * 32 +
+                            (size_t)16 * G * 2 + (size_t)G * kMaxWts);
+}
+
+// Sum of NV = 2^H values per lane over the 32 lanes of a warp with 31 - H
+// shuffles less than NV separate reductions: each halving step exchanges half
+// of the values.  Returns the total of value index (lane >> (5 - H)).
+template <int NV>
+__device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
+    constexpr int H = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : 4;
+#pragma unroll
+    for (int step = 0; step < H; step++) {
+        const int o = 16 >> step, half = NV >> (step + 1);
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int k = 0; k < half; k++) {
+            const float send = up ? v[k] : v[k + half];
+            const float keep = up ? v[k + half] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int o = 16 >> H; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
 }
 
 template <int EPL, int G>
-__global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
-    constexpr int HD = EPL * 32, RPW = kSub / 8;
+__global__ void __launch_bounds__(512, 1) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
+    constexpr int HD = EPL * 32, NW = 16, RPW = kSub / NW, NV = RPW * G;
+    constexpr int H = NV == 2 ? 1 : NV == 4 ? 2 : 3;  // log2(NV)
     extern __shared__ __align__(16) float dsm[];
     float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(dsm);  // [G][HD]
     float *knew = dsm + G * HD, *vnew = knew + HD;          // [HD] each
-    float *ring = vnew + HD;                                // [2 stages][K, V][kSub][HD]
-    float(*wml)[G][2] = reinterpret_cast<float(*)[G][2]>(ring + 4 * kSub * HD);  // [8][G] (max, sum)
-    float *wts = reinterpret_cast<float *>(wml + 8);        // [G][kMaxWts] merge weights
-    __shared__ __align__(8) uint64_t full[2];
+    float *ring = vnew + HD;                                // [kStages][K, V][kSub][HD]
+    float(*wml)[G][2] = reinterpret_cast<float(*)[G][2]>(ring + 2 * kStages * kSub * HD);  // [NW][G] (max, sum)
+    float *wts = reinterpret_cast<float *>(wml + NW);       // [G][kMaxWts] merge weights
+    __shared__ __align__(8) uint64_t full[kStages];
     __shared__ int ticket;
     __shared__ float mlf[G][2];
     pdl_trigger();
@@ -372,10 +397,10 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
     const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
     const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
 
-    // rows [beg + 32j, +cnt) of the split (ring slots, split at a wrap) -> stage j&1.  Row `pos` of a
-    // layer that appends is (re)written below; its stale slot may be read here and is ignored.
+    // rows [beg + 32j, +cnt) of the split (ring slots, split at a wrap) -> stage j % kStages.  Row `pos`
+    // of a layer that appends is (re)written below; its stale slot may be read here and is ignored.
     auto issue = [&](int j) {
-        const int st = j & 1, cnt = min(kSub, ctot - j * kSub);
+        const int st = j % kStages, cnt = min(kSub, ctot - j * kSub);
         float *kb = ring + (size_t)st * 2 * kSub * HD, *vb = kb + kSub * HD;
         const int s_a = (t0 + beg + j * kSub) % L.src_ring, n1 = min(cnt, L.src_ring - s_a);
         const uint32_t rb = HD * sizeof(float);
@@ -388,11 +413,9 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
         }
     };
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int k = 0; k < kStages; k++) mbar_init(&full[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        issue(0);
-        if (nsub > 1) issue(1);
+        for (int k = 0; k < kStages && k < nsub; k++) issue(k);
     }
     // query heads (and the new K/V row) into shared memory
     if (warp < G) {
@@ -424,15 +447,17 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
 #pragma unroll
         for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
     }
+    // this lane's score after the transpose sum: row r_l = idx / G, head g_l = idx % G
+    const int idx = (lane >> (5 - H)) & (NV - 1), g_l = idx % G, r_l = idx / G;
     for (int j = 0; j < nsub; j++) {
-        const int st = j & 1, cnt = min(kSub, ctot - j * kSub);
+        const int st = j % kStages, cnt = min(kSub, ctot - j * kSub);
         // bounded: on expiry record the status and go on (every thread still reaches the barriers)
-        if (!mbar_wait(&full[st], (j >> 1) & 1) && L.err) atomicExch(L.err, G4_ERR_TIMEOUT);
+        if (!mbar_wait(&full[st], (j / kStages) & 1) && L.err) atomicExch(L.err, G4_ERR_TIMEOUT);
         const float *kb = ring + (size_t)st * 2 * kSub * HD, *vb = kb + kSub * HD;
-        float sv[RPW][G];
+        float pv[NV];
 #pragma unroll
         for (int r = 0; r < RPW; r++) {
-            const int tl = warp + 8 * r;
+            const int tl = warp + NW * r;
             const int t = t0 + beg + j * kSub + tl;
             float kr[EPL];
             load_row<EPL>(kr, ((new_row && t == pos) ? knew : kb + min(tl, cnt - 1) * HD) + lane * EPL);
@@ -441,51 +466,51 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
                 float d = 0.0f;
 #pragma unroll
                 for (int e = 0; e < EPL; e++) d = fmaf(kr[e], qv[g][e], d);
-                d = warp_sum(d);
-                sv[r][g] = tl < cnt ? d : -INFINITY;
+                pv[r * G + g] = d;
             }
         }
-        // online softmax update of this warp's rows
-        float p[RPW][G];
+        float sc = warp_transpose_sum<NV>(pv, lane);  // score of (r_l, g_l)
+        if (warp + NW * r_l >= cnt) sc = -INFINITY;
+        // online softmax: the row max of each head (rows differ in lane bit 4), broadcast per head
+        const float mxl = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 16));
+        float mn_l = 0.0f;
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float mx = sv[0][g];
-#pragma unroll
-            for (int r = 1; r < RPW; r++) mx = fmaxf(mx, sv[r][g]);
+            const float mx = __shfl_sync(0xffffffffu, mxl, g << (5 - H));
             const float mn = fmaxf(m[g], mx);
-            if (mn == -INFINITY) {
+            if (mn > m[g]) {  // warp-uniform: rescale only when the running max moves
+                const float f = expf(m[g] - mn);  // 0 while m is -inf
+                l[g] *= f;
 #pragma unroll
-                for (int r = 0; r < RPW; r++) p[r][g] = 0.0f;
-                continue;
+                for (int e = 0; e < EPL; e++) acc[g][e] *= f;
+                m[g] = mn;
             }
-            const float sc = expf(m[g] - mn);  // 0 when m was -inf
-            l[g] *= sc;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) acc[g][e] *= sc;
-#pragma unroll
-            for (int r = 0; r < RPW; r++) {
-                p[r][g] = sv[r][g] == -INFINITY ? 0.0f : expf(sv[r][g] - mn);
-                l[g] += p[r][g];
-            }
-            m[g] = mn;
+            if (g == g_l) mn_l = m[g];
         }
+        const float p = sc == -INFINITY ? 0.0f : expf(sc - mn_l);
+        const float ps = p + __shfl_xor_sync(0xffffffffu, p, 16);
+#pragma unroll
+        for (int g = 0; g < G; g++) l[g] += __shfl_sync(0xffffffffu, ps, g << (5 - H));
+        // P.V over this warp's rows
 #pragma unroll
         for (int r = 0; r < RPW; r++) {
-            const int tl = warp + 8 * r;
+            const int tl = warp + NW * r;
             if (tl >= cnt) break;
             const int t = t0 + beg + j * kSub + tl;
             float vr[EPL];
             load_row<EPL>(vr, ((new_row && t == pos) ? vnew : vb + tl * HD) + lane * EPL);
 #pragma unroll
-            for (int g = 0; g < G; g++)
+            for (int g = 0; g < G; g++) {
+                const float pr = __shfl_sync(0xffffffffu, p, (r * G + g) << (5 - H));
 #pragma unroll
-                for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(p[r][g], vr[e], acc[g][e]);
+                for (int e = 0; e < EPL; e++) acc[g][e] = fmaf(pr, vr[e], acc[g][e]);
+            }
         }
         __syncthreads();  // stage st consumed by every warp
-        if (tid == 0 && j + 2 < nsub) issue(j + 2);
+        if (tid == 0 && j + kStages < nsub) issue(j + kStages);
     }
-    // combine the 8 warp states (the ring is free now)
-    float *red = ring;  // [8][G][HD]
+    // combine the NW warp states (the ring is free now)
+    float *red = ring;  // [NW][G][HD]
     if (lane == 0)
 #pragma unroll
         for (int g = 0; g < G; g++) { wml[warp][g][0] = m[g]; wml[warp][g][1] = l[g]; }
@@ -496,9 +521,9 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
     __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
-        for (int w = 0; w < 8; w++) M = fmaxf(M, wml[w][tid][0]);
+        for (int w = 0; w < NW; w++) M = fmaxf(M, wml[w][tid][0]);
         float S = 0.0f;
-        for (int w = 0; w < 8; w++) {
+        for (int w = 0; w < NW; w++) {
             const float f = wml[w][tid][0] == -INFINITY ? 0.0f : expf(wml[w][tid][0] - M);
             wml[w][tid][0] = f;  // combine weight of warp w
             S = fmaf(f, wml[w][tid][1], S);
@@ -507,13 +532,13 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
         mlf[tid][1] = S;
     }
     __syncthreads();
-    const size_t ps = (size_t)HD + 2;
-    for (int i = tid; i < G * HD; i += 256) {
+    const size_t ps_ = (size_t)HD + 2;
+    for (int i = tid; i < G * HD; i += NW * 32) {
         const int g = i / HD, d = i % HD;
         float o = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) o = fmaf(wml[w][g][0], red[((size_t)w * G + g) * HD + d], o);
-        float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + c) * ps;
+        for (int w = 0; w < NW; w++) o = fmaf(wml[w][g][0], red[((size_t)w * G + g) * HD + d], o);
+        float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + c) * ps_;
         pr[2 + d] = o;
         if (d == 0) { pr[0] = mlf[g][0]; pr[1] = mlf[g][1]; }
     }
@@ -525,29 +550,29 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
     __threadfence();
     // merge: M = max_c m_c; out = sum_c e^(m_c-M) o_c / sum_c e^(m_c-M) l_c
     if (warp < G) {
-        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + warp) * L.max_chunks * ps;
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + warp) * L.max_chunks * ps_;
         float M = -INFINITY;
-        for (int cc = lane; cc < nsplit; cc += 32) M = fmaxf(M, __ldcg(base + cc * ps));
+        for (int cc = lane; cc < nsplit; cc += 32) M = fmaxf(M, __ldcg(base + cc * ps_));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float S = 0.0f;
         for (int cc = lane; cc < nsplit; cc += 32) {
-            const float wgt = expf(__ldcg(base + cc * ps) - M);
+            const float wgt = expf(__ldcg(base + cc * ps_) - M);
             if (cc < kMaxWts) wts[warp * kMaxWts + cc] = wgt;
-            S = fmaf(wgt, __ldcg(base + cc * ps + 1), S);
+            S = fmaf(wgt, __ldcg(base + cc * ps_ + 1), S);
         }
         S = warp_sum(S);
         if (lane == 0) { mlf[warp][0] = M; mlf[warp][1] = 1.0f / S; }
     }
     __syncthreads();
-    for (int i = tid; i < G * HD; i += 256) {
+    for (int i = tid; i < G * HD; i += NW * 32) {
         const int g = i / HD, d = i % HD;
-        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps;
+        const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks * ps_;
         float o = 0.0f;
 #pragma unroll 8
         for (int cc = 0; cc < nsplit; cc++) {
-            const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps) - mlf[g][0]);
-            o = fmaf(wgt, __ldcg(base + cc * ps + 2 + d), o);
+            const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps_) - mlf[g][0]);
+            o = fmaf(wgt, __ldcg(base + cc * ps_ + 2 + d), o);
         }
         L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * mlf[g][1];
     }
@@ -556,7 +581,7 @@ __global__ void __launch_bounds__(256, 1) attn_stream_kernel(AttnLayer L, const 
 
 template <int EPL, int G>
 static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, cudaStream_t st) {
-    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(256), attn_stream_smem<EPL, G>(), st, L, pos_dev, span));
+    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(512), attn_stream_smem<EPL, G>(), st, L, pos_dev, span));
     return G4_OK;
 }
 
@@ -597,8 +622,8 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     int rc;
     if (L.hd <= 256) {
         // split length: a power-of-two number of 32-row sub-chunks (1..8) so that the grid is about
-        // two CTAs per SM of work
-        long want = ((long)span * B * L.n_kv + (long)kSub * 296 - 1) / ((long)kSub * 296);
+        // four waves of one CTA per SM
+        long want = ((long)span * B * L.n_kv + (long)kSub * 592 - 1) / ((long)kSub * 592);
         int k = 1;
         while (k < want && k < 8) k <<= 1;
         const int sp = k * kSub;
