@@ -579,8 +579,12 @@ static int tc_scratch(int n, int d, TcScratchDev **out) {
         G4_CUDA(cudaDeviceGetAttribute(&S.nsm, cudaDevAttrMultiProcessorCount, dev));
         G4_TRY(prime_tc_attrs());
         G4_TRY(prime_tc6_attrs());
+        G4_TRY(prime_bf16tc_attrs());
     }
-    const size_t bq = std::max(tc_operand_bytes(n), tc6_operand_bytes(n)), part = tc_part_bytes(d, n, S.nsm);
+    const int tiles = (d + 127) / 128;
+    const size_t bq = std::max(std::max(tc_operand_bytes(n), tc6_operand_bytes(n)), bf16tc_operand_bytes((n + 63) / 64 * 64)),
+                 part = std::max(tc_part_bytes(d, n, S.nsm),
+                                 (size_t)std::max(1, std::min(n / 64, S.nsm / tiles)) * 64 * d * sizeof(float));
     const int nt = tc_tickets(d);
     if (bq > S.bq_bytes || part > S.part_bytes || nt > S.n_tickets) {
         G4_CUDA(cudaDeviceSynchronize());  // earlier calls may still use the old buffers
@@ -643,6 +647,21 @@ static int mm_tc6(float *o, const float *x, const void *w, int n, int d, int bat
     return G4_OK;
 }
 
+// BF16 rows against `batch` fp32 activations on the tensor cores.
+static int mm_tcbf(float *o, const float *x, const void *w, int n, int d, int batch, cudaStream_t st) {
+    TcScratchDev *S = nullptr;
+    G4_TRY(tc_scratch(n, d, &S));
+    CUtensorMap tm;
+    G4_TRY(bf16tc_weight_map(&tm, w, n, d));
+    for (int g0 = 0; g0 < batch; g0 += 64) {
+        const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
+        G4_TRY(launch_bf3_split(x + (size_t)g0 * n, n, gb, n, np, S->bq, st));
+        G4_TRY(launch_gemm_bf16tc(&tm, n, d, S->bq, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes, S->tickets,
+                                  nullptr, S->nsm, EPI_STORE, nullptr, 0, st));
+    }
+    return G4_OK;
+}
+
 extern "C" {
 
 int g4_set_tc_min_batch(int b) {
@@ -662,6 +681,7 @@ int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_b
         set_error(G4_ERR_ARG, "mm: x is NULL");
         return G4_ERR_ARG;
     }
+    if (type == G4_BF16 && batch >= g_tc_min_batch.load() && n % 64 == 0) return mm_tcbf(o, x, w, n, d, batch, st);
     if (type == G4_F32 || type == G4_F16 || type == G4_BF16)
         return launch_gemv_dense(w, type, n, d, x, n, o, d, batch, EPI_STORE, nullptr, 0, st);
     if (is_q8_type(type) && batch >= g_tc_min_batch.load()) return mm_tc(o, w, n, d, type, q8, batch, st);

@@ -81,7 +81,7 @@ struct g4_engine {
     // tensor-core path for the batched step (B >= tc_min_batch)
     struct alignas(64) MapBuf { unsigned char b[512]; };
     std::map<const void *, MapBuf> tmaps;  // tensor maps per weight matrix
-    uint8_t *tcq = nullptr, *tc6 = nullptr;  // B operands (Q4_K/Q5_K and Q6_K)
+    uint8_t *tcq = nullptr, *tc6 = nullptr, *tcb = nullptr;  // B operands (Q4_K/Q5_K, Q6_K, BF16)
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
     int *tc_tickets = nullptr;
@@ -188,7 +188,9 @@ bool is_kq(int t) { return t == G4_Q4_K || t == G4_Q5_K || t == G4_Q6_K; }
 
 // Whether a GEMM of this step runs on the tensor cores.
 bool use_tc(const g4_engine *e, int B, int type, int epi) {
-    if (!e->tcq || B < e->tc_min_batch || !is_kq(type)) return false;
+    if (!e->tcq || B < e->tc_min_batch) return false;
+    if (type == G4_BF16) return epi == EPI_STORE || epi == EPI_GELU_SCALE;
+    if (!is_kq(type)) return false;
     return epi == EPI_STORE || (epi == EPI_SOFTCAP_ARGMAX && type == G4_Q6_K);
 }
 
@@ -200,6 +202,8 @@ int tc_maps(g4_engine *e, const void *w, int type, int n, int rows, const void *
         if (type == G4_Q6_K) {
             if (tc6_maps_bytes() > sizeof(mb.b)) { set_error(G4_ERR_STATE, "tensor-map bundle size"); return G4_ERR_STATE; }
             TRY(tc6_weight_maps(mb.b, w, n, rows));
+        } else if (type == G4_BF16) {
+            TRY(bf16tc_weight_map(reinterpret_cast<CUtensorMap *>(mb.b), w, n, rows));
         } else {
             TRY(tc_weight_map(reinterpret_cast<CUtensorMap *>(mb.b), w, type, n, rows));
         }
@@ -213,14 +217,20 @@ int tc_maps(g4_engine *e, const void *w, int type, int n, int rows, const void *
 // to 64 sequences.  act_ready: the B operand of this activation is already
 // in place (same activation as the previous call of the same type class).
 int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float *act, int ld, bool act_ready,
-            float *out, int ldo, int B, int epi = EPI_STORE, unsigned long long *keys = nullptr, float cap = 0.0f) {
+            float *out, int ldo, int B, int epi = EPI_STORE, unsigned long long *keys = nullptr, float cap = 0.0f,
+            const float *evec = nullptr, int ld_evec = 0) {
     const void *maps = nullptr;
     TRY(tc_maps(e, w, type, n, rows, &maps));
     if (B > 64) act_ready = false;
     for (int g0 = 0; g0 < B; g0 += 64) {
         const int gb = B - g0 < 64 ? B - g0 : 64, np = tc_np(gb);
         float *o = out ? out + (size_t)g0 * ldo : nullptr;
-        if (type == G4_Q6_K) {
+        if (type == G4_BF16) {
+            if (!act_ready) TRY(launch_bf3_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tcb, e->st));
+            TRY(launch_gemm_bf16tc((const CUtensorMap *)maps, n, rows, e->tcb, gb, np, o, ldo, e->tc_part,
+                                   e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, epi,
+                                   evec ? evec + (size_t)g0 * ld_evec : nullptr, ld_evec, e->st));
+        } else if (type == G4_Q6_K) {
             float *ys = (float *)(e->tc6 + tc6_ys_offset(n));
             if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, e->st));
             TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, e->tc_part, e->tc_part_bytes,
@@ -239,7 +249,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
                        e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
-    if (use_tc(e, B, e->ple_proj_t, EPI_STORE))
+    if (use_tc(e, B, e->ple_proj_t, EPI_STORE) && (e->ple_proj_t != G4_BF16 || dim % 64 == 0))
         TRY(tc_gemm(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
     else
         TRY(gemv(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
@@ -349,9 +359,16 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         r3.eps = e->eps;
         TRY(launch_resnorm(r3, B, e->st));
         // per-layer embedding injection (1986-1997)
-        TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
-                 e->ple + (size_t)l * pd, pd * L));
-        TRY(gemv(e, ly.proj, ly.proj_t, pd, dim, e->g, pd, false, e->p_raw, dim, B));
+        if (use_tc(e, B, ly.inp_gate_t, EPI_GELU_SCALE) && (ly.inp_gate_t != G4_BF16 || dim % 64 == 0))
+            TRY(tc_gemm(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE, nullptr,
+                        0.0f, e->ple + (size_t)l * pd, pd * L));
+        else
+            TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
+                     e->ple + (size_t)l * pd, pd * L));
+        if (use_tc(e, B, ly.proj_t, EPI_STORE) && (ly.proj_t != G4_BF16 || pd % 64 == 0))
+            TRY(tc_gemm(e, ly.proj, ly.proj_t, pd, dim, e->g, pd, false, e->p_raw, dim, B));
+        else
+            TRY(gemv(e, ly.proj, ly.proj_t, pd, dim, e->g, pd, false, e->p_raw, dim, B));
     }
     // last residual + out_scale (1995-2003), output norm (2021)
     const LayerDev &last = e->layers[L - 1];
@@ -737,14 +754,18 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         size_t part = 0;
         int rows_max = e->vocab;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
-                                 {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}};
+                                 {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}, {pd, dim}, {dim, pd}};
         for (auto &sh : shapes) {
             part = std::max(part, tc_part_bytes(sh[0], sh[1], e->nsm));
+            // BF16 K-split: up to nsm / tiles slices of the whole row set
+            const int tiles = (sh[0] + 127) / 128;
+            part = std::max(part, (size_t)std::max(1, std::min(sh[1] / 64, e->nsm / tiles)) * 64 * sh[0] * sizeof(float));
             rows_max = std::max(rows_max, sh[0]);
         }
         nmax = (nmax + G4_QK - 1) / G4_QK * G4_QK;
         TRY(dalloc_t(e, &e->tcq, tc_operand_bytes(nmax)));
         TRY(dalloc_t(e, &e->tc6, tc6_operand_bytes(nmax)));
+        TRY(dalloc_t(e, &e->tcb, bf16tc_operand_bytes((nmax + 63) / 64 * 64)));
         e->tc_part_bytes = std::max(part, (size_t)16);
         TRY(dalloc_t(e, &e->tc_part, e->tc_part_bytes / sizeof(float)));
         TRY(dalloc_t(e, &e->tc_tickets, (size_t)tc_tickets(rows_max)));

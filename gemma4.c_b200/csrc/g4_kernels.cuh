@@ -102,6 +102,15 @@ int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, in
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
 int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st);
 
+// ---- batched BF16-weight GEMM on tcgen05 (k_gemm_bf16tc.cu), 16..64 sequences
+size_t bf16tc_operand_bytes(int n);
+int bf16tc_weight_map(CUtensorMap *m, const void *w, int n, int rows);
+int launch_bf3_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, cudaStream_t st);
+int launch_gemm_bf16tc(const CUtensorMap *tm, int n, int rows, const uint8_t *bq, int B, int np, float *out, int ldo,
+                       float *part, size_t part_bytes, int *tickets, int *err, int nsm, int epi, const float *evec,
+                       int ld_evec, cudaStream_t st);
+int prime_bf16tc_attrs();
+
 // ---- batched Q6_K GEMM on tcgen05 (k_gemm_q6tc.cu), 16..64 sequences
 size_t tc6_operand_bytes(int n);     // x1/x2 operand + scales of one activation (NP = 64)
 size_t tc6_ys_offset(int n);

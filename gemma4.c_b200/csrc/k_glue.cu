@@ -321,6 +321,7 @@ int prime_kernel_attrs() {
     if (rc) return rc;
     if ((rc = prime_tc_attrs())) return rc;
     if ((rc = prime_tc6_attrs())) return rc;
+    if ((rc = prime_bf16tc_attrs())) return rc;
     return prime_attn_attrs();
 }
 }  // namespace g4

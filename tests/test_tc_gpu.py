@@ -149,3 +149,42 @@ def test_tc_q6K_vs_gemv(gpu, torch_cuda, g4):
     o_sv = _run6(g4, torch_cuda, w, x, n, rows, tc_min=1 << 30)
     for s in range(B):
         assert_close(o_tc[s], o_sv[s], what="TC vs GEMV Q6K seq %d" % s)
+
+
+BF16 = 30
+
+
+@pytest.mark.parametrize("rows,n,B", [
+    (256, 2560, 64),     # per-layer-embedding gate shape
+    (2560, 256, 64),     # per-layer-embedding projection shape
+    (1000, 2560, 20),    # ragged tile, padding sequences
+    (130, 512, 70),      # two groups
+])
+def test_tc_bf16_vs_oracle(gpu, torch_cuda, orc, g4, rows, n, B):
+    """BF16 rows (mm_bf16, main.c:1520-1537): fp32 dot of x with bf16 weights, for B activations at once."""
+    from _tol import dense_term_scale
+    rng = np.random.default_rng(31 * rows + n + B)
+    wf = rng.standard_normal((rows, n)).astype(np.float32) * 0.05
+    w = ((wf.view(np.uint32) + 0x8000) >> 16).astype(np.uint16)  # round to bf16
+    deq = (w.astype(np.uint32) << 16).view(np.float32)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    x[1] *= 1e4
+    x[2] *= 1e-5
+    dev = torch_cuda.device("cuda:0")
+    wd = g4.weight_upload(w, BF16, n, rows)
+    try:
+        xd = torch_cuda.from_numpy(x).to(dev)
+        o = torch_cuda.full((B, rows), float("nan"), dtype=torch_cuda.float32, device=dev)
+        prev = g4.set_tc_min_batch(1)
+        try:
+            g4.mm_device(o.data_ptr(), xd.data_ptr(), wd, n, rows, BF16, 0, 0, B, torch_cuda.cuda.current_stream().cuda_stream)
+            torch_cuda.cuda.synchronize()
+        finally:
+            g4.set_tc_min_batch(prev)
+        o = o.cpu().numpy()
+    finally:
+        g4.free(wd)
+    assert np.isfinite(o).all()
+    for s in range(B):
+        e = orc.mm(x[s], w, n, rows, BF16)
+        assert_close(o[s], e, dense_term_scale(deq, x[s]), what="TC BF16 seq %d" % s)
