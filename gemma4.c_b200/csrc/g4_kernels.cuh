@@ -133,6 +133,8 @@ size_t tc_yd_offset(int n);          // where the block scales start inside that
 TcPlan tc_plan(int rows, int nb, int nsm);
 size_t tc_part_bytes(int rows, int n, int nsm);
 int tc_tickets(int rows);
+int launch_tc_merge(const float *part, int ksplit, int np, int rows, int B, float *out, int ldo, int epi,
+                    const float *evec, int ld_evec, cudaStream_t st);
 int tc_weight_map(CUtensorMap *m, const void *w, int type, int n, int rows);
 int launch_tc_quant(int type, const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
 int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);

@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) gemm_bf16tc_kernel(const __grid
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.acc_empty[abuf]);
-            (void)rt;  // split tiles: the partials are summed by bf16_merge_kernel
+            (void)rt;  // split tiles: the partials are summed by tc_merge_kernel
         }
         if (!ok) bf_fail(S, a.err);
     }
@@ -242,21 +242,6 @@ __global__ void bf3_split_kernel(const float *__restrict__ x, int ldx, int B, in
     for (int q = 0; q < 3; q++)
         *reinterpret_cast<uint32_t *>(blk + (k >> 3) * (3 * NP * 16) + (q * NP + s) * 16 + (k & 7) * 2) =
             (uint32_t)p0[q] | ((uint32_t)p1[q] << 16);
-}
-
-// Sum of the K-slice partials in slice order (+ the GELU-scale epilogue):
-// one thread per (sequence, row).
-__global__ void bf16_merge_kernel(const float *__restrict__ part, int ksplit, int NP, int rows, int B,
-                                  float *__restrict__ out, int ldo, int epi, const float *__restrict__ evec, int ld_evec) {
-    pdl_trigger();
-    pdl_wait();
-    const int row = blockIdx.x * blockDim.x + threadIdx.x, s = blockIdx.y;
-    if (row >= rows || s >= B) return;
-    float v = 0.0f;
-    for (int k = 0; k < ksplit; k++) v += part[((size_t)k * NP + s) * rows + row];
-    if (epi == EPI_GELU_SCALE)
-        v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * v * (1.0f + 0.044715f * v * v))) * evec[(size_t)s * ld_evec + row];
-    out[(size_t)s * ldo + row] = v;
 }
 
 template <int NP>
@@ -317,11 +302,7 @@ int launch_gemm_bf16tc(const CUtensorMap *tm, int n, int rows, const uint8_t *bq
     G4_BFTC_CASE(16) else G4_BFTC_CASE(32) else G4_BFTC_CASE(64)
 #undef G4_BFTC_CASE
     G4_LAUNCHED();
-    if (p.ksplit > 1) {
-        G4_CUDA(launch_pdl(bf16_merge_kernel, dim3((rows + 127) / 128, B), dim3(128), 0, st, (const float *)part, p.ksplit,
-                           np, rows, B, out, ldo, epi, evec, ld_evec));
-        G4_LAUNCHED();
-    }
+    if (p.ksplit > 1) return launch_tc_merge(part, p.ksplit, np, rows, B, out, ldo, epi, evec, ld_evec, st);
     return G4_OK;
 }
 

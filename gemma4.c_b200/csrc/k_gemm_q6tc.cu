@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                 if (seq + 1 < a.B) a.out[(size_t)(seq + 1) * a.ldo + row] = v1;
             }
         };
-        auto finish = [&](int u) {
-            const int rt = u / a.ksplit, ks = u % a.ksplit, row = rt * 128 + r;
+        auto finish = [&](int u) {  // final values, or this K slice's partial (summed by tc_merge_kernel)
+            const int ks = u % a.ksplit, row = (u / a.ksplit) * 128 + r;
             if (a.ksplit == 1) {
 #pragma unroll
                 for (int s = 0; s < SP / 2; s++) {
@@ -361,30 +361,6 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                 }
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&a.tickets[rt * 8 + pw], 1) == a.ksplit - 1;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) return;
-            __threadfence();  // the last slice sums all slices of the tile, in slice order
-            if (row < a.rows)
-                for (int k = 0; k < a.ksplit; k++)
-#pragma unroll
-                    for (int s = 0; s < SP / 2; s++) {
-                        const int seq = p * SP + 2 * s;
-                        const float *src = a.part + ((size_t)k * NP + seq) * a.rows + row;
-                        const float l0 = seq < a.B ? __ldcg(src) : 0.0f;
-                        const float l1 = seq + 1 < a.B ? __ldcg(src + a.rows) : 0.0f;
-                        acc[s] = f2_add(acc[s], f2_pack(l0, l1));
-                    }
-#pragma unroll
-            for (int s = 0; s < SP / 2; s++) {
-                const float2 f = f2_unpack(acc[s]);
-                emit(row, s, f.x, f.y);
-                acc[s] = 0ull;
-            }
-            if (lane == 0) a.tickets[rt * 8 + pw] = 0;
         };
         int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
         float ndw = 0.f, nyl = 0.f;
@@ -536,7 +512,11 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
     if (epi != EPI_STORE && epi != EPI_SOFTCAP_ARGMAX) { set_error(G4_ERR_ARG, "q6 tc gemm: epilogue %d", epi); return G4_ERR_ARG; }
     if (epi == EPI_SOFTCAP_ARGMAX && !keys) { set_error(G4_ERR_ARG, "q6 tc gemm: argmax keys missing"); return G4_ERR_ARG; }
     const int nb = n / G4_QK;
-    const TcPlan p = tc_plan(rows, nb, nsm);
+    TcPlan p = tc_plan(rows, nb, nsm);
+    if (epi == EPI_SOFTCAP_ARGMAX) {  // the argmax epilogue needs whole rows: no K split
+        const int tiles = (rows + 127) / 128;
+        p = TcPlan{1, nb, tiles, tiles < nsm ? tiles : nsm};
+    }
     if (p.ksplit > 1 && (size_t)p.ksplit * np * rows * sizeof(float) > part_bytes) {
         set_error(G4_ERR_ARG, "q6 tc gemm: partial buffer too small");
         return G4_ERR_ARG;
@@ -551,6 +531,7 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
     G4_Q6TC_CASE(16) else G4_Q6TC_CASE(32) else G4_Q6TC_CASE(64)
 #undef G4_Q6TC_CASE
     G4_LAUNCHED();
+    if (p.ksplit > 1) return launch_tc_merge(part, p.ksplit, np, rows, B, out, ldo, EPI_STORE, nullptr, 0, st);
     return G4_OK;
 }
 

@@ -268,41 +268,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
             return true;
         };
-        // slices of one 128-row tile: store, or write a partial and let the last warp sum them
+        // slices of one 128-row tile: store, or write this K slice's partial (summed by tc_merge_kernel)
         auto finish = [&](int u) {
-            const int rt = u / a.ksplit, ks = u % a.ksplit, row = rt * 128 + r;
-            if (a.ksplit == 1) {
-                if (row < a.rows)
+            const int ks = u % a.ksplit, row = (u / a.ksplit) * 128 + r;
+            float *dst = a.ksplit == 1 ? a.out : a.part + (size_t)ks * NP * a.rows;
+            const size_t ld = a.ksplit == 1 ? (size_t)a.ldo : (size_t)a.rows;
+            if (row < a.rows)
 #pragma unroll
-                    for (int s = 0; s < HALF; s++) {
-                        const int seq = cb * HALF + s;
-                        if (seq < a.B) a.out[(size_t)seq * a.ldo + row] = acc[s];
-                    }
-            } else {
-                if (row < a.rows)
-#pragma unroll
-                    for (int s = 0; s < HALF; s++) {
-                        const int seq = cb * HALF + s;
-                        if (seq < a.B) a.part[((size_t)ks * NP + seq) * a.rows + row] = acc[s];
-                    }
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) last = atomicAdd(&a.tickets[rt * kTcMathWarps + mw], 1) == a.ksplit - 1;
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    if (row < a.rows)
-                        for (int s = 0; s < HALF; s++) {
-                            const int seq = cb * HALF + s;
-                            if (seq >= a.B) break;
-                            float v = 0.0f;
-                            for (int k = 0; k < a.ksplit; k++) v += __ldcg(a.part + ((size_t)k * NP + seq) * a.rows + row);
-                            a.out[(size_t)seq * a.ldo + row] = v;
-                        }
-                    if (lane == 0) a.tickets[rt * kTcMathWarps + mw] = 0;
+                for (int s = 0; s < HALF; s++) {
+                    const int seq = cb * HALF + s;
+                    if (seq < a.B) dst[(size_t)seq * ld + row] = acc[s];
                 }
-            }
 #pragma unroll
             for (int s = 0; s < HALF; s++) acc[s] = 0.0f;
         };
@@ -736,8 +712,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
             dm = f16_to_f32((uint16_t)(m >> 16));
             yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
         };
-        auto finish = [&](int u) {
-            const int rt = u / a.ksplit, ks = u % a.ksplit, row = rt * 128 + r;
+        auto finish = [&](int u) {  // final values, or this K slice's partial (summed by tc_merge_kernel)
+            const int ks = u % a.ksplit, row = (u / a.ksplit) * 128 + r;
             float *dst = a.ksplit == 1 ? a.out : a.part + (size_t)ks * NP * a.rows;
             const size_t ld = a.ksplit == 1 ? (size_t)a.ldo : (size_t)a.rows;
             if (row < a.rows)
@@ -750,35 +726,6 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                 }
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
-            if (a.ksplit == 1) return;
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&a.tickets[rt * 8 + pw], 1) == a.ksplit - 1;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) return;
-            // the last slice to finish sums all slices of this tile, in slice order
-            __threadfence();
-            if (row < a.rows) {
-                for (int k = 0; k < a.ksplit; k++)
-#pragma unroll
-                    for (int s = 0; s < SP / 2; s++) {
-                        const int seq = p * SP + 2 * s;
-                        const float *src = a.part + ((size_t)k * NP + seq) * a.rows + row;
-                        const float l0 = seq < a.B ? __ldcg(src) : 0.0f;
-                        const float l1 = seq + 1 < a.B ? __ldcg(src + a.rows) : 0.0f;
-                        acc[s] = f2_add(acc[s], f2_pack(l0, l1));
-                    }
-#pragma unroll
-                for (int s = 0; s < SP / 2; s++) {
-                    const float2 f = f2_unpack(acc[s]);
-                    const int seq = p * SP + 2 * s;
-                    if (seq < a.B) a.out[(size_t)seq * a.ldo + row] = f.x;
-                    if (seq + 1 < a.B) a.out[(size_t)(seq + 1) * a.ldo + row] = f.y;
-                    acc[s] = 0ull;
-                }
-            }
-            if (lane == 0) a.tickets[rt * 8 + pw] = 0;
         };
         // first block
         int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
@@ -946,8 +893,8 @@ TcPlan tc_plan(int rows, int nb, int nsm) {
     for (int ks = 1; ks <= nb; ks++) {
         const int ksplit = (nb + ks - 1) / ks;
         const int units = tiles * ksplit, grid = min(units, nsm), waves = (units + grid - 1) / grid;
-        // per unit: pipeline fill, plus fence/ticket/merge when the tile is split
-        const double cost = waves * (ks + (ksplit > 1 ? 3.0 : 1.0));
+        // in block times: per unit pipeline fill and partial store, per split one merge pass
+        const double cost = waves * (ks + 1.5) + (ksplit > 1 ? 3.0 : 0.0);
         if (cost < best_cost - 1e-9 || (fabs(cost - best_cost) < 1e-9 && ks > best.kslice)) {
             best_cost = cost;
             best = TcPlan{ksplit, ks, units, grid};
@@ -1012,6 +959,31 @@ int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int ro
 #undef G4_Q4TC_CASE
     (void)k;
     (void)smem;
+    G4_LAUNCHED();
+    if (p.ksplit > 1) return launch_tc_merge(part, p.ksplit, np, rows, B, out, ldo, EPI_STORE, nullptr, 0, st);
+    return G4_OK;
+}
+
+// Sum of the K-slice partials part[k][s][row] in slice order, then the
+// epilogue (store, or GELU(acc) * evec for the per-layer-embedding gate):
+// one thread per (sequence, row).
+__global__ void tc_merge_kernel(const float *__restrict__ part, int ksplit, int NP, int rows, int B,
+                                float *__restrict__ out, int ldo, int epi, const float *__restrict__ evec, int ld_evec) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x * blockDim.x + threadIdx.x, s = blockIdx.y;
+    if (row >= rows || s >= B) return;
+    float v = 0.0f;
+    for (int k = 0; k < ksplit; k++) v += part[((size_t)k * NP + s) * rows + row];
+    if (epi == EPI_GELU_SCALE)
+        v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * v * (1.0f + 0.044715f * v * v))) * evec[(size_t)s * ld_evec + row];
+    out[(size_t)s * ldo + row] = v;
+}
+
+int launch_tc_merge(const float *part, int ksplit, int np, int rows, int B, float *out, int ldo, int epi,
+                    const float *evec, int ld_evec, cudaStream_t st) {
+    G4_CUDA(launch_pdl(tc_merge_kernel, dim3((rows + 127) / 128, B), dim3(128), 0, st, part, ksplit, np, rows, B, out, ldo,
+                       epi, evec, ld_evec));
     G4_LAUNCHED();
     return G4_OK;
 }
