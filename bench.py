@@ -65,10 +65,13 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during a region."""
+    """SM clocks and clock-event (throttle) reasons sampled during a region:
+    NVML every 20 ms (read-only queries), else nvidia-smi every 200 ms."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits, in the order of the summary's names
+    BITS = (0x8, 0x40, 0x20, 0x4)  # hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
@@ -76,7 +79,35 @@ class ClockSampler:
         self._stop = threading.Event()
         self._t = None
 
+    def _run_nvml(self) -> bool:
+        try:
+            import pynvml as N
+            N.nvmlInit()
+        except Exception:
+            return False
+        try:
+            h = N.nvmlDeviceGetHandleByIndex(self.idx)
+            mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                rs = get_reasons(h)
+                self.rows.append([str(self.idx), str(sm), str(mx), "", hex(rs)] +
+                                 ["Active" if rs & b else "Not Active" for b in self.BITS])
+                self._stop.wait(0.02)
+            return True
+        except Exception:
+            return bool(self.rows)
+        finally:
+            try:
+                N.nvmlShutdown()
+            except Exception:
+                pass
+
     def _run(self):
+        if self._run_nvml():
+            return
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.Q,
@@ -168,6 +199,42 @@ def reference_sample(g4, model, ctx: int, n_steps: int, threads: int):
     dt = time.perf_counter() - t0
     rm.close()
     return n_steps / dt, dt, ref.max_threads, ref.blas
+
+
+# ---------------------------------------------------------------- attention roofline
+# DRAM bytes (read + write) per launch over the algorithmic K/V bytes, from
+# one ncu capture of each layer kind in the batch-64 E4B case
+# (gemma4.c_b200/kernel_cases.py attn; profiles/attn_stream_e4b_b64.md):
+# sliding (134.90 + 5.57) MB / 134.22 MB, global at context 2048
+# (537.72 + 7.00) MB / 536.87 MB.  The excess is the split partials.
+ATTN_TRAFFIC_RATIO = {"sliding": 1.0465, "global": 1.0146}
+
+
+def attention_roofline(eng, shape, B: int, pos: int, reps: int = 4):
+    """Decode attention (attn_stream_kernel) of the engine's own layers at the
+    current position, timed with CUDA events on the engine stream.  Sliding
+    and global layers are timed separately (five sliding layers in rotation so
+    that their 5 x 134 MB of K/V exceed L2) and combined with the step's mix
+    of layer kinds.  Algorithmic bytes per launch = the K and V rows read:
+    B * n_kv * nwin * hd * 4 B * 2."""
+    S_ = sys.modules["g4b200"].synth
+    swa = [l for l in range(shape.n_layers) if S_.is_swa(shape, l)]
+    glob = [l for l in range(shape.n_layers) if not S_.is_swa(shape, l)]
+    nwin_s = min(pos + 1, shape.sliding_window)
+    nwin_g = pos + 1
+    by_s = B * shape.n_kv_heads * nwin_s * shape.head_dim_swa * 8
+    by_g = B * shape.n_kv_heads * nwin_g * shape.head_dim_full * 8
+    ts = eng.time_attention(swa[:5], B, reps) / (reps * min(5, len(swa)))
+    tg = eng.time_attention(glob[:2], B, reps) / (reps * min(2, len(glob)))
+    step_bytes = len(swa) * by_s + len(glob) * by_g
+    step_traffic = ATTN_TRAFFIC_RATIO["sliding"] * len(swa) * by_s + ATTN_TRAFFIC_RATIO["global"] * len(glob) * by_g
+    step_ms = len(swa) * ts + len(glob) * tg
+    return {"sliding": {"us_per_launch": 1e3 * ts, "bytes_per_launch": by_s, "gbs": by_s / (ts * 1e-3) / 1e9,
+                        "launches_per_step": len(swa)},
+            "global": {"us_per_launch": 1e3 * tg, "bytes_per_launch": by_g, "gbs": by_g / (tg * 1e-3) / 1e9,
+                       "launches_per_step": len(glob)},
+            "step_ms": step_ms, "step_bytes": step_bytes, "step_traffic_bytes": step_traffic,
+            "gbs": step_bytes / (step_ms * 1e-3) / 1e9}
 
 
 # ---------------------------------------------------------------- GEMV roofline
@@ -270,7 +337,7 @@ def config0_gemv(g4, reps: int = 20, rows: int = 10240):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--workload", default="batch64", choices=["batch64", "batch1", "gemv0"])
@@ -396,9 +463,14 @@ def main():
            "d2h_bytes_per_step": 4 * B, "api": "g4_decode_batch (host token ids in, host next ids out)"}
 
     hbm_peak, tc_peak, peak_kind = measured_peaks()
+    if B >= 9:  # the engine's tensor-core threshold (engine.cu tc_min_batch)
+        dtype = ("tensor cores: Q4_K as exact fp16 integer products, Q5_K int8 x int8 -> int32, Q6_K and BF16 "
+                 "on split-fp32 activations (fp16 x2 / bf16 x3) -> fp32; fp32 attention, KV cache and norms")
+    else:
+        dtype = "int8 x int4/int5 dp4a -> int32 (Q4_K/Q5_K x Q8_K), fp32 (Q6_K, dense, attention, norms)"
     out = {"metric": metric, "value": value, "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True, "scaling": "strong",
-           "vs_baseline": None, "dtype": "int8xint4/int32 dots + fp32 (Q6_K, norms, attention)",
+           "vs_baseline": None, "dtype": dtype,
            "data": "synthetic (seeded random-init model and prompts)", "config": cfg,
            "e2e": e2e, "gpu_launches": int(kernels_per_step * a.steps),
            "kernels_per_step": kernels_per_step, "prefill_s": prefill_s,
@@ -406,11 +478,29 @@ def main():
     if dist.rank == 0 and not a.no_extras:
         rl = gemv_roofline(g4, B)
         lay = rl["layer"]
-        out["roofline"] = {"kernel": "gemv_kquant_kernel (config-1 layer matrices, batch %d)" % B, "bound": "hbm",
-                           "achieved": lay["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": lay["gbs"] / hbm_peak,
-                           "peak_kind": peak_kind, "traffic": None,
-                           "algorithmic_bytes_per_launch": lay["bytes_per_launch"],
-                           "us_per_launch": lay["us_per_launch"], "parts": rl}
+        gemm_kernel = ("tensor-core GEMMs gemm_q4tc_kernel / gemm_q6tc_kernel with their operand and merge kernels"
+                       if B >= 16 else "gemv_tma_kernel (streaming K-quant GEMV)")
+        gemm = {"kernel": gemm_kernel + ", config-1 layer matrices at batch %d" % B, "bound": "hbm",
+                "achieved": lay["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": lay["gbs"] / hbm_peak,
+                "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": lay["bytes_per_launch"],
+                "us_per_launch": lay["us_per_launch"], "parts": rl}
+        if B >= 16:  # batched decode: attention over 64 x 4096 fp32 K/V rows is the dominant kernel
+            at = attention_roofline(eng, S.E4B, B, pos - 1)
+            nl = at["sliding"]["launches_per_step"] + at["global"]["launches_per_step"]
+            out["roofline"] = {"kernel": "attn_stream_kernel (decode attention, %d sequences, context %d)"
+                                         % (B, pos), "bound": "hbm", "achieved": at["gbs"], "peak": hbm_peak,
+                               "unit": "GB/s", "frac": at["gbs"] / hbm_peak, "peak_kind": peak_kind,
+                               "traffic": at["step_traffic_bytes"] / nl,
+                               "algorithmic_bytes_per_launch": at["step_bytes"] / nl,
+                               "us_per_launch": 1e3 * at["step_ms"] / nl, "parts": at}
+            out["gemm_roofline"] = gemm
+            # the whole step against HBM: weights once + every layer's K/V rows
+            sb = wbytes + at["step_bytes"]
+            out["step_roofline"] = {"bound": "hbm", "algorithmic_bytes_per_step": sb,
+                                    "achieved": sb / (ms_max / a.steps * 1e-3) / 1e9, "peak": hbm_peak,
+                                    "unit": "GB/s", "frac": sb / (ms_max / a.steps * 1e-3) / 1e9 / hbm_peak}
+        else:
+            out["roofline"] = gemm
         out["q4k_gemv_config0"] = config0_gemv(g4)
         out["q4k_gemv_config0"]["frac"] = out["q4k_gemv_config0"]["gbs"] / hbm_peak
         out["step_hbm_gbs"] = wbytes / (ms_max / a.steps * 1e-3) / 1e9

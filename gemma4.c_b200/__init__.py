@@ -83,6 +83,7 @@ SIGNATURES = [
     ("g4_engine_get_kv", ip, [vp, ip, ip, ip, vp, vp]),
     ("g4_engine_last_step_kernels", ip, [vp]),
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
+    ("g4_engine_time_attention", ip, [vp, vp, ip, ip, ip, vp]),
     ("g4_set_tc_min_batch", ip, [ip]),
 ]
 
@@ -286,6 +287,13 @@ class Engine:
 
     def fill_kv(self, npos: int, seed: int = 1):
         _check(lib().g4_engine_fill_kv(self.h, npos, seed))
+
+    def time_attention(self, layers, batch: int, reps: int) -> float:
+        """Milliseconds for `reps` rounds of the attention of `layers` (CUDA events, engine stream)."""
+        ls = np.ascontiguousarray(layers, dtype=np.int32)
+        ms = np.zeros(1, np.float32)
+        _check(lib().g4_engine_time_attention(self.h, _p(ls), len(ls), batch, reps, _p(ms)))
+        return float(ms[0])
 
     def last_step_kernels(self) -> int:
         return int(lib().g4_engine_last_step_kernels(self.h))

@@ -245,6 +245,24 @@ int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float 
     return G4_OK;
 }
 
+// Attention of layer l at the engine's current position: q/k/v raw projections in, the new K/V row
+// normed, rotated and appended (layers that own a cache), qo out (main.c:1886-1950).
+static AttnLayer attn_args(const g4_engine *e, int l) {
+    const LayerDev &ly = e->layers[l];
+    AttnLayer A{};
+    A.hd = ly.hd; A.n_rot = ly.n_rot; A.n_heads = e->nh; A.n_kv = e->nkv;
+    A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
+    A.q_norm = ly.q_norm; A.k_norm = ly.k_norm;
+    A.rope = ly.swa ? e->rope_swa : e->rope_full;
+    A.append = l < G4_N_LAYER_KV; A.kc = ly.kc; A.vc = ly.vc; A.ring = ly.ring;
+    const LayerDev &src = e->layers[ly.src];
+    A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
+    A.window = ly.swa ? e->window : 0;
+    A.eps = e->eps; A.err = e->d_err;
+    A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
+    return A;
+}
+
 int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
@@ -304,18 +322,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                 TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
 
         // attention (main.c:1886-1950)
-        AttnLayer A{};
-        A.hd = ly.hd; A.n_rot = ly.n_rot; A.n_heads = e->nh; A.n_kv = e->nkv;
-        A.q_norm = ly.q_norm; A.k_norm = ly.k_norm;
-        A.rope = ly.swa ? e->rope_swa : e->rope_full;
-        A.append = has_kv; A.kc = ly.kc; A.vc = ly.vc; A.ring = ly.ring;
-        const LayerDev &src = e->layers[ly.src];
-        A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
-        A.window = ly.swa ? e->window : 0;
-        A.eps = e->eps; A.err = e->d_err;
-        A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
-        A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
-        TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
+        TRY(launch_attention(attn_args(e, l), B, e->d_pos, e->max_seq, e->st));
 
         // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
         if (use_tc(e, B, ly.wo_t, EPI_STORE))
@@ -467,18 +474,7 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
             }
         flip();  // cur = x after the PLE residual of layer l-1
 
-        AttnLayer A{};
-        A.hd = ly.hd; A.n_rot = ly.n_rot; A.n_heads = e->nh; A.n_kv = e->nkv;
-        A.q = e->q; A.k = e->k; A.v = e->v; A.prep = 1;
-        A.q_norm = ly.q_norm; A.k_norm = ly.k_norm;
-        A.rope = ly.swa ? e->rope_swa : e->rope_full;
-        A.append = has_kv; A.kc = ly.kc; A.vc = ly.vc; A.ring = ly.ring;
-        const LayerDev &src = e->layers[ly.src];
-        A.src_kc = src.kc; A.src_vc = src.vc; A.src_ring = src.ring;
-        A.window = ly.swa ? e->window : 0;
-        A.eps = e->eps; A.err = e->d_err;
-        A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
-        TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
+        TRY(launch_attention(attn_args(e, l), B, e->d_pos, e->max_seq, e->st));
 
         // O projection: the Q8_K quantization of qo is its prologue
         Prologue po{};
@@ -917,6 +913,36 @@ int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed) {
     }
     G4_CUDA(cudaStreamSynchronize(e->st));
     return G4_OK;
+}
+
+int g4_engine_time_attention(g4_engine *e, const int *layers, int n, int batch, int reps, float *ms) {
+    if (!e || !layers || n <= 0 || batch <= 0 || batch > e->max_batch || reps <= 0 || !ms) {
+        set_error(G4_ERR_ARG, "time_attention: bad arguments");
+        return G4_ERR_ARG;
+    }
+    for (int i = 0; i < n; i++)
+        if (layers[i] < 0 || layers[i] >= e->L) { set_error(G4_ERR_ARG, "time_attention: layer %d", layers[i]); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    G4_CUDA(cudaSetDevice(e->device));
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    cudaError_t ce = cudaEventCreate(&t0);
+    if (ce == cudaSuccess) ce = cudaEventCreate(&t1);
+    if (ce == cudaSuccess) ce = cudaEventRecord(t0, e->st);
+    int rc = ce == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+    for (int r = 0; r < reps && rc == G4_OK; r++)  // launch_attention records its own error text
+        for (int i = 0; i < n && rc == G4_OK; i++) rc = launch_attention(attn_args(e, layers[i]), batch, e->d_pos, e->max_seq, e->st);
+    if (rc == G4_OK) {
+        ce = cudaEventRecord(t1, e->st);
+        if (ce == cudaSuccess) ce = cudaEventSynchronize(t1);
+        if (ce == cudaSuccess) ce = cudaEventElapsedTime(ms, t0, t1);
+        if (ce != cudaSuccess) rc = G4_ERR_CUDA;
+    }
+    if (ce != cudaSuccess) set_error(G4_ERR_CUDA, "time_attention: %s", cudaGetErrorString(ce));
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
+    if (rc) return rc;
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return err_after_sync(e);
 }
 
 int g4_engine_get_hidden(g4_engine *e, int b, float *x) {

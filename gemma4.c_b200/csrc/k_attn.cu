@@ -329,20 +329,23 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
 // ---------------------------------------------------------------- streaming variant (head dim <= 256)
 //
 // One CTA per (split of `span` positions, kv head, sequence), span a multiple
-// of 32 chosen so that the grid is about two waves: the split is streamed in
-// sub-chunks of 32 rows through a two-stage shared-memory ring filled by bulk
-// copies (TMA), so the copy of sub-chunk j+1 overlaps the arithmetic of j.
-// Each warp keeps an online softmax state (max, sum, unnormalised P.V) per
-// query head over the rows it owns; the 8 warp states are combined once at
-// the end, then the split partials are merged by the last CTA of the (kv
-// head, sequence) as in attn_fused_kernel.
-constexpr int kSub = 32;
-constexpr int kStages = 3;  // ~128 KB of K/V in flight per SM at head dim 256
+// of 32 chosen so that the grid is about four waves: the split is streamed in
+// sub-chunks of kSub rows through a kStages-deep shared-memory ring filled by
+// bulk copies (TMA), so the copies of the next sub-chunks overlap the
+// arithmetic of this one.  Two CTAs share an SM, so one CTA's prologue and
+// merge tail overlap the other's streaming.  Each warp keeps an online
+// softmax state (max, sum, unnormalised P.V) per query head over the rows it
+// owns; the warp states are combined once at the end, then the split partials
+// are merged by the last CTA of the (kv head, sequence) as in
+// attn_fused_kernel.
+constexpr int kSub = 16;        // rows per ring stage
+constexpr int kStages = 3;      // 96 KB of K/V per CTA at head dim 256
+constexpr int kStreamWarps = 8;
 
 template <int EPL, int G>
 constexpr size_t attn_stream_smem() {
     return sizeof(float) * ((size_t)G * EPL * 32 + 2 * (size_t)EPL * 32 + 2 * kStages * (size_t)kSub * EPL * 32 +
-                            (size_t)16 * G * 2 + (size_t)G * kMaxWts);
+                            (size_t)kStreamWarps * G * 2 + (size_t)G * kMaxWts);
 }
 
 // Sum of NV = 2^H values per lane over the 32 lanes of a warp with 31 - H
@@ -369,8 +372,9 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
 }
 
 template <int EPL, int G>
-__global__ void __launch_bounds__(512, 1) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
-    constexpr int HD = EPL * 32, NW = 16, RPW = kSub / NW, NV = RPW * G;
+__global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
+    constexpr int HD = EPL * 32, NW = kStreamWarps, RPW = kSub / NW, NV = RPW * G;
+    static_assert(RPW == 2, "two rows per warp and sub-chunk: rows differ in lane bit 4 after the transpose sum");
     constexpr int H = NV == 2 ? 1 : NV == 4 ? 2 : 3;  // log2(NV)
     extern __shared__ __align__(16) float dsm[];
     float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(dsm);  // [G][HD]
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(512, 1) attn_stream_kernel(AttnLayer L, const 
     const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
     const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
 
-    // rows [beg + 32j, +cnt) of the split (ring slots, split at a wrap) -> stage j % kStages.  Row `pos`
+    // rows [beg + kSub*j, +cnt) of the split (ring slots, split at a wrap) -> stage j % kStages.  Row `pos`
     // of a layer that appends is (re)written below; its stale slot may be read here and is ignored.
     auto issue = [&](int j) {
         const int st = j % kStages, cnt = min(kSub, ctot - j * kSub);
@@ -581,7 +585,8 @@ __global__ void __launch_bounds__(512, 1) attn_stream_kernel(AttnLayer L, const 
 
 template <int EPL, int G>
 static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, cudaStream_t st) {
-    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(512), attn_stream_smem<EPL, G>(), st, L, pos_dev, span));
+    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(kStreamWarps * 32), attn_stream_smem<EPL, G>(), st, L,
+                       pos_dev, span));
     return G4_OK;
 }
 
@@ -621,12 +626,13 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     dim3 grid(nch, L.n_kv, B);
     int rc;
     if (L.hd <= 256) {
-        // split length: a power-of-two number of 32-row sub-chunks (1..8) so that the grid is about
-        // four waves of one CTA per SM
-        long want = ((long)span * B * L.n_kv + (long)kSub * 592 - 1) / ((long)kSub * 592);
+        // split length: a power-of-two number (1..8) of kChunk rows so that the grid is about four
+        // waves of two CTAs per SM (kChunk-row splits keep the partials within max_chunks)
+        const long slots = 4L * 2 * 148;
+        long want = ((long)span * B * L.n_kv + kChunk * slots - 1) / (kChunk * slots);
         int k = 1;
         while (k < want && k < 8) k <<= 1;
-        const int sp = k * kSub;
+        const int sp = k * kChunk;
         const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
         switch (L.hd) {
         case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;

@@ -265,6 +265,13 @@ void *g4_engine_stream(g4_engine *e);
  * cached values).  Not part of the reference interface. */
 int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed);
 
+/* Benchmark helper: time `reps` rounds of the decode attention of layers[0..n)
+ * (in that order) for the first `batch` sequences at the position of the most
+ * recent step, on the engine stream with CUDA events; *ms = total milliseconds.
+ * Re-running a step's attention rewrites the same K/V row, so the engine state
+ * is unchanged.  Not part of the reference interface. */
+int g4_engine_time_attention(g4_engine *e, const int *layers, int n, int batch, int reps, float *ms);
+
 /* Number of kernels in the most recent step (the nodes of its CUDA graph). */
 int g4_engine_last_step_kernels(const g4_engine *e);
 
