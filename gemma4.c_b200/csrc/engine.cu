@@ -260,6 +260,10 @@ static AttnLayer attn_args(const g4_engine *e, int l) {
     A.window = ly.swa ? e->window : 0;
     A.eps = e->eps; A.err = e->d_err;
     A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
+    // Steps run as whole CUDA graphs in stream order, so every cache row but `pos` was written by an
+    // earlier graph launch (or fill_kv) that has completed; row `pos` of a shared-KV source is
+    // written by an earlier kernel of this step and is only read after the dependency wait.
+    A.early = 1;
     return A;
 }
 

@@ -69,6 +69,9 @@ struct AttnLayer {
     float *part;                    // scratch [B][n_heads][max_chunks][hd+2]
     int *counters;                  // [B][n_kv] zero-initialised tickets
     int max_chunks;
+    int early;                      // 1: every cache row but `pos` was written before the launch's
+                                    //    stream predecessor started (earlier graph launches), so it
+                                    //    may be copied before the grid dependency wait
 };
 int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq, cudaStream_t st);
 int attn_chunk_size();

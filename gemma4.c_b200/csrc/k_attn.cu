@@ -21,6 +21,7 @@
 // sum, unnormalised output) are merged by the last CTA to finish.
 // The position is read from device memory so one CUDA graph serves all
 // positions; the grid covers the largest window and idle chunks exit.
+#include <algorithm>
 #include <math.h>
 
 #include "g4_async.cuh"
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     __shared__ int ticket;
     __shared__ float mlf[G][2];
     pdl_trigger();
-    pdl_wait();
+    if (!L.early) pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pos = *pos_dev;
@@ -416,11 +417,21 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
             bulk_g2s(vb + n1 * HD, L.src_vc + head_base * HD, (uint32_t)(cnt - n1) * rb, &full[st]);
         }
     };
+    // Sub-chunk j may be copied before the dependency wait (L.early) unless it holds row `pos` of a
+    // cache that an earlier kernel of this step writes (a layer without its own cache reads row
+    // `pos` of layer 22/23).  Row `pos` of a layer that appends comes from knew/vnew instead.
+    auto early_ok = [&](int j) { return L.append || c != nsplit - 1 || (j + 1) * kSub < ctot; };
     if (tid == 0) {
         for (int k = 0; k < kStages; k++) mbar_init(&full[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int k = 0; k < kStages && k < nsub; k++) issue(k);
+        if (L.early)
+            for (int k = 0; k < kStages && k < nsub; k++)
+                if (early_ok(k)) issue(k);
     }
+    if (L.early) pdl_wait();
+    if (tid == 0)
+        for (int k = 0; k < kStages && k < nsub; k++)
+            if (!L.early || !early_ok(k)) issue(k);
     // query heads (and the new K/V row) into shared memory
     if (warp < G) {
         const float *src = L.q + (size_t)b * qd + (size_t)(h * G + warp) * HD;
@@ -626,13 +637,21 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     dim3 grid(nch, L.n_kv, B);
     int rc;
     if (L.hd <= 256) {
-        // split length: a power-of-two number (1..8) of kChunk rows so that the grid is about four
-        // waves of two CTAs per SM (kChunk-row splits keep the partials within max_chunks)
-        const long slots = 4L * 2 * 148;
-        long want = ((long)span * B * L.n_kv + kChunk * slots - 1) / (kChunk * slots);
-        int k = 1;
-        while (k < want && k < 8) k <<= 1;
-        const int sp = k * kChunk;
+        // split length sp = kChunk * 2^j (whole kChunk rows keep the partials within max_chunks),
+        // minimising waves * (fixed cost of a CTA + rows streamed per CTA) over two CTAs per SM.
+        // A CTA's fixed cost (q/k/v prologue, first copy latency, combine and merge) is about
+        // the time it takes to stream kFixedRows rows.
+        constexpr long kFixedRows = 64;
+        int dev = 0, nsm = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        const long slots = 2L * nsm, pairs = (long)B * L.n_kv;
+        int sp = kChunk;
+        long best = -1;
+        for (int cand = kChunk; cand <= 1024 && cand < 2 * span; cand *= 2) {
+            const long ctas = (long)((span + cand - 1) / cand) * pairs;
+            const long cost = (ctas + slots - 1) / slots * (kFixedRows + std::min(cand, span));
+            if (best < 0 || cost < best) { best = cost; sp = cand; }
+        }
         const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
         switch (L.hd) {
         case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;

@@ -580,26 +580,26 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                 const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
                 for (int b = b0; b < b1 && ok; b++, i++) {
                     const int abuf = i & 1, bs = i % BS;
-                    // Test every barrier this block needs at once (the tests overlap; a test whose
-                    // result is used immediately costs a barrier round trip), then fence once.
+                    const uint32_t pa = i & 1;
+                    // The accumulator pair and the B stage are tested together (the tests overlap;
+                    // a test whose result is used immediately costs a barrier round trip).  Each
+                    // A quarter is waited for just before its MMAs, so the quarters of this block
+                    // start while the expand warps still work on the later ones.
                     {
-                        const uint32_t pa = i & 1;
                         const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
                         const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
-                        const bool r2 = mbar_try_wait(&S.a_full[0], pa), r3 = mbar_try_wait(&S.a_full[2], pa);
-                        const bool r4 = mbar_try_wait(&S.a_full[1], pa), r5 = mbar_try_wait(&S.a_full[3], pa);
-                        if (!(r0 && r1 && r2 && r3 && r4 && r5)) {
-                            if (!q4_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) || !q4_wait(S, &S.b_full[bs], (i / BS) & 1) ||
-                                !q4_wait(S, &S.a_full[0], pa) || !q4_wait(S, &S.a_full[2], pa) ||
-                                !q4_wait(S, &S.a_full[1], pa) || !q4_wait(S, &S.a_full[3], pa)) { ok = false; break; }
+                        if (!(r0 && r1)) {
+                            if (!q4_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) ||
+                                !q4_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
                         }
                     }
-                    tc_fence_after();
                     const uint32_t bsa = smem_u32(bst + bs * BST);
                     const uint32_t d0 = tbase + abuf * 2 * NP;
                     for (int qi = 0; qi < 4; qi++) {
                         // the two expand warp groups finish quarters 0 and 2 first, then 1 and 3
                         const int q = ((qi & 1) << 1) | (qi >> 1);
+                        if (!mbar_try_wait(&S.a_full[q], pa) && !q4_wait(S, &S.a_full[q], pa)) { ok = false; break; }
+                        tc_fence_after();
                         const uint32_t acol = tbase + TM::a + 32 * q;
                         const uint32_t dq = d0 + (q >> 1) * NP;  // S0: weights 0..127, S1: 128..255
 #pragma unroll
