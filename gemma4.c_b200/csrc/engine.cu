@@ -267,6 +267,25 @@ static AttnLayer attn_args(const g4_engine *e, int l) {
     return A;
 }
 
+// Two Q4_K matrices that read the same activation (Q and K, or gate and up) in one tensor-core
+// launch.  epi EPI_GELU_MUL: out = GELU(W act) * (W2 act) (out2 unused).
+int tc_gemm_q4_pair(g4_engine *e, const void *w, int rows, float *out, int ldo, const void *w2, int rows2, float *out2,
+                    int ldo2, int n, const float *act, int ld, bool act_ready, int B, int epi) {
+    const void *m1 = nullptr, *m2 = nullptr;
+    TRY(tc_maps(e, w, G4_Q4_K, n, rows, &m1));
+    TRY(tc_maps(e, w2, G4_Q4_K, n, rows2, &m2));
+    if (B > 64) act_ready = false;
+    float *yd = (float *)(e->tcq + tc_yd_offset(n));
+    for (int g0 = 0; g0 < B; g0 += 64) {
+        const int gb = B - g0 < 64 ? B - g0 : 64, np = tc_np(gb);
+        if (!act_ready) TRY(launch_tc_quant(G4_Q4_K, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
+        TRY(launch_gemm_q4tc2((const CUtensorMap *)m1, w, rows, out + (size_t)g0 * ldo, ldo, (const CUtensorMap *)m2, w2,
+                              rows2, out2 ? out2 + (size_t)g0 * ldo2 : nullptr, ldo2, n, e->tcq, yd, gb, np, e->tc_part,
+                              e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, e->st, epi));
+    }
+    return G4_OK;
+}
+
 int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
@@ -296,7 +315,14 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
         if (tcq_l) {
             bool ready8 = false, ready6 = false;  // operand of xn already laid out (Q4/Q5 class, Q6 class)
-            for (int i = 0; i < np; i++) {
+            int i0 = 0;
+            if (np > 1 && pr[0].t == G4_Q4_K && pr[1].t == G4_Q4_K) {  // Q and K in one launch
+                TRY(tc_gemm_q4_pair(e, pr[0].w, pr[0].rows, pr[0].out, pr[0].rows, pr[1].w, pr[1].rows, pr[1].out,
+                                    pr[1].rows, dim, e->xn, dim, false, B, EPI_STORE));
+                ready8 = true;
+                i0 = 2;
+            }
+            for (int i = i0; i < np; i++) {
                 if (use_tc(e, B, pr[i].t, EPI_STORE)) {
                     bool &rdy = pr[i].t == G4_Q6_K ? ready6 : ready8;
                     // Q4_K and Q5_K operands differ in layout: reuse only within one type
@@ -342,7 +368,10 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
 
         // gate / up with the GELU product fused (1976-1978)
         const bool kq = !(ly.gate_t == G4_F32 || ly.gate_t == G4_F16 || ly.gate_t == G4_BF16);
-        if (tc_ffn) {  // gate and up share the activation operand; GELU product as its own pass
+        if (tc_ffn && ly.gate_t == G4_Q4_K && ly.up_t == G4_Q4_K) {  // one launch, GELU product in its merge
+            TRY(tc_gemm_q4_pair(e, ly.gate, e->hidden, e->hb, e->hidden, ly.up, e->hidden, nullptr, e->hidden, dim, e->xn,
+                                dim, false, B, EPI_GELU_MUL));
+        } else if (tc_ffn) {  // gate and up share the activation operand; GELU product as its own pass
             TRY(tc_gemm(e, ly.gate, ly.gate_t, dim, e->hidden, e->xn, dim, false, e->hb, e->hidden, B));
             TRY(tc_gemm(e, ly.up, ly.up_t, dim, e->hidden, e->xn, dim, ly.up_t == ly.gate_t, e->hb2, e->hidden, B));
             TRY(launch_gelu_mul(e->hb, e->hb2, (size_t)B * e->hidden, e->st));
@@ -754,7 +783,8 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         size_t part = 0;
         int rows_max = e->vocab;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
-                                 {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}, {pd, dim}, {dim, pd}};
+                                 {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}, {pd, dim}, {dim, pd},
+                                 {e->qd_max + e->kvd_max, dim}, {2 * e->hidden, dim}};  // + Q4_K pair launches
         for (auto &sh : shapes) {
             part = std::max(part, tc_part_bytes(sh[0], sh[1], e->nsm));
             // BF16 K-split: up to nsm / tiles slices of the whole row set

@@ -130,6 +130,17 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
 struct TcPlan {
     int ksplit, kslice, units, grid;  // K-slices per 128-row tile, blocks per slice, work units, CTAs
 };
+struct Q4Plan {
+    int share, grid, nseg_max;        // units per CTA, CTAs, most CTAs sharing one row tile
+};
+Q4Plan q4_plan(int tiles, int nb, int nsm);
+// Q4_K GEMM of one or two matrices (same n, same activation; w2 = null for one) in one launch,
+// plus the merge of split row tiles.  epi: EPI_STORE, or EPI_GELU_MUL for a gate/up pair
+// (out = GELU(gate) * up; out2 unused).
+int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
+                      const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
+                      int np, float *part, size_t part_bytes, int *tickets, int *err, int nsm, cudaStream_t st,
+                      int epi);
 int tc_np(int B);                    // padded sequence count: 16, 32 or 64
 size_t tc_operand_bytes(int n);      // B operand + block scales of one activation (NP = 64)
 size_t tc_yd_offset(int n);          // where the block scales start inside that buffer

@@ -23,6 +23,15 @@ struct TcArgs {
     int epi;                    // EPI_STORE, or EPI_SOFTCAP_ARGMAX (logits: out may be null)
     float cap;                  // softcap of EPI_SOFTCAP_ARGMAX
     unsigned long long *keys;   // [B] argmax keys of EPI_SOFTCAP_ARGMAX (atomicMax)
+    // gemm_q4tc_kernel only: stream-K work split over the (row tile, super-block) units of up to
+    // two matrices that share the activation (gate and up, or Q and K).
+    const uint8_t *w2;          // second matrix: row tiles tiles0.. of the launch (null: none)
+    float *out2;                // [B][ldo2]
+    int rows2, ldo2, tiles0;
+    int share;                  // consecutive units per CTA (tile-major, super-block minor)
+    int total;                  // all tiles * nb
+    int prow;                   // rows of a partial slice: all tiles * 128
+    int all_part;               // 1: every tile goes through the partial slots (merge epilogue)
 };
 
 __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {

@@ -33,6 +33,7 @@
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // G4_ERR_TIMEOUT in *err, the producer waits for its copies in flight, the
 // MMA lane for its MMAs, TMEM is freed and the CTA returns.
+#include <algorithm>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -499,7 +500,8 @@ __device__ __forceinline__ void q4_fail(Q4State &S, int *err) {
 // Expansion of block i+1 and the epilogue of block i then run concurrently
 // on every SMSP.
 template <int NP>
-__global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_constant__ CUtensorMap tmw, TcArgs a) {
+__global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_constant__ CUtensorMap tmw,
+                                                                  const __grid_constant__ CUtensorMap tmw2, TcArgs a) {
     constexpr int RAW = Q4Smem<NP>::raw, BST = Q4Smem<NP>::bst, BS = Q4Smem<NP>::bstages, RS = kQ4RawStages;
     constexpr int SP = NP / 2;  // sequences per epilogue warp
     using TM = Q4Tmem<NP>;
@@ -536,26 +538,27 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = S.tmem_base;
+    // this CTA's units [g0, g1): unit g = (row tile g / nb, super-block g % nb)
+    const int g0 = blockIdx.x * a.share, g1 = min(a.total, g0 + a.share);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             int i = 0, nb_issued = 0;
             bool ok = true, dep = false;
-            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-                const int rt = u / a.ksplit, b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
-                for (int b = b0; b < b1; b++, i++) {
-                    const int rs = i % RS;
-                    if (!q4_wait(S, &S.raw_empty[rs], ((i / RS) & 1) ^ 1)) { ok = false; break; }
-                    mbar_expect_tx(&S.raw_full[rs], RAW);
-                    tma_load_2d(raw + rs * RAW, &tmw, b * 144, rt * 128, &S.raw_full[rs]);
-                    if (!dep) { pdl_wait(); dep = true; }
-                    const int bs = i % BS;
-                    if (!q4_wait(S, &S.b_empty[bs], ((i / BS) & 1) ^ 1)) { ok = false; i++; break; }
-                    mbar_expect_tx(&S.b_full[bs], BST);
-                    bulk_g2s(bst + bs * BST, a.bq + (size_t)b * BST, BST, &S.b_full[bs]);
-                    nb_issued = i + 1;
-                }
+            for (int g = g0; g < g1; g++, i++) {
+                const int t = g / a.nb, b = g - t * a.nb;
+                const bool m2 = t >= a.tiles0;
+                const int rs = i % RS;
+                if (!q4_wait(S, &S.raw_empty[rs], ((i / RS) & 1) ^ 1)) { ok = false; break; }
+                mbar_expect_tx(&S.raw_full[rs], RAW);
+                tma_load_2d(raw + rs * RAW, m2 ? &tmw2 : &tmw, b * 144, (m2 ? t - a.tiles0 : t) * 128, &S.raw_full[rs]);
+                if (!dep) { pdl_wait(); dep = true; }
+                const int bs = i % BS;
+                if (!q4_wait(S, &S.b_empty[bs], ((i / BS) & 1) ^ 1)) { ok = false; i++; break; }
+                mbar_expect_tx(&S.b_full[bs], BST);
+                bulk_g2s(bst + bs * BST, a.bq + (size_t)b * BST, BST, &S.b_full[bs]);
+                nb_issued = i + 1;
             }
             if (!dep) pdl_wait();
             if (!ok) {
@@ -576,9 +579,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
             constexpr uint32_t idesc = umma_idesc(1, 0, 0, NP);  // f32 += f16 * f16
             int i = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-                const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
-                for (int b = b0; b < b1 && ok; b++, i++) {
+            {
+                for (int g = g0; g < g1 && ok; g++, i++) {
                     const int abuf = i & 1, bs = i % BS;
                     const uint32_t pa = i & 1;
                     // The accumulator pair and the B stage are tested together (the tests overlap;
@@ -633,9 +635,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         const uint32_t raw_s = smem_u32(raw);
         int i = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-            const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
-            for (int b = b0; b < b1; b++, i++) {
+        {
+            for (int g = g0; g < g1; g++, i++) {
                 const int rs = i % RS;
                 if (!q4_wait(S, &S.raw_full[rs], (i / RS) & 1)) { ok = false; break; }
                 const uint32_t rw = raw_s + rs * RAW + r * 144;
@@ -702,44 +703,59 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         int i = 0;
         bool ok = true;
-        // scales of the next block: d, dmin of row r (weights, just streamed through L2) and the
-        // Q8_K d of sequence p*SP + lane, loaded one block ahead
-        auto fetch = [&](int u, int b, float &dw, float &dm, float &yl) {
-            const int row = (u / a.ksplit) * 128 + r;
+        // scales of unit g: d, dmin of row r of its super-block (weights, just streamed through L2)
+        // and the Q8_K d of sequence p*SP + lane, loaded one unit ahead
+        auto fetch = [&](int g, float &dw, float &dm, float &yl) {
+            const int t = g / a.nb, b = g - t * a.nb;
+            const bool m2 = t >= a.tiles0;
+            const int row = (m2 ? t - a.tiles0 : t) * 128 + r;
             uint32_t m = 0;
-            if (row < a.rows) m = __ldg(reinterpret_cast<const uint32_t *>(a.w + (size_t)row * a.row_bytes + (size_t)b * 144));
+            if (row < (m2 ? a.rows2 : a.rows))
+                m = __ldg(reinterpret_cast<const uint32_t *>((m2 ? a.w2 : a.w) + (size_t)row * a.row_bytes + (size_t)b * 144));
             dw = f16_to_f32((uint16_t)(m & 0xffffu));
             dm = f16_to_f32((uint16_t)(m >> 16));
             yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
         };
-        auto finish = [&](int u) {  // final values, or this K slice's partial (summed by tc_merge_kernel)
-            const int ks = u % a.ksplit, row = (u / a.ksplit) * 128 + r;
-            float *dst = a.ksplit == 1 ? a.out : a.part + (size_t)ks * NP * a.rows;
-            const size_t ld = a.ksplit == 1 ? (size_t)a.ldo : (size_t)a.rows;
-            if (row < a.rows)
+        // End of this CTA's units of row tile t.  A tile wholly inside this CTA is stored (unless
+        // a.all_part); a tile shared by several CTAs leaves its partial in slot (CTA - first CTA of
+        // the tile), and sk_merge_kernel sums the slots in slot order.
+        auto finish = [&](int t) {
+            const bool m2 = t >= a.tiles0;
+            const int row = (m2 ? t - a.tiles0 : t) * 128 + r;
+            const int first = (t * a.nb) / a.share;
+            const int nseg = ((t + 1) * a.nb - 1) / a.share - first + 1;
+            if (nseg == 1 && !a.all_part) {
+                float *dst = (m2 ? a.out2 : a.out) + row;
+                const size_t ld = m2 ? (size_t)a.ldo2 : (size_t)a.ldo;
+                if (row < (m2 ? a.rows2 : a.rows))
+#pragma unroll
+                    for (int s = 0; s < SP / 2; s++) {
+                        const float2 f = f2_unpack(acc[s]);
+                        const int seq = p * SP + 2 * s;
+                        if (seq < a.B) dst[(size_t)seq * ld] = f.x;
+                        if (seq + 1 < a.B) dst[(size_t)(seq + 1) * ld] = f.y;
+                    }
+            } else {
+                const size_t prow = (size_t)a.prow;
+                float *mine = a.part + (size_t)(blockIdx.x - first) * NP * prow + (size_t)t * 128 + r +
+                              (size_t)(p * SP) * prow;
 #pragma unroll
                 for (int s = 0; s < SP / 2; s++) {
                     const float2 f = f2_unpack(acc[s]);
-                    const int seq = p * SP + 2 * s;
-                    if (seq < a.B) dst[(size_t)seq * ld + row] = f.x;
-                    if (seq + 1 < a.B) dst[(size_t)(seq + 1) * ld + row] = f.y;
+                    mine[(size_t)(2 * s) * prow] = f.x;
+                    mine[(size_t)(2 * s + 1) * prow] = f.y;
                 }
+            }
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         };
-        // first block
-        int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
         float ndw = 0.f, ndm = 0.f, nyl = 0.f;
-        if (u < a.units) fetch(u, b, ndw, ndm, nyl);
-        while (u < a.units && ok) {
-            const int b1 = min(a.nb, (u % a.ksplit) * a.kslice + a.kslice);
+        if (g0 < g1) fetch(g0, ndw, ndm, nyl);
+        for (int g = g0; g < g1; g++, i++) {
             const float dw = ndw, dm = ndm;
             if (lane < SP) S.yd[pw][i & 1][lane] = nyl;
             __syncwarp();
-            // advance to the next block and prefetch its scales
-            int nu = u, nbk = b + 1;
-            if (nbk >= b1) { nu = u + gridDim.x; nbk = nu < a.units ? (nu % a.ksplit) * a.kslice : 0; }
-            if (nu < a.units) fetch(nu, nbk, ndw, ndm, nyl);
+            if (g + 1 < g1) fetch(g + 1, ndw, ndm, nyl);  // prefetch the next unit's scales
             // ---- epilogue of block i
             if (!q4_wait(S, &S.acc_full[i & 1], (i >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
@@ -770,8 +786,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                     acc[4 * c + k] = f2_fma(f2_pack(y.x, y.y), t, acc[4 * c + k]);
                 }
             }
-            if (nu != u) finish(u);
-            u = nu; b = nbk; i++;
+            if (g + 1 == g1 || (g + 1) % a.nb == 0) finish(g / a.nb);
         }
         if (!ok) q4_fail(S, a.err);
     }
@@ -920,16 +935,117 @@ int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *b
     return G4_OK;
 }
 
+// Stream-K split of the Q4_K GEMM: `share` consecutive (row tile, super-block) units per CTA,
+// chosen to minimise waves * (share + per-CTA fixed cost) + the fix-up of split tiles, all in
+// super-block times.  nseg_max = most CTAs sharing one tile (partial slots needed).
+Q4Plan q4_plan(int tiles, int nb, int nsm) {
+    const int total = tiles * nb;
+    Q4Plan best{1, 0, 1};
+    if (total <= 0 || nsm <= 0) return best;
+    best.share = total;
+    best.grid = 1;
+    double best_cost = 1e30;
+    for (int share = 1; share <= total; share++) {
+        const int ctas = (total + share - 1) / share, waves = (ctas + nsm - 1) / nsm;
+        // some CTA boundary falls inside a tile unless every boundary is a multiple of nb
+        const bool split = share < total && share % nb != 0;
+        const double cost = waves * (share + 2.5) + (split ? 0.5 : 0.0);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best.share = share;
+            best.grid = ctas;
+        }
+    }
+    best.nseg_max = 1;
+    for (int t = 0; t < tiles; t++)
+        best.nseg_max = max(best.nseg_max, ((t + 1) * nb - 1) / best.share - (t * nb) / best.share + 1);
+    return best;
+}
+
 size_t tc_part_bytes(int rows, int n, int nsm) {
     const TcPlan p = tc_plan(rows, n / G4_QK, nsm);
-    return p.ksplit > 1 ? (size_t)p.ksplit * 64 * rows * sizeof(float) : 0;
+    const int tiles = (rows + 127) / 128;
+    const Q4Plan q = q4_plan(tiles, n / G4_QK, nsm);
+    const size_t uni = p.ksplit > 1 ? (size_t)p.ksplit * 64 * rows * sizeof(float) : 0;
+    const size_t sk = (size_t)q.nseg_max * 64 * tiles * 128 * sizeof(float);  // split tiles, or a merge epilogue
+    return std::max(uni, sk);
 }
 int tc_tickets(int rows) { return ((rows + 127) / 128) * 8; }
+
+// Sum of the partial slots of gemm_q4tc (slot order) for the row tiles that several CTAs shared,
+// or for every tile (all_part), then the epilogue: store, or GELU(gate) * up for a gate/up pair
+// (matrix 1 = gate, matrix 2 = up, same rows; main.c:1973-1978).  One thread per (row, sequence).
+__global__ void sk_merge_kernel(const float *__restrict__ part, int prow, int NP, int nb, int share, int tiles0,
+                                int rows, float *__restrict__ out, int ldo, int rows2, float *__restrict__ out2,
+                                int ldo2, int B, int epi, int all_part) {
+    pdl_trigger();
+    pdl_wait();
+    const int grow = blockIdx.x * blockDim.x + threadIdx.x, s = blockIdx.y;
+    if (grow >= prow || s >= B) return;
+    auto sum = [&](int t, int gr) {
+        const int first = (t * nb) / share, nseg = ((t + 1) * nb - 1) / share - first + 1;
+        float v = 0.0f;
+        for (int k = 0; k < nseg; k++) v += part[((size_t)k * NP + s) * prow + gr];
+        return v;
+    };
+    const int t = grow / 128;
+    if (epi == EPI_GELU_MUL) {  // grid covers the gate tiles only
+        if (grow >= rows) return;
+        const float g = sum(t, grow), u = sum(tiles0 + t, tiles0 * 128 + grow);
+        out[(size_t)s * ldo + grow] =
+            0.5f * g * (1.0f + tanhf(0.7978845608028654f * g * (1.0f + 0.044715f * g * g))) * u;
+        return;
+    }
+    if (!all_part && ((t + 1) * nb - 1) / share == (t * nb) / share) return;  // stored by its CTA
+    const bool m2 = t >= tiles0;
+    const int row = grow - (m2 ? tiles0 * 128 : 0);
+    if (row >= (m2 ? rows2 : rows)) return;
+    (m2 ? out2 : out)[(size_t)s * (m2 ? ldo2 : ldo) + row] = sum(t, grow);
+}
+
+int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
+                      const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
+                      int np, float *part, size_t part_bytes, int *tickets, int *err, int nsm, cudaStream_t st,
+                      int epi) {
+    if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
+    if (epi != EPI_STORE && !(epi == EPI_GELU_MUL && w2 && rows2 == rows)) {
+        set_error(G4_ERR_ARG, "tc gemm: epilogue %d needs a gate/up pair of equal shape", epi);
+        return G4_ERR_ARG;
+    }
+    const int nb = n / G4_QK, tiles0 = (rows + 127) / 128, tiles = tiles0 + (w2 ? (rows2 + 127) / 128 : 0);
+    const Q4Plan p = q4_plan(tiles, nb, nsm);
+    const bool all_part = epi == EPI_GELU_MUL, merge = all_part || p.nseg_max > 1;
+    if (merge && (size_t)p.nseg_max * np * tiles * 128 * sizeof(float) > part_bytes) {
+        set_error(G4_ERR_ARG, "tc gemm: partial buffer too small");
+        return G4_ERR_ARG;
+    }
+    TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q4_K, n), bq, yd, out, part, tickets, err, nb, rows, B, ldo,
+             1, nb, tiles, EPI_STORE, 0.0f, nullptr};
+    a.w2 = (const uint8_t *)w2; a.out2 = out2; a.rows2 = rows2; a.ldo2 = ldo2; a.tiles0 = w2 ? tiles0 : tiles;
+    a.share = p.share; a.total = tiles * nb; a.prow = tiles * 128; a.all_part = all_part ? 1 : 0;
+    const CUtensorMap *m2 = w2 ? tm2 : tm;
+#define G4_Q4TC_CASE(N)                                                                                  \
+    if (np == N)                                                                                           \
+        G4_CUDA(launch_pdl(gemm_q4tc_kernel<N>, dim3(p.grid), dim3(kQ4Threads), (size_t)Q4Smem<N>::total, st, *tm, \
+                           *m2, a));
+    G4_Q4TC_CASE(16) else G4_Q4TC_CASE(32) else G4_Q4TC_CASE(64)
+#undef G4_Q4TC_CASE
+    G4_LAUNCHED();
+    if (!merge) return G4_OK;
+    const int mrows = all_part ? tiles0 * 128 : tiles * 128;
+    G4_CUDA(launch_pdl(sk_merge_kernel, dim3((unsigned)(mrows / 128), (unsigned)B), dim3(128), 0, st, (const float *)part,
+                       tiles * 128, np, nb, p.share, a.tiles0, rows, out, ldo, rows2, out2, ldo2, B, epi, a.all_part));
+    G4_LAUNCHED();
+    return G4_OK;
+}
 
 int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
                    float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
                    cudaStream_t st) {
     if (type != G4_Q4_K && type != G4_Q5_K) { set_error(G4_ERR_TYPE, "tc gemm: type %d", type); return G4_ERR_TYPE; }
+    if (type == G4_Q4_K)
+        return launch_gemm_q4tc2(tm, w, rows, out, ldo, nullptr, nullptr, 0, nullptr, 0, n, bq, yd, B, np, part, part_bytes,
+                                 tickets, err, nsm, st, EPI_STORE);
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     const int nb = n / G4_QK;
     const TcPlan p = tc_plan(rows, nb, nsm);
@@ -947,16 +1063,8 @@ int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int ro
         smem = TcSmem<T, N>::total;                                                \
         G4_CUDA(launch_pdl(gemm_tc_kernel<T, N>, dim3(p.grid), dim3(kTcThreads), smem, st, *tm, a)); \
     }
-#define G4_Q4TC_CASE(N)                                                           \
-    if (type == G4_Q4_K && np == N) {                                              \
-        k = q4tc_kernel_ptr<N>();                                                  \
-        smem = Q4Smem<N>::total;                                                   \
-        G4_CUDA(launch_pdl(gemm_q4tc_kernel<N>, dim3(p.grid), dim3(kQ4Threads), smem, st, *tm, a)); \
-    }
-    G4_Q4TC_CASE(16) else G4_Q4TC_CASE(32) else G4_Q4TC_CASE(64)
-    else G4_TC_CASE(G4_Q5_K, 16) else G4_TC_CASE(G4_Q5_K, 32) else G4_TC_CASE(G4_Q5_K, 64)
+    G4_TC_CASE(G4_Q5_K, 16) else G4_TC_CASE(G4_Q5_K, 32) else G4_TC_CASE(G4_Q5_K, 64)
 #undef G4_TC_CASE
-#undef G4_Q4TC_CASE
     (void)k;
     (void)smem;
     G4_LAUNCHED();
