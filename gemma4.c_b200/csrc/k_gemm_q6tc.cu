@@ -188,23 +188,21 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                 const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
                 for (int b = b0; b < b1 && ok; b++, i++) {
                     const int abuf = i & 1, bs = i % BS;
-                    {   // test every barrier of this block at once, then fence once
-                        const uint32_t pa = i & 1;
+                    const uint32_t pa = i & 1;
+                    {   // accumulator and B stage tested together; each A quarter just before its MMAs
                         const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
                         const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
-                        const bool r2 = mbar_try_wait(&S.a_full[0], pa), r3 = mbar_try_wait(&S.a_full[2], pa);
-                        const bool r4 = mbar_try_wait(&S.a_full[1], pa), r5 = mbar_try_wait(&S.a_full[3], pa);
-                        if (!(r0 && r1 && r2 && r3 && r4 && r5)) {
-                            if (!q6_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) || !q6_wait(S, &S.b_full[bs], (i / BS) & 1) ||
-                                !q6_wait(S, &S.a_full[0], pa) || !q6_wait(S, &S.a_full[2], pa) ||
-                                !q6_wait(S, &S.a_full[1], pa) || !q6_wait(S, &S.a_full[3], pa)) { ok = false; break; }
+                        if (!(r0 && r1)) {
+                            if (!q6_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) ||
+                                !q6_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
                         }
                     }
-                    tc_fence_after();
                     const uint32_t bsa = smem_u32(bst + bs * BST);
                     const uint32_t d = tbase + abuf * 2 * NP;
                     for (int qi = 0; qi < 4; qi++) {
                         const int q = ((qi & 1) << 1) | (qi >> 1);  // 0, 2, 1, 3: the order the expand warps finish
+                        if (!mbar_try_wait(&S.a_full[q], pa) && !q6_wait(S, &S.a_full[q], pa)) { ok = false; break; }
+                        tc_fence_after();
                         const uint32_t acol = tbase + TM::a + 64 * q;
 #pragma unroll
                         for (int ks = 0; ks < 4; ks++) {
@@ -214,6 +212,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                         }
                         tc_commit(&S.a_empty[q]);
                     }
+                    if (!ok) break;
                     tc_commit(&S.b_empty[bs]);
                     tc_commit(&S.acc_full[abuf]);
                 }
@@ -270,18 +269,22 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                     if (!q6_wait(S, &S.a_empty[q], (i & 1) ^ 1)) { ok = false; break; }
 #pragma unroll
                     for (int set = 0; set < 2; set++) {  // set 0: weights l (scales t=0,1); set 1: l+32 (t=2,3)
-                        uint32_t ch[16], cl[16];
 #pragma unroll
-                        for (int w = 0; w < 8; w++) {
-                            const uint32_t lw = ql[8 * set + w], hw = qh[w];
-                            uint32_t qb;
-                            if (qq == 0) qb = (lw & 0x0F0F0F0Fu) | ((set ? (hw << 2) : (hw << 4)) & 0x30303030u);
-                            else qb = ((lw >> 4) & 0x0F0F0F0Fu) | ((set ? (hw >> 2) : hw) & 0x30303030u);
-                            const int t = 2 * set + (w >> 2);  // 16 weights per scale
-                            q6_expand4(qb, scs[t], cs[t], ch[2 * w], ch[2 * w + 1], cl[2 * w], cl[2 * w + 1]);
+                        for (int hf = 0; hf < 2; hf++) {  // 16 weights of scale t = 2*set + hf: 8 columns of h, of l
+                            const int t = 2 * set + hf;
+                            uint32_t ch[8], cl[8];
+#pragma unroll
+                            for (int ww = 0; ww < 4; ww++) {
+                                const int w = 4 * hf + ww;
+                                const uint32_t lw = ql[8 * set + w], hw = qh[w];
+                                uint32_t qb;
+                                if (qq == 0) qb = (lw & 0x0F0F0F0Fu) | ((set ? (hw << 2) : (hw << 4)) & 0x30303030u);
+                                else qb = ((lw >> 4) & 0x0F0F0F0Fu) | ((set ? (hw >> 2) : hw) & 0x30303030u);
+                                q6_expand4(qb, scs[t], cs[t], ch[2 * ww], ch[2 * ww + 1], cl[2 * ww], cl[2 * ww + 1]);
+                            }
+                            tc_st8(tl + TM::a + 64 * q + 16 * set + 8 * hf, ch);
+                            tc_st8(tl + TM::a + 64 * q + 32 + 16 * set + 8 * hf, cl);
                         }
-                        tc_st16(tl + TM::a + 64 * q + 16 * set, ch);
-                        tc_st16(tl + TM::a + 64 * q + 32 + 16 * set, cl);
                     }
                     tc_wait_st();
                     tc_fence_before();
@@ -350,15 +353,16 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                 }
                 return;
             }
-            if (row < a.rows)
+            if (row < a.rows) {  // all NP slots of the partial exist: no per-sequence bound
+                float *dst = a.part + ((size_t)ks * NP + p * SP) * a.rows + row;
+                const size_t st = (size_t)a.rows;
 #pragma unroll
                 for (int s = 0; s < SP / 2; s++) {
                     const float2 f = f2_unpack(acc[s]);
-                    const int seq = p * SP + 2 * s;
-                    float *dst = a.part + ((size_t)ks * NP + seq) * a.rows + row;
-                    if (seq < a.B) dst[0] = f.x;
-                    if (seq + 1 < a.B) dst[a.rows] = f.y;
+                    dst[(size_t)(2 * s) * st] = f.x;
+                    dst[(size_t)(2 * s + 1) * st] = f.y;
                 }
+            }
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         };
