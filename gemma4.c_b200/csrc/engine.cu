@@ -286,6 +286,26 @@ int tc_gemm_q4_pair(g4_engine *e, const void *w, int rows, float *out, int ldo, 
     return G4_OK;
 }
 
+// Let a residual/norm launch of a batched step also write the tensor-core B operand of its output
+// for the GEMM that reads it next (one group of <= 64 sequences): saves that GEMM's own operand
+// launch.  Returns whether the operand was attached.
+bool attach_operand(g4_engine *e, ResNorm &r, int B, int type, int n) {
+    if (!e->tcq || B > 64 || n != r.dim) return false;
+    r.tc_np = tc_np(B);
+    if (type == G4_Q4_K) {
+        r.tc4_bq = e->tcq;
+        r.tc4_yd = (float *)(e->tcq + tc_yd_offset(n));
+    } else if (type == G4_Q6_K) {
+        r.tc6_bq = e->tc6;
+        r.tc6_ys = (float *)(e->tc6 + tc6_ys_offset(n));
+    } else if (type == G4_BF16 && n % 64 == 0) {
+        r.bf3_bq = e->tcb;
+    } else {
+        return false;
+    }
+    return true;
+}
+
 int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
@@ -306,6 +326,13 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         r.x_in = e->x; r.delta = prev ? e->p_raw : nullptr; r.post_w = prev ? prev->post_norm : nullptr;
         r.scale = prev ? prev->out_scale : nullptr; r.x_out = e->x; r.pre_w = ly.attn_norm; r.xn_out = e->xn;
         r.q8_out = q8_in ? e->q8 : nullptr; r.dim = dim; r.eps = e->eps;
+        // operands of xn for the Q (Q4_K) and V (Q6_K) tensor-core GEMMs, written by this launch
+        bool ready8 = false, ready6 = false;  // operand of xn already laid out (Q4/Q5 class, Q6 class)
+        if (tcq_l) {
+            ready8 = ly.wq_t == G4_Q4_K && attach_operand(e, r, B, G4_Q4_K, dim);
+            ready6 = has_kv && ly.wv_t == G4_Q6_K && use_tc(e, B, G4_Q6_K, EPI_STORE) &&
+                     attach_operand(e, r, B, G4_Q6_K, dim);
+        }
         TRY(launch_resnorm(r, B, e->st));
 
         // Q / K / V projections (main.c:1884-1891): one launch per tensor type
@@ -314,11 +341,10 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         const int np = has_kv ? 3 : 1;
         const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
         if (tcq_l) {
-            bool ready8 = false, ready6 = false;  // operand of xn already laid out (Q4/Q5 class, Q6 class)
             int i0 = 0;
             if (np > 1 && pr[0].t == G4_Q4_K && pr[1].t == G4_Q4_K) {  // Q and K in one launch
                 TRY(tc_gemm_q4_pair(e, pr[0].w, pr[0].rows, pr[0].out, pr[0].rows, pr[1].w, pr[1].rows, pr[1].out,
-                                    pr[1].rows, dim, e->xn, dim, false, B, EPI_STORE));
+                                    pr[1].rows, dim, e->xn, dim, ready8, B, EPI_STORE));
                 ready8 = true;
                 i0 = 2;
             }
@@ -364,13 +390,15 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         ResNorm r2{};
         r2.x_in = e->x; r2.delta = e->o_raw; r2.post_w = ly.post_attn_norm; r2.x_out = e->x; r2.pre_w = ly.ffn_norm;
         r2.xn_out = e->xn; r2.q8_out = q8_ffn ? e->q8 : nullptr; r2.dim = dim; r2.eps = e->eps;
+        const bool pair_ffn = tc_ffn && ly.gate_t == G4_Q4_K && ly.up_t == G4_Q4_K;
+        const bool ffn_ready = pair_ffn && attach_operand(e, r2, B, G4_Q4_K, dim);
         TRY(launch_resnorm(r2, B, e->st));
 
         // gate / up with the GELU product fused (1976-1978)
         const bool kq = !(ly.gate_t == G4_F32 || ly.gate_t == G4_F16 || ly.gate_t == G4_BF16);
-        if (tc_ffn && ly.gate_t == G4_Q4_K && ly.up_t == G4_Q4_K) {  // one launch, GELU product in its merge
+        if (pair_ffn) {  // one launch, GELU product in its merge
             TRY(tc_gemm_q4_pair(e, ly.gate, e->hidden, e->hb, e->hidden, ly.up, e->hidden, nullptr, e->hidden, dim, e->xn,
-                                dim, false, B, EPI_GELU_MUL));
+                                dim, ffn_ready, B, EPI_GELU_MUL));
         } else if (tc_ffn) {  // gate and up share the activation operand; GELU product as its own pass
             TRY(tc_gemm(e, ly.gate, ly.gate_t, dim, e->hidden, e->xn, dim, false, e->hb, e->hidden, B));
             TRY(tc_gemm(e, ly.up, ly.up_t, dim, e->hidden, e->xn, dim, ly.up_t == ly.gate_t, e->hb2, e->hidden, B));
@@ -397,10 +425,12 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         ResNorm r3{};
         r3.x_in = e->x; r3.delta = e->d_raw; r3.post_w = ly.post_ffw_norm; r3.x_out = e->x; r3.dim = dim;
         r3.eps = e->eps;
+        const bool tc_gate = use_tc(e, B, ly.inp_gate_t, EPI_GELU_SCALE) && (ly.inp_gate_t != G4_BF16 || dim % 64 == 0);
+        const bool gate_ready = tc_gate && attach_operand(e, r3, B, ly.inp_gate_t, dim);
         TRY(launch_resnorm(r3, B, e->st));
         // per-layer embedding injection (1986-1997)
-        if (use_tc(e, B, ly.inp_gate_t, EPI_GELU_SCALE) && (ly.inp_gate_t != G4_BF16 || dim % 64 == 0))
-            TRY(tc_gemm(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE, nullptr,
+        if (tc_gate)
+            TRY(tc_gemm(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, gate_ready, e->g, pd, B, EPI_GELU_SCALE, nullptr,
                         0.0f, e->ple + (size_t)l * pd, pd * L));
         else
             TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
@@ -415,12 +445,14 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     ResNorm rf{};
     rf.x_in = e->x; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = e->x;
     rf.pre_w = lm_mode ? e->norm_out : nullptr; rf.xn_out = e->xf; rf.dim = dim; rf.eps = e->eps;
+    const bool tc_head = lm_mode && use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX);
+    const bool head_ready = tc_head && attach_operand(e, rf, B, e->embd_t, dim);
     TRY(launch_resnorm(rf, B, e->st));
     if (!lm_mode) return G4_OK;
     // tied LM head + softcap + first-max argmax (1780-1796, 2045-2050)
     const bool dense = e->embd_t == G4_F32 || e->embd_t == G4_F16 || e->embd_t == G4_BF16;
-    if (use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX))
-        TRY(tc_gemm(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, want_logits ? e->logits : nullptr,
+    if (tc_head)
+        TRY(tc_gemm(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, head_ready, want_logits ? e->logits : nullptr,
                     e->vocab, B, EPI_SOFTCAP_ARGMAX, e->keys, e->softcap));
     else
         TRY(gemv(e, e->embd, e->embd_t, dim, e->vocab, e->xf, dim, false, (want_logits || dense) ? e->logits : nullptr,

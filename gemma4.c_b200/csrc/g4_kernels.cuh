@@ -90,6 +90,15 @@ struct ResNorm {
     void *q8_out;           // [B][dim/256] BlockQ8_K of xn_out or null
     int dim;
     float eps;
+    // Tensor-core B operands of the output vector (xn when pre_w is set, else x) for sequence
+    // blockIdx.x of one group of tc_np <= 64 sequences, in the layouts of tc4_quant_kernel,
+    // tc6_split_kernel and bf3_split_kernel (null: not written).  Padding slots are not written.
+    uint8_t *tc4_bq;
+    float *tc4_yd;
+    uint8_t *tc6_bq;
+    float *tc6_ys;
+    uint8_t *bf3_bq;
+    int tc_np;
 };
 int launch_resnorm(const ResNorm &r, int B, cudaStream_t st);
 int launch_embed_v(const void *embd, int embd_t, int dim, size_t vocab, float emb_scale, const void *ple_tok,

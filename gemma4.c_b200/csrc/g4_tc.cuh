@@ -1,6 +1,7 @@
 // g4_tc.cuh — pieces shared by the tensor-core (tcgen05) GEMM kernels:
 // launch arguments, packed fp16x2 / fp32x2 arithmetic.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -77,6 +78,92 @@ __device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
     float2 r;
     asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
     return r;
+}
+
+// B operand of gemm_q4tc for super-block k: q8 as fp16, K-major core
+// matrices (byte (k'/8)*(NP*16) + s*16 + (k'%8)*2, k' = weight index with
+// positions 1 and 2 of every 4 swapped), then bsums[16] as fp16 (byte
+// 512*NP + (t/8)*(NP*16) + s*16 + (t%8)*2).
+__device__ __forceinline__ void tc4_store_q8(uint8_t *blk, float *ydk, int NP, int s, int lane, const uint32_t q[2],
+                                             float d, int ls) {
+    int v[8];
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        v[b] = (int)(int8_t)(q[0] >> (8 * b));
+        v[4 + b] = (int)(int8_t)(q[1] >> (8 * b));
+    }
+    const uint4 o = make_uint4(h_of_int(v[0]) | (h_of_int(v[2]) << 16), h_of_int(v[1]) | (h_of_int(v[3]) << 16),
+                               h_of_int(v[4]) | (h_of_int(v[6]) << 16), h_of_int(v[5]) | (h_of_int(v[7]) << 16));
+    *reinterpret_cast<uint4 *>(blk + (size_t)lane * (NP * 16) + s * 16) = o;
+    const int b16 = ls + __shfl_xor_sync(0xffffffffu, ls, 1);  // lanes 2t, 2t+1: elements 16t..16t+15
+    if ((lane & 1) == 0) {
+        const int t = lane >> 1;
+        *reinterpret_cast<uint16_t *>(blk + 512 * NP + (t >> 3) * (NP * 16) + s * 16 + (t & 7) * 2) =
+            (uint16_t)h_of_int(b16);
+    }
+    if (lane == 0) ydk[s] = d;
+}
+
+// B operand of gemm_q6tc for super-block k of sequence s, from this lane's elements 8*lane ..
+// 8*lane+7 (one warp per block and sequence): the block scaled by a power of two 2^e (largest |x|
+// in [2^13, 2^14)) and split into fp16 x1 + x2, as 2*NP rows (x1 of sequence s in row s, x2 in row
+// NP+s) of K-major core matrices: byte (k'/8)*(2*NP*16) + row*16 + (k'%8)*2, with k' = weight
+// index with positions 1 and 2 of every 4 swapped (the order the expand warps write A in).
+// ys[k][s] = 2^-e (0 when !valid).
+__device__ __forceinline__ void tc6_store_block(uint8_t *bq, float *ys, int k, int NP, int s, int lane, const float (&v)[8],
+                                                bool valid) {
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int e = 0;
+    if (m > 0.0f) {
+        int E = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;  // floor(log2 m) for normal m
+        if (E < -126) E = -126;
+        e = 13 - E;
+        if (e > 126) e = 126;
+    }
+    const float up = __uint_as_float((uint32_t)(127 + e) << 23), down = __uint_as_float((uint32_t)(127 - e) << 23);
+    uint16_t h1[8], h2[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float t = v[j] * up;  // exact (power of two)
+        const __half a = __float2half_rn(t);
+        h1[j] = __half_as_ushort(a);
+        h2[j] = __half_as_ushort(__float2half_rn(t - __half2float(a)));  // the difference is exact in fp32
+    }
+    uint8_t *blk = bq + (size_t)k * 1024 * NP + (size_t)lane * (2 * NP * 16);
+    *reinterpret_cast<uint4 *>(blk + s * 16) =
+        make_uint4(h1[0] | ((uint32_t)h1[2] << 16), h1[1] | ((uint32_t)h1[3] << 16), h1[4] | ((uint32_t)h1[6] << 16),
+                   h1[5] | ((uint32_t)h1[7] << 16));
+    *reinterpret_cast<uint4 *>(blk + (NP + s) * 16) =
+        make_uint4(h2[0] | ((uint32_t)h2[2] << 16), h2[1] | ((uint32_t)h2[3] << 16), h2[4] | ((uint32_t)h2[6] << 16),
+                   h2[5] | ((uint32_t)h2[7] << 16));
+    if (lane == 0) ys[(size_t)k * NP + s] = valid ? down : 0.0f;
+}
+
+// B operand of gemm_bf16tc for the 64-element group g of sequence s, from this lane's elements
+// 2*lane, 2*lane+1 (one warp per group and sequence): x = x1 + x2 + x3 in bf16 (remainders exact in
+// fp32), rows q*NP + s of K-major core matrices.
+constexpr int kBfK = 64;  // weights per group (one pipeline stage of gemm_bf16tc)
+__device__ __forceinline__ void bf3_store_group(uint8_t *bq, int g, int NP, int s, int lane, float v0, float v1) {
+    uint8_t *blk = bq + (size_t)g * 3 * NP * kBfK * 2;
+    const int k = 2 * lane;
+    uint16_t p0[3], p1[3];
+    float r0 = v0, r1 = v1;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {  // remainders are exact in fp32
+        const __nv_bfloat16 a0 = __float2bfloat16_rn(r0), a1 = __float2bfloat16_rn(r1);
+        p0[q] = __bfloat16_as_ushort(a0);
+        p1[q] = __bfloat16_as_ushort(a1);
+        r0 -= __bfloat162float(a0);
+        r1 -= __bfloat162float(a1);
+    }
+#pragma unroll
+    for (int q = 0; q < 3; q++)
+        *reinterpret_cast<uint32_t *>(blk + (k >> 3) * (3 * NP * 16) + (q * NP + s) * 16 + (k & 7) * 2) =
+            (uint32_t)p0[q] | ((uint32_t)p1[q] << 16);
 }
 
 }  // namespace g4

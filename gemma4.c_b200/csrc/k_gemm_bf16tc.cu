@@ -34,7 +34,6 @@ namespace {
 
 constexpr int kBfThreads = 192;  // producer, MMA, 4 epilogue warps
 constexpr int kBfStages = 4;
-constexpr int kBfK = 64;         // weights per stage
 
 template <int NP>
 struct BfSmem {
@@ -226,22 +225,7 @@ __global__ void bf3_split_kernel(const float *__restrict__ x, int ldx, int B, in
         v0 = t.x;
         v1 = t.y;
     }
-    uint8_t *blk = bq + (size_t)g * 3 * NP * kBfK * 2;
-    const int k = 2 * lane;
-    uint16_t p0[3], p1[3];
-    float r0 = v0, r1 = v1;
-#pragma unroll
-    for (int q = 0; q < 3; q++) {  // remainders are exact in fp32
-        const __nv_bfloat16 a0 = __float2bfloat16_rn(r0), a1 = __float2bfloat16_rn(r1);
-        p0[q] = __bfloat16_as_ushort(a0);
-        p1[q] = __bfloat16_as_ushort(a1);
-        r0 -= __bfloat162float(a0);
-        r1 -= __bfloat162float(a1);
-    }
-#pragma unroll
-    for (int q = 0; q < 3; q++)
-        *reinterpret_cast<uint32_t *>(blk + (k >> 3) * (3 * NP * 16) + (q * NP + s) * 16 + (k & 7) * 2) =
-            (uint32_t)p0[q] | ((uint32_t)p1[q] << 16);
+    bf3_store_group(bq, g, NP, s, lane, v0, v1);
 }
 
 template <int NP>

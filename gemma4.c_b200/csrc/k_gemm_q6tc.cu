@@ -432,35 +432,7 @@ __global__ void tc6_split_kernel(const float *__restrict__ x, int ldx, int B, in
         const float4 a0 = p[0], a1 = p[1];
         v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
     }
-    float m = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    int e = 0;
-    if (m > 0.0f) {
-        int E = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;  // floor(log2 m) for normal m
-        if (E < -126) E = -126;
-        e = 13 - E;
-        if (e > 126) e = 126;
-    }
-    const float up = __uint_as_float((uint32_t)(127 + e) << 23), down = __uint_as_float((uint32_t)(127 - e) << 23);
-    uint16_t h1[8], h2[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float t = v[j] * up;  // exact (power of two)
-        const __half a = __float2half_rn(t);
-        h1[j] = __half_as_ushort(a);
-        h2[j] = __half_as_ushort(__float2half_rn(t - __half2float(a)));  // the difference is exact in fp32
-    }
-    uint8_t *blk = bq + (size_t)k * 1024 * NP + (size_t)lane * (2 * NP * 16);
-    *reinterpret_cast<uint4 *>(blk + s * 16) =
-        make_uint4(h1[0] | ((uint32_t)h1[2] << 16), h1[1] | ((uint32_t)h1[3] << 16), h1[4] | ((uint32_t)h1[6] << 16),
-                   h1[5] | ((uint32_t)h1[7] << 16));
-    *reinterpret_cast<uint4 *>(blk + (NP + s) * 16) =
-        make_uint4(h2[0] | ((uint32_t)h2[2] << 16), h2[1] | ((uint32_t)h2[3] << 16), h2[4] | ((uint32_t)h2[6] << 16),
-                   h2[5] | ((uint32_t)h2[7] << 16));
-    if (lane == 0) ys[(size_t)k * NP + s] = s < B ? down : 0.0f;
+    tc6_store_block(bq, ys, k, NP, s, lane, v, s < B);
 }
 
 template <int NP>

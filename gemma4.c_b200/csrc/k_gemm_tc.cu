@@ -798,30 +798,6 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
     }
 }
 
-// B operand of gemm_q4tc for super-block k: q8 as fp16, K-major core
-// matrices (byte (k'/8)*(NP*16) + s*16 + (k'%8)*2, k' = weight index with
-// positions 1 and 2 of every 4 swapped), then bsums[16] as fp16 (byte
-// 512*NP + (t/8)*(NP*16) + s*16 + (t%8)*2).
-__device__ __forceinline__ void tc4_store_q8(uint8_t *blk, float *ydk, int NP, int s, int lane, const uint32_t q[2],
-                                             float d, int ls) {
-    int v[8];
-#pragma unroll
-    for (int b = 0; b < 4; b++) {
-        v[b] = (int)(int8_t)(q[0] >> (8 * b));
-        v[4 + b] = (int)(int8_t)(q[1] >> (8 * b));
-    }
-    const uint4 o = make_uint4(h_of_int(v[0]) | (h_of_int(v[2]) << 16), h_of_int(v[1]) | (h_of_int(v[3]) << 16),
-                               h_of_int(v[4]) | (h_of_int(v[6]) << 16), h_of_int(v[5]) | (h_of_int(v[7]) << 16));
-    *reinterpret_cast<uint4 *>(blk + (size_t)lane * (NP * 16) + s * 16) = o;
-    const int b16 = ls + __shfl_xor_sync(0xffffffffu, ls, 1);  // lanes 2t, 2t+1: elements 16t..16t+15
-    if ((lane & 1) == 0) {
-        const int t = lane >> 1;
-        *reinterpret_cast<uint16_t *>(blk + 512 * NP + (t >> 3) * (NP * 16) + s * 16 + (t & 7) * 2) =
-            (uint16_t)h_of_int(b16);
-    }
-    if (lane == 0) ydk[s] = d;
-}
-
 __global__ void tc4_quant_kernel(const float *__restrict__ x, int ldx, int B, int NP, uint8_t *__restrict__ bq,
                                  float *__restrict__ yd) {
     pdl_trigger();

@@ -16,6 +16,7 @@
 #include "g4_kernels.cuh"
 #include "g4_prologue.cuh"
 #include "g4_quant.cuh"
+#include "g4_tc.cuh"
 
 namespace g4 {
 
@@ -56,29 +57,58 @@ __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
         float *xo = r.x_out + (size_t)b * dim;
         for (int i = tid; i < dim; i += blockDim.x) xo[i] = xs[i];
     }
-    if (!r.pre_w) return;
-    const float ss = canon_sumsq(xs, dim, red);
-    const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
-    for (int i = tid; i < dim; i += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(xs[i], inv), r.pre_w[i]);
-        xn[i] = v;
-        if (r.xn_out) r.xn_out[(size_t)b * dim + i] = v;
-    }
-    if (!r.q8_out) return;
-    __syncthreads();
     const int nb = dim / G4_QK, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
-    uint8_t *q8 = (uint8_t *)r.q8_out + (size_t)b * nb * G4_Q8_BYTES;
-    for (int k = warp; k < nb; k += nw) {
-        uint32_t q[2];
-        float d;
-        int ls;
-        warp_quant_block(xn + k * G4_QK, lane, q, d, ls);
-        store_q8_block(q8 + (size_t)k * G4_Q8_BYTES, lane, q, d, ls);
+    if (r.pre_w) {
+        const float ss = canon_sumsq(xs, dim, red);
+        const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
+        for (int i = tid; i < dim; i += blockDim.x) {
+            const float v = __fmul_rn(__fmul_rn(xs[i], inv), r.pre_w[i]);
+            xn[i] = v;
+            if (r.xn_out) r.xn_out[(size_t)b * dim + i] = v;
+        }
+        if (r.q8_out) {
+            __syncthreads();
+            uint8_t *q8 = (uint8_t *)r.q8_out + (size_t)b * nb * G4_Q8_BYTES;
+            for (int k = warp; k < nb; k += nw) {
+                uint32_t q[2];
+                float d;
+                int ls;
+                warp_quant_block(xn + k * G4_QK, lane, q, d, ls);
+                store_q8_block(q8 + (size_t)k * G4_Q8_BYTES, lane, q, d, ls);
+            }
+        }
     }
+    if (!r.tc4_bq && !r.tc6_bq && !r.bf3_bq) return;
+    // tensor-core operands of sequence b (the same per-warp writers as the standalone kernels)
+    __syncthreads();
+    const float *src = r.pre_w ? xn : xs;
+    if (r.tc4_bq)
+        for (int k = warp; k < nb; k += nw) {
+            uint32_t q[2];
+            float d;
+            int ls;
+            warp_quant_block(src + k * G4_QK, lane, q, d, ls);
+            tc4_store_q8(r.tc4_bq + (size_t)k * 544 * r.tc_np, r.tc4_yd + (size_t)k * r.tc_np, r.tc_np, b, lane, q, d, ls);
+        }
+    if (r.tc6_bq)
+        for (int k = warp; k < nb; k += nw) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = src[k * G4_QK + 8 * lane + j];
+            tc6_store_block(r.tc6_bq, r.tc6_ys, k, r.tc_np, b, lane, v, true);
+        }
+    if (r.bf3_bq)
+        for (int g = warp; g < dim / kBfK; g += nw)
+            bf3_store_group(r.bf3_bq, g, r.tc_np, b, lane, src[g * kBfK + 2 * lane], src[g * kBfK + 2 * lane + 1]);
 }
 
 int launch_resnorm(const ResNorm &r, int B, cudaStream_t st) {
-    if (r.q8_out && r.dim % G4_QK) { set_error(G4_ERR_ARG, "resnorm: dim %d not a multiple of 256", r.dim); return G4_ERR_ARG; }
+    if ((r.q8_out || r.tc4_bq || r.tc6_bq) && r.dim % G4_QK) { set_error(G4_ERR_ARG, "resnorm: dim %d not a multiple of 256", r.dim); return G4_ERR_ARG; }
+    if (r.bf3_bq && r.dim % kBfK) { set_error(G4_ERR_ARG, "resnorm: dim %d not a multiple of %d", r.dim, kBfK); return G4_ERR_ARG; }
+    if ((r.tc4_bq || r.tc6_bq || r.bf3_bq) && (B > r.tc_np || (r.tc_np != 16 && r.tc_np != 32 && r.tc_np != 64))) {
+        set_error(G4_ERR_ARG, "resnorm: %d sequences in a tensor-core group of %d", B, r.tc_np);
+        return G4_ERR_ARG;
+    }
     const size_t smem = (size_t)r.dim * 8;
     if (smem > 100 * 1024) { set_error(G4_ERR_ARG, "resnorm: dim %d too large", r.dim); return G4_ERR_ARG; }
     G4_CUDA(launch_pdl(resnorm_kernel, dim3(B), dim3(512), smem, st, r));
