@@ -306,12 +306,12 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
         int i = 0;
         bool ok = true;
         // per block: d of row r (fp16 after the quant planes of the row) and the activation scale of
-        // sequence p*SP + lane, loaded one block ahead
-        auto fetch = [&](int u, int b, float &dw, float &yl) {
+        // sequence p*SP + lane, loaded one block ahead and converted only when used, so the load
+        // latency overlaps the current block
+        auto fetch = [&](int u, int b, uint16_t &hd, float &yl) {
             const int row = (u / a.ksplit) * 128 + r;
-            uint16_t h = 0;
-            if (row < a.rows) h = __ldg(reinterpret_cast<const uint16_t *>(a.w + (size_t)row * a.row_bytes + (size_t)a.nb * 208) + b);
-            dw = 64.0f * f16_to_f32(h);
+            hd = 0;
+            if (row < a.rows) hd = __ldg(reinterpret_cast<const uint16_t *>(a.w + (size_t)row * a.row_bytes + (size_t)a.nb * 208) + b);
             yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
         };
         // final values of sequences p*SP + 2s, +1 for row `row`
@@ -367,17 +367,19 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         };
         int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
-        float ndw = 0.f, nyl = 0.f;
-        if (u < a.units) fetch(u, b, ndw, nyl);
+        uint16_t nhd = 0;
+        float nyl = 0.f;
+        if (u < a.units) fetch(u, b, nhd, nyl);
         while (u < a.units && ok) {
             const int b1 = min(a.nb, (u % a.ksplit) * a.kslice + a.kslice);
-            const float dw = ndw;
+            const uint16_t hd = nhd;
             if (lane < SP) S.ys[pw][i & 1][lane] = nyl;
             __syncwarp();
             int nu = u, nbk = b + 1;
             if (nbk >= b1) { nu = u + gridDim.x; nbk = nu < a.units ? (nu % a.ksplit) * a.kslice : 0; }
-            if (nu < a.units) fetch(nu, nbk, ndw, nyl);
+            if (nu < a.units) fetch(nu, nbk, nhd, nyl);
             if (!q6_wait(S, &S.acc_full[i & 1], (i >> 1) & 1)) { ok = false; break; }
+            const float dw = 64.0f * f16_to_f32(hd);
             tc_fence_after();
             const float *yv = S.ys[pw][i & 1];
             const unsigned long long dw2 = f2_pack(dw, dw);

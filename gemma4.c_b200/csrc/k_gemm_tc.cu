@@ -449,7 +449,7 @@ __global__ void tc_from_q8_kernel(const uint8_t *__restrict__ q8, int nb, int B,
 // one 16-bit lane pair become one 32-bit TMEM column with one mask.  The B
 // operand is written in the same order, so the dot product is unchanged.
 
-constexpr int kQ4Threads = 576;  // warp 0 producer, warp 1 MMA, warps 2..17 expand + epilogue
+constexpr int kQ4Threads = 608;  // warp 0 producer, warps 1 and 18 MMA, warps 2..17 expand + epilogue
 constexpr int kQ4RawStages = 5;
 
 template <int NP>
@@ -458,19 +458,23 @@ struct Q4Smem {
     static constexpr int bst = 544 * NP;  // 256*NP fp16 quants + 16*NP fp16 bsums
     static constexpr int bstages = NP == 64 ? 3 : 4;
     static constexpr int b_off = kQ4RawStages * raw;
-    static constexpr int total = b_off + bstages * bst + 1024;
+    // A operand of the mins MMA, two slots: 128 rows x 16 fp16, K-major core matrices
+    // (byte (k/8)*2048 + r*16 + (k%8)*2)
+    static constexpr int mins_off = b_off + bstages * bst;
+    static constexpr int total = mins_off + 2 * 4096 + 1024;
 };
-// TMEM columns: [D_s0 | D_s1] for two blocks in flight, D_m, the four
-// 64-weight quarters of A (32 columns each), the mins of two blocks (8 each).
+// TMEM columns: [D_s0 | D_s1] and D_m for two blocks in flight (slot i&1 of
+// block i is released by the epilogue through acc_empty), then the four
+// 64-weight quarters of A (32 columns each).
 template <int NP>
 struct Q4Tmem {
-    static constexpr uint32_t dm = 4 * NP, a = 5 * NP, mins = 5 * NP + 128;
-    static_assert(mins + 16 <= 512, "TMEM columns");
+    static constexpr uint32_t dm = 4 * NP, a = 6 * NP;
+    static_assert(a + 128 <= 512, "TMEM columns");
 };
 
 struct Q4State {
     uint64_t raw_full[kQ4RawStages], raw_empty[kQ4RawStages], b_full[4], b_empty[4];
-    uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], dm_empty, mma_done;
+    uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
     float yd[8][2][32];  // per epilogue warp: block scales of its sequences, by block parity
@@ -508,7 +512,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
     extern __shared__ uint8_t smem_dyn[];
     __shared__ Q4State S;
     uint8_t *smem = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
-    uint8_t *raw = smem, *bst = smem + Q4Smem<NP>::b_off;
+    uint8_t *raw = smem, *bst = smem + Q4Smem<NP>::b_off, *mins_s = smem + Q4Smem<NP>::mins_off;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_trigger();
     if (tid == 0) {
@@ -518,18 +522,17 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         }
         for (int i = 0; i < BS; i++) {
             mbar_init(&S.b_full[i], 1);
-            mbar_init(&S.b_empty[i], 1);
+            mbar_init(&S.b_empty[i], 2);  // both MMA issuers
         }
         for (int i = 0; i < 4; i++) {
             mbar_init(&S.a_full[i], 4);  // the four lane quadrants of quarter i
             mbar_init(&S.a_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
-            mbar_init(&S.acc_full[i], 1);
+            mbar_init(&S.acc_full[i], 2);   // both MMA issuers
             mbar_init(&S.acc_empty[i], 8);  // epilogue warps
         }
-        mbar_init(&S.dm_empty, 8);
-        mbar_init(&S.mma_done, 1);
+        mbar_init(&S.mma_done, 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort = 0;
     }
@@ -573,54 +576,51 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == kQ4Threads / 32 - 1) {
+        // ------------------------------------------------------------ MMA issuers
+        // Two threads issue MMAs: warp 1 the quarters 0, 1 (S0) and the mins, the last warp the
+        // quarters 2, 3 (S1), each right after the expand warp group of its quarters.  Each
+        // issuer's commits track its own MMAs; acc_full, b_empty and mma_done count both.
+        const int h = warp == 1 ? 0 : 1;
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc(1, 0, 0, NP);  // f32 += f16 * f16
             int i = 0;
             bool ok = true;
-            {
-                for (int g = g0; g < g1 && ok; g++, i++) {
-                    const int abuf = i & 1, bs = i % BS;
-                    const uint32_t pa = i & 1;
-                    // The accumulator pair and the B stage are tested together (the tests overlap;
-                    // a test whose result is used immediately costs a barrier round trip).  Each
-                    // A quarter is waited for just before its MMAs, so the quarters of this block
-                    // start while the expand warps still work on the later ones.
-                    {
-                        const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
-                        const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
-                        if (!(r0 && r1)) {
-                            if (!q4_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) ||
-                                !q4_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
-                        }
+            for (int g = g0; g < g1 && ok; g++, i++) {
+                const int abuf = i & 1, bs = i % BS;
+                const uint32_t pa = i & 1;
+                {   // the accumulator pair and the B stage tested together (the tests overlap)
+                    const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
+                    const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
+                    if (!(r0 && r1)) {
+                        if (!q4_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) ||
+                            !q4_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
                     }
-                    const uint32_t bsa = smem_u32(bst + bs * BST);
-                    const uint32_t d0 = tbase + abuf * 2 * NP;
-                    for (int qi = 0; qi < 4; qi++) {
-                        // the two expand warp groups finish quarters 0 and 2 first, then 1 and 3
-                        const int q = ((qi & 1) << 1) | (qi >> 1);
-                        if (!mbar_try_wait(&S.a_full[q], pa) && !q4_wait(S, &S.a_full[q], pa)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t acol = tbase + TM::a + 32 * q;
-                        const uint32_t dq = d0 + (q >> 1) * NP;  // S0: weights 0..127, S1: 128..255
-#pragma unroll
-                        for (int ks = 0; ks < 4; ks++)
-                            tc_mma_f16_ts(dq, acol + 8 * ks, umma_desc(bsa + (8 * q + 2 * ks) * NP * 16, NP * 16, 128),
-                                          idesc, (ks | (q & 1)) != 0);
-                        tc_commit(&S.a_empty[q]);
-                    }
-                    if (!ok) break;
-                    // mins x bsums (K = 16) into the single D_m, once the epilogue of block i-1 has read it.
-                    // The mins of block i sit in slot i&1; the expand warps rewrite that slot for block
-                    // i+2 only after quarter 0 of block i+1 was consumed, i.e. after this MMA completed.
-                    if (i > 0 && !q4_wait(S, &S.dm_empty, (i - 1) & 1)) { ok = false; break; }
-                    tc_fence_after();
-                    tc_mma_f16_ts(tbase + TM::dm, tbase + TM::mins + 8 * (i & 1), umma_desc(bsa + 512 * NP, NP * 16, 128),
-                                  idesc, 0);
-                    tc_commit(&S.b_empty[bs]);
-                    tc_commit(&S.acc_full[abuf]);
                 }
+                const uint32_t bsa = smem_u32(bst + bs * BST);
+                const uint32_t dq = tbase + abuf * 2 * NP + h * NP;  // S0: weights 0..127, S1: 128..255
+                for (int qq = 0; qq < 2; qq++) {
+                    const int q = 2 * h + qq;
+                    if (!mbar_try_wait(&S.a_full[q], pa) && !q4_wait(S, &S.a_full[q], pa)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t acol = tbase + TM::a + 32 * q;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        tc_mma_f16_ts(dq, acol + 8 * ks, umma_desc(bsa + (8 * q + 2 * ks) * NP * 16, NP * 16, 128), idesc,
+                                      (ks | qq) != 0);
+                    tc_commit(&S.a_empty[q]);
+                }
+                if (!ok) break;
+                if (h == 0) {
+                    // mins x bsums (K = 16) into D_m slot i&1 (free: acc_empty above).  The mins of block
+                    // i sit in shared-memory slot i&1 (written with quarter 0); the expand warps rewrite
+                    // it for block i+2 only after quarter 0 of block i+1 was consumed, i.e. after this
+                    // MMA (issued by the same thread before that quarter) completed.
+                    tc_mma_f16(tbase + TM::dm + NP * abuf, umma_desc(smem_u32(mins_s) + 4096 * abuf, 2048, 128),
+                               umma_desc(bsa + 512 * NP, NP * 16, 128), idesc, 0);
+                }
+                tc_commit(&S.b_empty[bs]);
+                tc_commit(&S.acc_full[abuf]);
             }
             if (!ok) q4_fail(S, a.err);
             tc_commit(&S.mma_done);
@@ -683,7 +683,12 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                     }
                     tc_st16(tl + TM::a + 32 * q, col);
                     tc_st16(tl + TM::a + 32 * q + 16, coh);
-                    if (q == 0) tc_st8(tl + TM::mins + 8 * (i & 1), mc);
+                    if (q == 0) {  // mins of row r for the mins MMA (generic-proxy stores, then proxy fence)
+                        uint8_t *mrow = mins_s + 4096 * (i & 1) + r * 16;
+                        *reinterpret_cast<uint4 *>(mrow) = make_uint4(mc[0], mc[1], mc[2], mc[3]);
+                        *reinterpret_cast<uint4 *>(mrow + 2048) = make_uint4(mc[4], mc[5], mc[6], mc[7]);
+                        fence_proxy_async_smem();
+                    }
                     tc_wait_st();
                     tc_fence_before();
                     __syncwarp();
@@ -703,17 +708,16 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         int i = 0;
         bool ok = true;
-        // scales of unit g: d, dmin of row r of its super-block (weights, just streamed through L2)
-        // and the Q8_K d of sequence p*SP + lane, loaded one unit ahead
-        auto fetch = [&](int g, float &dw, float &dm, float &yl) {
+        // scales of unit g: the (d, dmin) word of row r of its super-block (weights, just streamed
+        // through L2) and the Q8_K d of sequence p*SP + lane, loaded one unit ahead and converted
+        // only when used, so the load latency overlaps the current unit
+        auto fetch = [&](int g, uint32_t &mw, float &yl) {
             const int t = g / a.nb, b = g - t * a.nb;
             const bool m2 = t >= a.tiles0;
             const int row = (m2 ? t - a.tiles0 : t) * 128 + r;
-            uint32_t m = 0;
+            mw = 0;
             if (row < (m2 ? a.rows2 : a.rows))
-                m = __ldg(reinterpret_cast<const uint32_t *>((m2 ? a.w2 : a.w) + (size_t)row * a.row_bytes + (size_t)b * 144));
-            dw = f16_to_f32((uint16_t)(m & 0xffffu));
-            dm = f16_to_f32((uint16_t)(m >> 16));
+                mw = __ldg(reinterpret_cast<const uint32_t *>((m2 ? a.w2 : a.w) + (size_t)row * a.row_bytes + (size_t)b * 144));
             yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
         };
         // End of this CTA's units of row tile t.  A tile wholly inside this CTA is stored (unless
@@ -749,32 +753,31 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         };
-        float ndw = 0.f, ndm = 0.f, nyl = 0.f;
-        if (g0 < g1) fetch(g0, ndw, ndm, nyl);
+        uint32_t nmw = 0;
+        float nyl = 0.f;
+        if (g0 < g1) fetch(g0, nmw, nyl);
         for (int g = g0; g < g1; g++, i++) {
-            const float dw = ndw, dm = ndm;
+            const uint32_t mw = nmw;
             if (lane < SP) S.yd[pw][i & 1][lane] = nyl;
             __syncwarp();
-            if (g + 1 < g1) fetch(g + 1, ndw, ndm, nyl);  // prefetch the next unit's scales
+            if (g + 1 < g1) fetch(g + 1, nmw, nyl);  // prefetch the next unit's scales
             // ---- epilogue of block i
             if (!q4_wait(S, &S.acc_full[i & 1], (i >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
             const float *yv = S.yd[pw][i & 1];
+            const float dw = f16_to_f32((uint16_t)(mw & 0xffffu)), dm = f16_to_f32((uint16_t)(mw >> 16));
             const unsigned long long dw2 = f2_pack(dw, dw), ndm2 = f2_pack(-dm, -dm);
 #pragma unroll
             for (int c = 0; c < SP / 8; c++) {
                 uint32_t v0[8], v1[8], vm[8];
                 tc_ld8(tl + (i & 1) * 2 * NP + p * SP + 8 * c, v0);
                 tc_ld8(tl + (i & 1) * 2 * NP + NP + p * SP + 8 * c, v1);
-                tc_ld8(tl + TM::dm + p * SP + 8 * c, vm);
+                tc_ld8(tl + TM::dm + (i & 1) * NP + p * SP + 8 * c, vm);
                 tc_wait_ld();
                 if (c == SP / 8 - 1) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&S.acc_empty[i & 1]);
-                        mbar_arrive(&S.dm_empty);
-                    }
+                    if (lane == 0) mbar_arrive(&S.acc_empty[i & 1]);
                 }
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
