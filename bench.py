@@ -140,20 +140,39 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- distributed plumbing
+def shard(seqs: int, world: int, rank: int) -> range:
+    """The sequences of `rank`: an even split of `seqs` independent sequences
+    over `world` ranks (each rank decodes its share with its own weight
+    replica; no collective on the data path)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank %d of world %d" % (rank, world))
+    if seqs % world:
+        raise ValueError("%d sequences do not divide evenly over %d ranks" % (seqs, world))
+    b = seqs // world
+    return range(rank * b, (rank + 1) * b)
+
+
 class Dist:
-    def __init__(self, n_gpus: int):
+    """One process per GPU (torchrun env), NCCL for the barrier and the
+    max-over-ranks time; backend "gloo" runs the same host logic on CPU."""
+
+    def __init__(self, n_gpus: int, backend: str = "nccl"):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
         self.pg = None
         if self.world > 1:
             import datetime
 
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                        device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(backend, timeout=datetime.timedelta(seconds=60))
             self.pg = dist
         if n_gpus != self.world and self.world > 1:
             raise SystemExit("--gpus %d but WORLD_SIZE=%d" % (n_gpus, self.world))
@@ -161,14 +180,17 @@ class Dist:
     def barrier(self):
         if self.pg:
             import torch
-            self.pg.barrier(device_ids=[self.local])
-            torch.cuda.synchronize()
+            if self.backend == "nccl":
+                self.pg.barrier(device_ids=[self.local])
+                torch.cuda.synchronize()
+            else:
+                self.pg.barrier()
 
     def max(self, v: float) -> float:
         if not self.pg:
             return v
         import torch
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device="cuda" if self.backend == "nccl" else "cpu")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -401,9 +423,11 @@ def main():
     dist = Dist(a.gpus)
     import torch
     torch.cuda.set_device(dist.local)
-    if seqs % dist.world:
-        raise SystemExit("sequences must divide evenly over ranks")
-    B = seqs // dist.world
+    try:
+        mine_ids = shard(seqs, dist.world, dist.rank)
+    except ValueError as ex:
+        raise SystemExit(str(ex))
+    B = len(mine_ids)
     model = S.make_model(S.E4B, seed=3)
     wbytes = model.weight_bytes()
     max_seq = prompt + a.warmup + a.steps * 2 + 8
@@ -413,7 +437,7 @@ def main():
     # prompts: seeded per global sequence id
     rng = np.random.default_rng(1234)
     allp = rng.integers(0, S.E4B.vocab_size, size=(seqs, prompt), dtype=np.int32)
-    mine = allp[dist.rank * B:(dist.rank + 1) * B]
+    mine = allp[mine_ids.start:mine_ids.stop]
     prompts_dev = torch.from_numpy(np.ascontiguousarray(mine.T)).cuda()  # [prompt][B]
     prefill = a.prefill or ("fill" if a.workload == "batch64" else "run")
     cfg["prefill"] = prefill
