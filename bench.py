@@ -518,8 +518,8 @@ def main():
                                "algorithmic_bytes_per_launch": at["step_bytes"] / nl,
                                "us_per_launch": 1e3 * at["step_ms"] / nl, "parts": at}
             out["gemm_roofline"] = gemm
-            # the whole step against HBM: weights once + every layer's K/V rows
-            sb = wbytes + at["step_bytes"]
+            # the whole step against HBM: the streamed weights once + every layer's K/V rows
+            sb = model.streamed_bytes(B) + at["step_bytes"]
             out["step_roofline"] = {"bound": "hbm", "algorithmic_bytes_per_step": sb,
                                     "achieved": sb / (ms_max / a.steps * 1e-3) / 1e9, "peak": hbm_peak,
                                     "unit": "GB/s", "frac": sb / (ms_max / a.steps * 1e-3) / 1e9 / hbm_peak}

@@ -193,6 +193,13 @@ class SynthModel:
             total += sum(a.nbytes for a in lt.values() if a is not None)
         return total
 
+    def streamed_bytes(self, batch: int) -> int:
+        """Weight bytes one decode step reads for `batch` sequences: every
+        tensor once, except the per-layer token table, of which only the
+        `batch` token rows are gathered (emb_lookup, main.c:1696-1723)."""
+        ple = self.t["ple_tok"]
+        return self.weight_bytes() - ple.nbytes + batch * (ple.nbytes // ple.shape[0])
+
     def desc(self) -> Desc:
         s = self.shape
         L = s.n_layers

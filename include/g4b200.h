@@ -156,13 +156,16 @@ int g4d_quantize_row_q8_K(const float *x, g4_block_q8_K *y, int k, int batch, vo
 /* mm on device (same semantics as g4_mm; q8 is a device buffer). */
 int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_block_q8_K *q8, int q8_ready,
            int batch, void *stream);
-/* Q4_K/Q5_K with batch >= the tensor-core threshold (default 16) run as a
- * tcgen05 int8 GEMM over groups of up to 64 activations (exact integer block
- * sums, fp32 block epilogue); smaller batches use the streaming GEMV.  The
- * tensor-core path keeps a per-device scratch (activation operand, K-slice
- * partials, tickets) shared by all calls: calls on different streams must be
- * ordered by the caller.  Not part of the reference interface: sets the
- * threshold (>= 1) and returns the previous one, or -1 on a bad value. */
+/* K-quant and BF16 matrices with batch >= the tensor-core threshold (default
+ * 16) run as tcgen05 GEMMs over groups of up to 64 activations: Q4_K as exact
+ * fp16 integer products, Q5_K as int8 x int8 -> int32 (both with exact
+ * integer block sums and an fp32 block epilogue), Q6_K and BF16 on
+ * activations split into fp16 / bf16 parts; smaller batches use the
+ * streaming GEMV.  The tensor-core path keeps a per-device scratch
+ * (activation operand, K-slice partials) shared by all calls: calls on
+ * different streams must be ordered by the caller.  Not part of the
+ * reference interface: sets the threshold (>= 1) and returns the previous
+ * one, or -1 on a bad value. */
 int g4_set_tc_min_batch(int min_batch);
 
 /* Decode attention (the result of g4_attn_decode) on DEVICE pointers, for
