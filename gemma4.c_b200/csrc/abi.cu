@@ -562,8 +562,6 @@ struct TcScratchDev {  // per device; calls that use it must be ordered on the G
     size_t bq_bytes = 0;
     float *part = nullptr;
     size_t part_bytes = 0;
-    int *tickets = nullptr;
-    int n_tickets = 0;
     int nsm = 0;
 };
 static TcScratchDev g_tcs[64];
@@ -585,8 +583,7 @@ static int tc_scratch(int n, int d, TcScratchDev **out) {
     const size_t bq = std::max(std::max(tc_operand_bytes(n), tc6_operand_bytes(n)), bf16tc_operand_bytes((n + 63) / 64 * 64)),
                  part = std::max(tc_part_bytes(d, n, S.nsm),
                                  (size_t)std::max(1, std::min(n / 64, S.nsm / tiles)) * 64 * d * sizeof(float));
-    const int nt = tc_tickets(d);
-    if (bq > S.bq_bytes || part > S.part_bytes || nt > S.n_tickets) {
+    if (bq > S.bq_bytes || part > S.part_bytes) {
         G4_CUDA(cudaDeviceSynchronize());  // earlier calls may still use the old buffers
         if (bq > S.bq_bytes) {
             cudaFree(S.bq);
@@ -599,13 +596,6 @@ static int tc_scratch(int n, int d, TcScratchDev **out) {
             S.part = nullptr; S.part_bytes = 0;
             G4_CUDA(cudaMalloc(&S.part, part));
             S.part_bytes = part;
-        }
-        if (nt > S.n_tickets) {
-            cudaFree(S.tickets);
-            S.tickets = nullptr; S.n_tickets = 0;
-            G4_CUDA(cudaMalloc(&S.tickets, sizeof(int) * (size_t)nt));
-            G4_CUDA(cudaMemset(S.tickets, 0, sizeof(int) * (size_t)nt));
-            S.n_tickets = nt;
         }
     }
     *out = &S;
@@ -625,7 +615,7 @@ static int mm_tc(float *o, const void *w, int n, int d, int type, const g4_block
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
         G4_TRY(launch_tc_from_q8(type, (const uint8_t *)q8 + (size_t)g0 * nb * G4_Q8_BYTES, gb, n, np, S->bq, yd, st));
         G4_TRY(launch_gemm_tc(&tm, w, type, n, d, S->bq, yd, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
-                              S->tickets, nullptr, S->nsm, st));
+                              nullptr, S->nsm, st));
     }
     return G4_OK;
 }
@@ -642,7 +632,7 @@ static int mm_tc6(float *o, const float *x, const void *w, int n, int d, int bat
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
         G4_TRY(launch_tc6_split(x + (size_t)g0 * n, n, gb, n, np, S->bq, ys, st));
         G4_TRY(launch_gemm_q6tc(maps, w, n, d, S->bq, ys, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
-                                S->tickets, nullptr, S->nsm, EPI_STORE, 0.0f, nullptr, st));
+                                nullptr, S->nsm, EPI_STORE, 0.0f, nullptr, st));
     }
     return G4_OK;
 }
@@ -656,7 +646,7 @@ static int mm_tcbf(float *o, const float *x, const void *w, int n, int d, int ba
     for (int g0 = 0; g0 < batch; g0 += 64) {
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
         G4_TRY(launch_bf3_split(x + (size_t)g0 * n, n, gb, n, np, S->bq, st));
-        G4_TRY(launch_gemm_bf16tc(&tm, n, d, S->bq, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes, S->tickets,
+        G4_TRY(launch_gemm_bf16tc(&tm, n, d, S->bq, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
                                   nullptr, S->nsm, EPI_STORE, nullptr, 0, st));
     }
     return G4_OK;

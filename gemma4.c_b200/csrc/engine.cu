@@ -84,7 +84,6 @@ struct g4_engine {
     uint8_t *tcq = nullptr, *tc6 = nullptr, *tcb = nullptr;  // B operands (Q4_K/Q5_K, Q6_K, BF16)
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
-    int *tc_tickets = nullptr;
     int nsm = 0, tc_min_batch = 9;
     std::mutex mu;
 };
@@ -228,18 +227,18 @@ int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float 
         if (type == G4_BF16) {
             if (!act_ready) TRY(launch_bf3_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tcb, e->st));
             TRY(launch_gemm_bf16tc((const CUtensorMap *)maps, n, rows, e->tcb, gb, np, o, ldo, e->tc_part,
-                                   e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, epi,
+                                   e->tc_part_bytes, e->d_err, e->nsm, epi,
                                    evec ? evec + (size_t)g0 * ld_evec : nullptr, ld_evec, e->st));
         } else if (type == G4_Q6_K) {
             float *ys = (float *)(e->tc6 + tc6_ys_offset(n));
             if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, e->st));
             TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, e->tc_part, e->tc_part_bytes,
-                                 e->tc_tickets, e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st));
+                                 e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st));
         } else {
             float *yd = (float *)(e->tcq + tc_yd_offset(n));
             if (!act_ready) TRY(launch_tc_quant(type, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
             TRY(launch_gemm_tc((const CUtensorMap *)maps, w, type, n, rows, e->tcq, yd, gb, np, o, ldo, e->tc_part,
-                               e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, e->st));
+                               e->tc_part_bytes, e->d_err, e->nsm, e->st));
         }
     }
     return G4_OK;
@@ -281,7 +280,7 @@ int tc_gemm_q4_pair(g4_engine *e, const void *w, int rows, float *out, int ldo, 
         if (!act_ready) TRY(launch_tc_quant(G4_Q4_K, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
         TRY(launch_gemm_q4tc2((const CUtensorMap *)m1, w, rows, out + (size_t)g0 * ldo, ldo, (const CUtensorMap *)m2, w2,
                               rows2, out2 ? out2 + (size_t)g0 * ldo2 : nullptr, ldo2, n, e->tcq, yd, gb, np, e->tc_part,
-                              e->tc_part_bytes, e->tc_tickets, e->d_err, e->nsm, e->st, epi));
+                              e->tc_part_bytes, e->d_err, e->nsm, e->st, epi));
     }
     return G4_OK;
 }
@@ -813,7 +812,6 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
         int nmax = std::max(std::max(dim, e->hidden), std::max(e->qd_max, pd));
         size_t part = 0;
-        int rows_max = e->vocab;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
                                  {dim, e->hidden}, {pd * L, dim}, {e->vocab, dim}, {pd, dim}, {dim, pd},
                                  {e->qd_max + e->kvd_max, dim}, {2 * e->hidden, dim}};  // + Q4_K pair launches
@@ -822,7 +820,6 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
             // BF16 K-split: up to nsm / tiles slices of the whole row set
             const int tiles = (sh[0] + 127) / 128;
             part = std::max(part, (size_t)std::max(1, std::min(sh[1] / 64, e->nsm / tiles)) * 64 * sh[0] * sizeof(float));
-            rows_max = std::max(rows_max, sh[0]);
         }
         nmax = (nmax + G4_QK - 1) / G4_QK * G4_QK;
         TRY(dalloc_t(e, &e->tcq, tc_operand_bytes(nmax)));
@@ -830,7 +827,6 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         TRY(dalloc_t(e, &e->tcb, bf16tc_operand_bytes((nmax + 63) / 64 * 64)));
         e->tc_part_bytes = std::max(part, (size_t)16);
         TRY(dalloc_t(e, &e->tc_part, e->tc_part_bytes / sizeof(float)));
-        TRY(dalloc_t(e, &e->tc_tickets, (size_t)tc_tickets(rows_max)));
     }
     TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
     TRY(dalloc_t(e, &e->d_err, 1));

@@ -119,7 +119,7 @@ size_t bf16tc_operand_bytes(int n);
 int bf16tc_weight_map(CUtensorMap *m, const void *w, int n, int rows);
 int launch_bf3_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, cudaStream_t st);
 int launch_gemm_bf16tc(const CUtensorMap *tm, int n, int rows, const uint8_t *bq, int B, int np, float *out, int ldo,
-                       float *part, size_t part_bytes, int *tickets, int *err, int nsm, int epi, const float *evec,
+                       float *part, size_t part_bytes, int *err, int nsm, int epi, const float *evec,
                        int ld_evec, cudaStream_t st);
 int prime_bf16tc_attrs();
 
@@ -132,7 +132,7 @@ int prime_tc6_attrs();
 int prime_tc_attrs();
 int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *ys, cudaStream_t st);
 int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
-                     int np, float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                     int np, float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
                      int epi, float cap, unsigned long long *keys, cudaStream_t st);
 
 // ---- batched K-quant GEMM on tcgen05 (k_gemm_tc.cu), 16..64 sequences
@@ -148,21 +148,20 @@ Q4Plan q4_plan(int tiles, int nb, int nsm);
 // (out = GELU(gate) * up; out2 unused).
 int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
                       const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
-                      int np, float *part, size_t part_bytes, int *tickets, int *err, int nsm, cudaStream_t st,
+                      int np, float *part, size_t part_bytes, int *err, int nsm, cudaStream_t st,
                       int epi);
 int tc_np(int B);                    // padded sequence count: 16, 32 or 64
 size_t tc_operand_bytes(int n);      // B operand + block scales of one activation (NP = 64)
 size_t tc_yd_offset(int n);          // where the block scales start inside that buffer
 TcPlan tc_plan(int rows, int nb, int nsm);
 size_t tc_part_bytes(int rows, int n, int nsm);
-int tc_tickets(int rows);
 int launch_tc_merge(const float *part, int ksplit, int np, int rows, int B, float *out, int ldo, int epi,
                     const float *evec, int ld_evec, cudaStream_t st);
 int tc_weight_map(CUtensorMap *m, const void *w, int type, int n, int rows);
 int launch_tc_quant(int type, const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
 int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
 int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
-                   float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                   float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
                    cudaStream_t st);
 
 }  // namespace g4

@@ -17,7 +17,6 @@ struct TcArgs {
     const float *yd;    // [nb][NP] Q8_K block scales (0 for padding sequences)
     float *out;         // [B][ldo]
     float *part;        // [ksplit][NP][rows] slice partials (ksplit > 1)
-    int *tickets;       // [row_tiles][8], zero between launches
     int *err;
     int nb, rows, B, ldo;
     int ksplit, kslice, units;

@@ -265,7 +265,7 @@ int launch_bf3_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq,
 }
 
 int launch_gemm_bf16tc(const CUtensorMap *tm, int n, int rows, const uint8_t *bq, int B, int np, float *out, int ldo,
-                       float *part, size_t part_bytes, int *tickets, int *err, int nsm, int epi, const float *evec,
+                       float *part, size_t part_bytes, int *err, int nsm, int epi, const float *evec,
                        int ld_evec, cudaStream_t st) {
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "bf16 tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     if (epi != EPI_STORE && epi != EPI_GELU_SCALE) { set_error(G4_ERR_ARG, "bf16 tc gemm: epilogue %d", epi); return G4_ERR_ARG; }
@@ -277,7 +277,7 @@ int launch_gemm_bf16tc(const CUtensorMap *tm, int n, int rows, const uint8_t *bq
     ksplit = (ng + kslice - 1) / kslice;
     if (ksplit > 1 && (size_t)ksplit * np * rows * sizeof(float) > part_bytes) ksplit = 1;
     const TcPlan p{ksplit, ksplit > 1 ? kslice : ng, tiles * ksplit, std::min(tiles * ksplit, nsm)};
-    TcArgs a{nullptr, 0, bq, nullptr, out, part, tickets, err, ng, rows, B, ldo, p.ksplit, p.kslice, p.units, epi, 0.0f,
+    TcArgs a{nullptr, 0, bq, nullptr, out, part, err, ng, rows, B, ldo, p.ksplit, p.kslice, p.units, epi, 0.0f,
              nullptr};
     const BfExtra ex{evec, ld_evec};
 #define G4_BFTC_CASE(N)                                                                                        \

@@ -484,7 +484,7 @@ int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq,
 }
 
 int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
-                     int np, float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                     int np, float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
                      int epi, float cap, unsigned long long *keys, cudaStream_t st) {
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "q6 tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     if (epi != EPI_STORE && epi != EPI_SOFTCAP_ARGMAX) { set_error(G4_ERR_ARG, "q6 tc gemm: epilogue %d", epi); return G4_ERR_ARG; }
@@ -499,7 +499,7 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
         set_error(G4_ERR_ARG, "q6 tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
-    TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q6_K, n), bq, ys, out, part, tickets, err, nb, rows, B, ldo,
+    TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q6_K, n), bq, ys, out, part, err, nb, rows, B, ldo,
              p.ksplit, p.kslice, p.units, epi, cap, keys};
 #define G4_Q6TC_CASE(N)                                                                             \
     if (np == N) {                                                                                   \

@@ -22,13 +22,16 @@
 // integer partial sums are those of the reference and the float sum differs
 // only in summation order.
 //
+// That is the Q5_K kernel (gemm_tc_kernel).  Q4_K uses gemm_q4tc_kernel
+// below: kind::f16 with exact fp16 integer operands, fewer MMAs per block.
+//
 // CTA (one per SM, persistent): warp 0 issues the bulk tensor copies (TMA) of
 // 128-row x 1-super-block weight tiles and of the pre-laid-out B operand;
 // warp 1 owns TMEM and one lane issues the MMAs; warps 2..9 expand the raw
 // weight tile into the A operands (core-matrix layout, no swizzle) and run the
 // epilogue of the previous super-block.  Work units are (128-row tile,
-// K-slice); slices of one tile are summed in a fixed order by the warp that
-// arrives last (per-warp tickets, no spin-waiting).
+// K-slice); the slices of a tile leave fp32 partials that tc_merge_kernel
+// sums in slice order (Q4_K: stream-K units, summed by sk_merge_kernel).
 //
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // G4_ERR_TIMEOUT in *err, the producer waits for its copies in flight, the
@@ -949,7 +952,6 @@ size_t tc_part_bytes(int rows, int n, int nsm) {
     const size_t sk = (size_t)q.nseg_max * 64 * tiles * 128 * sizeof(float);  // split tiles, or a merge epilogue
     return std::max(uni, sk);
 }
-int tc_tickets(int rows) { return ((rows + 127) / 128) * 8; }
 
 // Sum of the partial slots of gemm_q4tc (slot order) for the row tiles that several CTAs shared,
 // or for every tile (all_part), then the epilogue: store, or GELU(gate) * up for a gate/up pair
@@ -984,7 +986,7 @@ __global__ void sk_merge_kernel(const float *__restrict__ part, int prow, int NP
 
 int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
                       const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
-                      int np, float *part, size_t part_bytes, int *tickets, int *err, int nsm, cudaStream_t st,
+                      int np, float *part, size_t part_bytes, int *err, int nsm, cudaStream_t st,
                       int epi) {
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     if (epi != EPI_STORE && !(epi == EPI_GELU_MUL && w2 && rows2 == rows)) {
@@ -998,7 +1000,7 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
         set_error(G4_ERR_ARG, "tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
-    TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q4_K, n), bq, yd, out, part, tickets, err, nb, rows, B, ldo,
+    TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q4_K, n), bq, yd, out, part, err, nb, rows, B, ldo,
              1, nb, tiles, EPI_STORE, 0.0f, nullptr};
     a.w2 = (const uint8_t *)w2; a.out2 = out2; a.rows2 = rows2; a.ldo2 = ldo2; a.tiles0 = w2 ? tiles0 : tiles;
     a.share = p.share; a.total = tiles * nb; a.prow = tiles * 128; a.all_part = all_part ? 1 : 0;
@@ -1019,12 +1021,12 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
 }
 
 int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
-                   float *out, int ldo, float *part, size_t part_bytes, int *tickets, int *err, int nsm,
+                   float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
                    cudaStream_t st) {
     if (type != G4_Q4_K && type != G4_Q5_K) { set_error(G4_ERR_TYPE, "tc gemm: type %d", type); return G4_ERR_TYPE; }
     if (type == G4_Q4_K)
         return launch_gemm_q4tc2(tm, w, rows, out, ldo, nullptr, nullptr, 0, nullptr, 0, n, bq, yd, B, np, part, part_bytes,
-                                 tickets, err, nsm, st, EPI_STORE);
+                                 err, nsm, st, EPI_STORE);
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     const int nb = n / G4_QK;
     const TcPlan p = tc_plan(rows, nb, nsm);
@@ -1032,7 +1034,7 @@ int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int ro
         set_error(G4_ERR_ARG, "tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
-    TcArgs a{(const uint8_t *)w, device_row_bytes(type, n), bq, yd, out, part, tickets, err, nb, rows, B, ldo,
+    TcArgs a{(const uint8_t *)w, device_row_bytes(type, n), bq, yd, out, part, err, nb, rows, B, ldo,
              p.ksplit, p.kslice, p.units, EPI_STORE, 0.0f, nullptr};
     void *k = nullptr;
     size_t smem = 0;
