@@ -137,6 +137,12 @@ __device__ __forceinline__ void k4_scale_min(int j, uint32_t s0, uint32_t s1, ui
     }
 }
 
+// tanh-approximation GELU with the reference's constants and expression order
+// (gelu_f32, main.c:1490-1492).
+__device__ __forceinline__ float gelu_f32(float x) {
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
+}
+
 // Packed (value, index) key whose unsigned max is the largest value with the
 // LOWEST index among equals: the first-max rule of sample_token
 // (main.c:2045-2050).  NaN is not expected (softcapped logits are finite).

@@ -188,9 +188,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) gemm_bf16tc_kernel(const __grid
                     float v = __uint_as_float(v1[k]) + __uint_as_float(v2[k]) + __uint_as_float(v3[k]);
                     if (seq < a.B && row < a.rows) {
                         if (final_now && a.epi == EPI_GELU_SCALE) {
-                            const float xg = v;
-                            v = 0.5f * xg * (1.0f + tanhf(0.7978845608028654f * xg * (1.0f + 0.044715f * xg * xg))) *
-                                ex.evec[(size_t)seq * ex.ld_evec + row];
+                            v = gelu_f32(v) * ex.evec[(size_t)seq * ex.ld_evec + row];
                         }
                         dst[(size_t)seq * ld + row] = v;
                     }

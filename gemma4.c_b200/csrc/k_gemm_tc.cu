@@ -973,8 +973,7 @@ __global__ void sk_merge_kernel(const float *__restrict__ part, int prow, int NP
     if (epi == EPI_GELU_MUL) {  // grid covers the gate tiles only
         if (grow >= rows) return;
         const float g = sum(t, grow), u = sum(tiles0 + t, tiles0 * 128 + grow);
-        out[(size_t)s * ldo + grow] =
-            0.5f * g * (1.0f + tanhf(0.7978845608028654f * g * (1.0f + 0.044715f * g * g))) * u;
+        out[(size_t)s * ldo + grow] = gelu_f32(g) * u;
         return;
     }
     if (!all_part && ((t + 1) * nb - 1) / share == (t * nb) / share) return;  // stored by its CTA
@@ -1065,7 +1064,7 @@ __global__ void tc_merge_kernel(const float *__restrict__ part, int ksplit, int 
     float v = 0.0f;
     for (int k = 0; k < ksplit; k++) v += part[((size_t)k * NP + s) * rows + row];
     if (epi == EPI_GELU_SCALE)
-        v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * v * (1.0f + 0.044715f * v * v))) * evec[(size_t)s * ld_evec + row];
+        v = gelu_f32(v) * evec[(size_t)s * ld_evec + row];
     out[(size_t)s * ldo + row] = v;
 }
 

@@ -42,10 +42,6 @@ int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStre
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
-__device__ __forceinline__ float gelu_tanh(float x) {  // gelu_f32, main.c:1490-1492
-    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
-}
-
 // ---------------------------------------------------------------- dense GEMV
 
 // One warp per row; x staged in shared memory as fp32.  Epilogues: plain
@@ -113,7 +109,7 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
     }
     acc = warp_sum(acc);
     if (lane == 0) {
-        if (epi == EPI_GELU_SCALE) acc = gelu_tanh(acc) * evec[(size_t)s * ld_evec + row];
+        if (epi == EPI_GELU_SCALE) acc = gelu_f32(acc) * evec[(size_t)s * ld_evec + row];
         out[(size_t)s * ldo + row] = acc;
     }
 }
@@ -218,7 +214,7 @@ __global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restri
     for (int s = 0; s < NS; s++) {
         float a = warp_sum(acc[s]);
         if (lane == 0 && s < ns) {
-            if (epi == EPI_GELU_SCALE) a = gelu_tanh(a) * evec[(size_t)(s0 + s) * ld_evec + row];
+            if (epi == EPI_GELU_SCALE) a = gelu_f32(a) * evec[(size_t)(s0 + s) * ld_evec + row];
             out[(size_t)(s0 + s) * ldo + row] = a;
         }
     }

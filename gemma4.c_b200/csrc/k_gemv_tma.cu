@@ -37,9 +37,6 @@ constexpr int kTmGroups = kTmConsumerWarps * 4;       // consumer lane groups
 constexpr int kTmThreads = (kTmConsumerWarps + 1) * 32;  // + producer warp
 constexpr int kTmMaxStages = 6;
 
-__device__ __forceinline__ float tm_gelu(float x) {  // gelu_f32, main.c:1490-1492
-    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
-}
 __device__ __forceinline__ float tm_q6(uint32_t w, int i) {  // byte i (0..63) -> q - 32, exact
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + i)) - 8388640.0f;
 }
@@ -350,14 +347,14 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                         float a = acc[0][s];
                         float *out = J.out ? J.out + (size_t)(s0 + s) * J.out_stride : nullptr;
                         if (J.epi == EPI_GELU_MUL) {
-                            out[row] = tm_gelu(a) * acc[R - 1][s];
+                            out[row] = gelu_f32(a) * acc[R - 1][s];
                         } else if (J.epi == EPI_SOFTCAP_ARGMAX) {
                             if (J.cap > 0.0f) a = J.cap * tanhf(a * (1.0f / J.cap));
                             if (out) out[row] = a;
                             const unsigned long long kk = argmax_key(a, row);
                             mykey[s] = kk > mykey[s] ? kk : mykey[s];
                         } else if (J.epi == EPI_GELU_SCALE) {
-                            out[row] = tm_gelu(a) * J.evec[(size_t)(s0 + s) * J.ld_evec + row];
+                            out[row] = gelu_f32(a) * J.evec[(size_t)(s0 + s) * J.ld_evec + row];
                         } else {
                             out[row] = a;
                         }

@@ -226,15 +226,11 @@ int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cu
 
 namespace g4 {
 
-__device__ __forceinline__ float gelu_ref(float x) {  // gelu_f32, main.c:1490-1492
-    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * x * (1.0f + 0.044715f * x * x)));
-}
-
 __global__ void gelu_mul_kernel(float *a, const float *b, size_t n) {
     pdl_trigger();
     pdl_wait();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) a[i] = gelu_ref(a[i]) * b[i];
+    if (i < n) a[i] = gelu_f32(a[i]) * b[i];
 }
 
 int launch_gelu_mul(float *a, const float *b, size_t n, cudaStream_t st) {

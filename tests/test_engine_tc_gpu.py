@@ -112,12 +112,14 @@ def test_tc_batched_q4km_mix(g4, gpu, tiny):
     assert same >= int(0.8 * B), (same, B)
 
 
-def test_tc_batched_64_sequences(g4, gpu, tiny):
-    """A full group of 64 (NP = 64 kernels) plus one more sequence (a second group)."""
-    B = 65
+@pytest.mark.parametrize("B", [64, 65])
+def test_tc_batched_64_sequences(g4, gpu, tiny, B):
+    """A full group of 64 (NP = 64 kernels; the residual/norm launches write the
+    GEMM operands themselves) and 64 + 1 (a second group; separate operand
+    launches)."""
     toks = np.random.default_rng(11).integers(0, 4096, B)
     nxt, kv, hid = _first_step(g4, tiny, toks)
-    for b in (0, 31, 63, 64):
+    for b in sorted({0, 31, 63, B - 1}):
         n1, (k1, v1), h1 = _single_first_step(g4, tiny, toks[b])
         assert normwise(kv[b][0], k1) < 1e-5 and normwise(kv[b][1], v1) < 1e-5, b
         assert normwise(hid[b], h1) < 0.3, (b, normwise(hid[b], h1))
