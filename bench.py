@@ -19,11 +19,12 @@ tokens/s with token ids and weights already in HBM (greedy feedback on the
 device, CUDA-graph replay); `e2e` is the same metric through the public C-ABI
 call g4_decode_batch with host token buffers (H2D + D2H every step).
 
-Extras on rank 0: the kernel roofline of the dominant kernel (the K-quant GEMV,
-timed with CUDA events on the engine's own stream over the config-1 layer
-matrices at the workload's batch), the config-0 Q4_K GEMV GB/s, and the
-reference CPU path (gemma4-4b/cpu-blas/main.c compiled unchanged, OpenMP on
-all host cores) timed on a bounded sample of the same workload.
+Extras on rank 0: the roofline of the dominant kernel (batch >= 16: decode
+attention, timed live with CUDA events on the engine stream over the engine's
+own layers; batch 1: the K-quant GEMV over the config-1 layer matrices), the
+tensor-core GEMM and whole-step rooflines, the config-0 Q4_K GEMV GB/s, and
+the reference CPU path (gemma4-4b/cpu-blas/main.c compiled unchanged, OpenMP
+on all host cores) timed on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
