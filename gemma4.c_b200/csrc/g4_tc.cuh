@@ -16,7 +16,8 @@ struct TcArgs {
     const uint8_t *bq;  // [nb][320*NP]: q8 quants (core-matrix layout) then the bsum operand
     const float *yd;    // [nb][NP] Q8_K block scales (0 for padding sequences)
     float *out;         // [B][ldo]
-    float *part;        // [ksplit][NP][rows] slice partials (ksplit > 1)
+    float *part;        // split partials: [ksplit][NP][rows] (K slices), or [slot][NP][prow]
+                        // (gemm_q4tc stream-K: one slot per CTA sharing a row tile)
     int *err;
     int nb, rows, B, ldo;
     int ksplit, kslice, units;
