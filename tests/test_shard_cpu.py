@@ -77,3 +77,24 @@ def test_gloo_ranks_shard_and_max(world):
         assert ok is True, ok
         assert ms == 10.0 + world - 1
         assert n == 64 // world
+
+
+def test_clock_summary_and_streamed_bytes():
+    """Bench host helpers: the clock record's reasons and median, and the
+    per-step weight bytes (every tensor once, only the gathered rows of the
+    per-layer token table)."""
+    bench = _bench()
+    c = bench.ClockSampler(0)
+    c.rows = [["0", "1965", "1965", "", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+              ["0", "1800", "1965", "", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+              ["0", "1965", "1965", "", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"]]
+    s = c.summary()
+    assert s["sm_mhz"] == 1965.0 and s["sm_max_mhz"] == 1965.0 and s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"]
+    assert bench.ClockSampler(0).summary()["reasons"] == ["unsampled"]
+
+    g4 = bench.load_pkg()
+    m = g4.synth.make_model(g4.synth.TINY, seed=1)
+    ple = m.t["ple_tok"]
+    row = ple.nbytes // ple.shape[0]
+    assert m.streamed_bytes(4) == m.weight_bytes() - ple.nbytes + 4 * row
