@@ -81,6 +81,7 @@ SIGNATURES = [
     ("g4_engine_stream", vp, [vp]),
     ("g4_engine_get_hidden", ip, [vp, ip, vp]),
     ("g4_engine_get_kv", ip, [vp, ip, ip, ip, vp, vp]),
+    ("g4_engine_set_kv", ip, [vp, ip, ip, ip, ip, vp, vp]),
     ("g4_engine_last_step_kernels", ip, [vp]),
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
     ("g4_engine_time_attention", ip, [vp, vp, ip, ip, ip, vp]),
@@ -284,6 +285,13 @@ class Engine:
         v = np.zeros(n, np.float32)
         _check(lib().g4_engine_get_kv(self.h, b, layer, pos, _p(k), _p(v)))
         return k, v
+
+    def set_kv(self, layer: int, pos0: int, k, v, b: int = 0):
+        """Write K/V rows [npos][n_kv*hd] of positions pos0.. of sequence b (test tap)."""
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        assert k.shape == v.shape and k.ndim == 2
+        _check(lib().g4_engine_set_kv(self.h, b, layer, pos0, k.shape[0], _p(k), _p(v)))
 
     def fill_kv(self, npos: int, seed: int = 1):
         _check(lib().g4_engine_fill_kv(self.h, npos, seed))

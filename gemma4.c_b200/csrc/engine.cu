@@ -1018,6 +1018,33 @@ int g4_engine_get_hidden(g4_engine *e, int b, float *x) {
     return G4_OK;
 }
 
+int g4_engine_set_kv(g4_engine *e, int b, int layer, int pos0, int npos, const float *k, const float *v) {
+    if (!e || !k || !v || b < 0 || b >= e->max_batch || layer < 0 || layer >= e->L || layer >= G4_N_LAYER_KV ||
+        pos0 < 0 || npos < 0 || pos0 + npos > e->max_seq) {
+        set_error(G4_ERR_ARG, "set_kv: bad arguments");
+        return G4_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    G4_CUDA(cudaSetDevice(e->device));
+    const LayerDev &ly = e->layers[layer];
+    const size_t rowf = (size_t)e->nkv * ly.hd;  // host row: n_kv heads of hd floats
+    // positions map to ring slots pos % ring; copy runs of consecutive slots per head
+    for (int p = pos0; p < pos0 + npos;) {
+        const int slot = p % ly.ring, run = std::min(pos0 + npos - p, ly.ring - slot);
+        for (int h = 0; h < e->nkv; h++) {
+            const size_t drow = (((size_t)b * e->nkv + h) * ly.ring + slot) * ly.hd;
+            const size_t srow = (size_t)(p - pos0) * rowf + (size_t)h * ly.hd;
+            G4_CUDA(cudaMemcpy2DAsync(ly.kc + drow, ly.hd * sizeof(float), k + srow, rowf * sizeof(float),
+                                      ly.hd * sizeof(float), run, cudaMemcpyHostToDevice, e->st));
+            G4_CUDA(cudaMemcpy2DAsync(ly.vc + drow, ly.hd * sizeof(float), v + srow, rowf * sizeof(float),
+                                      ly.hd * sizeof(float), run, cudaMemcpyHostToDevice, e->st));
+        }
+        p += run;
+    }
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return G4_OK;
+}
+
 int g4_engine_get_kv(g4_engine *e, int b, int layer, int pos, float *k, float *v) {
     if (!e || b < 0 || b >= e->max_batch || layer < 0 || layer >= e->L || layer >= G4_N_LAYER_KV || pos < 0 ||
         pos >= e->max_seq) {

@@ -17,6 +17,12 @@
 // before any stream capture.  Every call shares the one array: calls whose
 // work can overlap on the GPU (different streams, or different host threads)
 // race on it and must be ordered by the caller.
+//
+// The call is asynchronous, so it cannot return the status of the kernel's
+// bounded device-side waits.  A wait that gave up (2 s without progress; not
+// expected on a healthy GPU) is recorded in a status word inside the array and
+// a follow-up kernel then fills `out` with NaN, so the failure is visible in
+// the result instead of silently returning partial sums.
 #include <mutex>
 
 #include "g4_internal.cuh"
@@ -29,7 +35,8 @@ int prime_attn_attrs();
 using namespace g4;
 
 // Maximum scratch: partials n_heads * ceil(nwin/32) * (head_dim + 2) floats,
-// then one int per kv head (tickets) and the position, each 256-byte aligned.
+// then one int per kv head (tickets) followed by the wait-status word, then
+// the position, each group 256-byte aligned.
 // 4 MiB covers 8 heads of head_dim 256 over an 8192-position window
 // (about 2.1 MiB).
 static constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
@@ -38,6 +45,13 @@ static __device__ __align__(256) unsigned char g4_noalloc_scratch[kNoAllocScratc
 // Writes the query position into the scratch array (a kernel argument, so no
 // host buffer has to outlive the asynchronous call).
 static __global__ void noalloc_set_pos(int *dst, int value) { *dst = value; }
+
+// After the attention: if a bounded wait gave up, the output is not the
+// attention result; make that visible as NaN.
+static __global__ void noalloc_poison(const int *status, float *out, int n) {
+    if (*status == 0) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = __int_as_float(0x7fc00000);
+}
 
 static std::mutex g_na_mu;
 static void *g_na_addr[64];   // device address of the array, per device ordinal
@@ -64,7 +78,7 @@ extern "C" int g4d_attn_decode_noalloc(float *out, const float *q, const float *
     const int nch = (nwin + chunk - 1) / chunk;
     const size_t part_bytes = sizeof(float) * (size_t)n_heads * nch * (hd + 2);
     const size_t ctr_off = (part_bytes + 255) & ~(size_t)255;
-    const size_t pos_off = (ctr_off + sizeof(int) * (size_t)n_kv_heads + 255) & ~(size_t)255;
+    const size_t pos_off = (ctr_off + sizeof(int) * ((size_t)n_kv_heads + 1) + 255) & ~(size_t)255;
     const size_t need = pos_off + sizeof(int);
     if (need > kNoAllocScratchBytes) {
         set_error(G4_ERR_ARG, "attn_decode_noalloc: needs %zu scratch bytes, the static limit is %zu", need,
@@ -91,9 +105,10 @@ extern "C" int g4d_attn_decode_noalloc(float *out, const float *q, const float *
         base = g_na_addr[dev];
     }
     int *counters = (int *)((unsigned char *)base + ctr_off);
+    int *status = counters + n_kv_heads;
     int *pos_dev = (int *)((unsigned char *)base + pos_off);
-    // the tickets must start at zero; the array keeps whatever the last call left
-    G4_CUDA(cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)n_kv_heads, st));
+    // the tickets and the status word must start at zero; the array keeps whatever the last call left
+    G4_CUDA(cudaMemsetAsync(counters, 0, sizeof(int) * ((size_t)n_kv_heads + 1), st));
     noalloc_set_pos<<<1, 1, 0, st>>>(pos_dev, nwin - 1);
     G4_LAUNCHED();
     G4_CUDA(cudaGetLastError());
@@ -101,7 +116,12 @@ extern "C" int g4d_attn_decode_noalloc(float *out, const float *q, const float *
     L.hd = hd; L.n_rot = 0; L.n_heads = n_heads; L.n_kv = n_kv_heads;
     L.q = q; L.prep = 0; L.append = 0;
     L.src_kc = k; L.src_vc = v; L.src_ring = nwin;   // [n_kv][nwin][hd]: slot t = t
-    L.window = 0; L.eps = 0.0f;
+    L.window = 0; L.eps = 0.0f; L.err = status;
     L.qo = out; L.part = (float *)base; L.counters = counters; L.max_chunks = nch;
-    return launch_attention(L, 1, pos_dev, nwin, st);
+    const int rc = launch_attention(L, 1, pos_dev, nwin, st);
+    if (rc) return rc;
+    noalloc_poison<<<4, 256, 0, st>>>(status, out, n_heads * hd);
+    G4_LAUNCHED();
+    G4_CUDA(cudaGetLastError());
+    return G4_OK;
 }

@@ -41,6 +41,13 @@ def _uniform_f16(rng, shape, lo, hi):
     return rng.uniform(lo, hi, size=shape).astype(np.float16).view(np.uint8).reshape(*shape, 2)
 
 
+def random_bytes(rng: np.random.Generator, n: int) -> np.ndarray:
+    """n uniformly random bytes (uint8[n], writable) from the generator's raw
+    64-bit output (an order of magnitude faster than Generator.bytes)."""
+    words = rng.bit_generator.random_raw((n + 7) // 8)
+    return words.view(np.uint8)[:n]
+
+
 def rand_blocks(rng: np.random.Generator, t: int, rows: int, n: int, d_lo: float, d_hi: float,
                 dmin_lo: float | None = None, dmin_hi: float | None = None) -> np.ndarray:
     """Random `rows` x `n` tensor of type t (Q4_K/Q5_K/Q6_K) as uint8[rows, row_bytes].
@@ -51,7 +58,7 @@ def rand_blocks(rng: np.random.Generator, t: int, rows: int, n: int, d_lo: float
     assert n % QK_K == 0
     nb = n // QK_K
     bb = BLOCK_BYTES[t]
-    raw = np.frombuffer(rng.bytes(rows * nb * bb), dtype=np.uint8).reshape(rows, nb, bb).copy()
+    raw = random_bytes(rng, rows * nb * bb).reshape(rows, nb, bb)
     if t in (Q4_K, Q5_K):
         raw[..., 0:2] = _uniform_f16(rng, (rows, nb), d_lo, d_hi)
         lo = d_lo if dmin_lo is None else dmin_lo
@@ -102,7 +109,7 @@ class ModelShape:
     rope_theta_swa: float = 1e4
     norm_eps: float = 1e-6
     logit_softcapping: float = 30.0
-    # tensor types (the Q4_K_M mix of BASELINE config 1)
+    # tensor types: the Q4_K_M mix (Q/K/O/gate/up Q4_K, V/down Q6_K, BF16 per-layer-embedding matrices)
     wq_t: int = Q4_K
     wk_t: int = Q4_K
     wv_t: int = Q6_K

@@ -177,7 +177,9 @@ int g4_set_tc_min_batch(int min_batch);
  * (each kv head's rows contiguous), q [n_heads * hd], out [n_heads * hd].
  * The first call on a device looks the array up and should precede any
  * stream capture; calls that may overlap on the GPU share the array and must
- * be serialised by the caller. */
+ * be serialised by the caller.  The call is asynchronous: if a bounded
+ * device-side wait gives up (not expected on a healthy GPU), `out` is filled
+ * with NaN instead of a status being returned. */
 int g4d_attn_decode_noalloc(float *out, const float *q, const float *k, const float *v, int nwin, int n_heads,
                             int n_kv_heads, int hd, void *stream);
 
@@ -282,6 +284,10 @@ int g4_engine_last_step_kernels(const g4_engine *e);
  * K/V rows (n_kv_heads * head_dim floats each) stored for (layer, pos). */
 int g4_engine_get_hidden(g4_engine *e, int b, float *x);
 int g4_engine_get_kv(g4_engine *e, int b, int layer, int pos, float *k, float *v);
+/* Test tap: write the K/V rows of positions [pos0, pos0+npos) of sequence b
+ * in a KV layer (< 24) from host rows k/v[npos][n_kv_heads * head_dim], so a
+ * test can start the engine and the reference from identical caches. */
+int g4_engine_set_kv(g4_engine *e, int b, int layer, int pos0, int npos, const float *k, const float *v);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,7 @@
 """GPU parity of the per-call C ABI (libg4b200.so) against the oracle.
 
 Integer results bit-exact; float results within the term-scaled tolerance of
-tests/_tol.py (1e-5).  Sizes go up to BASELINE config 0 (Q4_K 10240 x 2560).
+tests/_tol.py (1e-5).  Sizes go up to the single-GEMV benchmark shape (Q4_K 10240 x 2560).
 """
 import numpy as np
 import pytest
