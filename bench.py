@@ -1,30 +1,40 @@
-"""Benchmark of the decode hot path (BASELINE metric: decode tok/s; Q4_K GEMV
-HBM GB/s vs peak).
+"""Benchmark of the decode hot path (metric: decode tok/s at batch 1 and
+batch 64 on 1/2/4/8 GPUs; Q4_K GEMV HBM GB/s against the measured peak).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl g4|reference]
-                    [--workload batch64|batch1]
+                    [--workload batch64|batch1|gemv0|kernel-q4|kernel-q6|kernel-gemv|kernel-attn]
 
-Workloads (seeded synthetic data with the reference configurations' shapes;
-random-init Gemma-4-E4B-shaped Q4_K_M model, no network, no real GGUF):
-  batch64  BASELINE config 4: 64 independent sequences with a 4096-token
-           context, then greedy decode.  The prompt's KV rows are filled from a
-           seed (--prefill fill; a decode step's work does not depend on them)
-           and the last prompt token runs through the model; --prefill run
-           decodes the whole prompt.  The 64 sequences are sharded over the N
-           ranks (one process per GPU, no collective on the data path) ->
-           "scaling": "strong".
-  batch1   BASELINE config 3: one sequence, 512-token prompt, greedy decode.
+Workloads (seeded synthetic data with the shapes of the reference's
+configurations; random-init Gemma-4-E4B-shaped Q4_K_M model, no network, no
+real GGUF):
+  batch64  64 independent sequences with a 4096-token context, then greedy
+           decode.  The prompt's KV rows are filled from a seed (--prefill
+           fill; a decode step's work does not depend on them) and the last
+           prompt token runs through the model; --prefill run decodes the
+           whole prompt.  The 64 sequences are sharded over the N ranks (one
+           process per GPU, no collective on the data path) -> "scaling":
+           "strong".
+  batch1   one sequence, 512-token prompt, 128 greedy tokens.
+  gemv0    the single Q4_K 10240 x 2560 GEMV alone.
+  kernel-* one kernel family on a small case (a few GB on the device), for
+           profiler captures: q4 / q6 = the Q4_K gate/up and Q6_K down shapes
+           at 64 sequences on the tensor cores, gemv = Q4_K 10240 x 2560 at
+           batch 1, attn = a six-layer E4B-shaped model decoding 64 sequences
+           at context 2048.
 A step is one decode position for all local sequences.  `value` is whole-job
 tokens/s with token ids and weights already in HBM (greedy feedback on the
 device, CUDA-graph replay); `e2e` is the same metric through the public C-ABI
 call g4_decode_batch with host token buffers (H2D + D2H every step).
 
-Extras on rank 0: the roofline of the dominant kernel (batch >= 16: decode
-attention, timed live with CUDA events on the engine stream over the engine's
-own layers; batch 1: the K-quant GEMV over the config-1 layer matrices), the
-tensor-core GEMM and whole-step rooflines, the config-0 Q4_K GEMV GB/s, and
-the reference CPU path (gemma4-4b/cpu-blas/main.c compiled unchanged, OpenMP
-on all host cores) timed on a bounded sample of the same workload.
+Extras on rank 0 of the default run: the roofline of the dominant kernel
+(batch >= 16: decode attention, timed live with CUDA events on the engine
+stream over the engine's own layers; batch 1: the K-quant GEMV over one
+layer's matrices), the tensor-core GEMM and whole-step rooflines with the
+step's time shares, the single Q4_K GEMV, the `batch1` block (batch-1 decode
+of the same model, its step roofline and e2e through g4_forward), GPU and
+reference-CPU timings of the single GEMV, one layer's GEMVs and the decode
+attention, and the reference CPU path (gemma4-4b/cpu-blas/main.c compiled
+unchanged, OpenMP on all host cores) on a bounded sample of the workload.
 """
 from __future__ import annotations
 
@@ -227,7 +237,7 @@ def reference_sample(g4, model, ctx: int, n_steps: int, threads: int):
 # ---------------------------------------------------------------- attention roofline
 # DRAM bytes (read + write) per launch over the algorithmic K/V bytes, from
 # one ncu capture of each layer kind in the batch-64 E4B case
-# (gemma4.c_b200/kernel_cases.py attn; profiles/attn_stream_e4b_b64.md):
+# (bench.py --workload kernel-attn; profiles/attn_stream_e4b_b64.md):
 # sliding (135.01 + 3.95) MB / 134.22 MB, global at context 2048
 # (537.72 + 10.62) MB / 536.87 MB.  The excess is the split partials and
 # the new K/V rows.
@@ -287,7 +297,9 @@ def _graph_time(fn, reps: int, stream_holder):
 
 
 def gemv_roofline(g4, B: int, reps: int = 10):
-    """The K-quant GEMV kernel over the config-1 layer matrices at batch B,
+    """The K-quant GEMV kernel over one decoder layer's matrices at the Q4_K_M
+    mix (Q 2048x2560, K 512x2560 Q4_K; V 512x2560 Q6_K; O 2560x2048, gate/up
+    10240x2560 Q4_K; down 2560x10240 Q6_K) at batch B,
     weights rotated over enough copies to exceed L2, timed as CUDA-graph
     replays with CUDA events."""
     import torch
@@ -329,7 +341,7 @@ def gemv_roofline(g4, B: int, reps: int = 10):
 
 
 def config0_gemv(g4, reps: int = 20, rows: int = 10240):
-    """Q4_K 10240 x 2560 GEMV at batch 1 (activation
+    """The single Q4_K 10240 x 2560 GEMV at batch 1 (activation
     quantized to Q8_K once), weights rotated over enough copies to exceed L2
     (20 copies = 295 MB), timed as CUDA-graph replays with CUDA events.
     `rows` > 10240 times the same kernel on a taller matrix."""
@@ -357,6 +369,187 @@ def config0_gemv(g4, reps: int = 20, rows: int = 10240):
     return {"us_per_gemv": ms * 1e3, "gbs": byts / (ms * 1e-3) / 1e9, "bytes": byts}
 
 
+# ---------------------------------------------------------------- batch-1 decode
+def batch1_decode(g4, model, prompt: int, new: int, dev: int):
+    """Batch-1 greedy decode: `prompt` positions run one by one (lm_mode 0,
+    the reference's prefill loop, main.c:2366-2402), then `new` greedy tokens
+    timed with CUDA events on the engine stream (argmax fed back on the
+    device).  e2e: the same tokens through g4_forward with a host token in
+    and the host argmax out every position (the drop-in for forward())."""
+    import torch
+    S = g4.synth
+    eng = g4.Engine(model, dev, max_seq=prompt + 2 * new + 8, max_batch=1)
+    try:
+        toks = np.random.default_rng(4321).integers(0, S.E4B.vocab_size, size=prompt).astype(np.int32)
+        td = torch.from_numpy(toks).cuda()
+        t0 = time.perf_counter()
+        for pos in range(prompt):
+            eng.decode_batch_device(1, td.data_ptr() + 4 * pos, pos, 1 if pos == prompt - 1 else 0, None)
+        eng.sync()
+        prefill_s = time.perf_counter() - t0
+        s = torch.cuda.ExternalStream(eng.stream())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pos = prompt
+        for _ in range(3):  # warm-up (graph capture of the feedback step)
+            eng.decode_batch_device(1, None, pos, 1, None)
+            pos += 1
+        eng.sync()
+        e0.record(s)
+        for _ in range(new):
+            eng.decode_batch_device(1, None, pos, 1, None)
+            pos += 1
+        e1.record(s)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        nxt = eng.forward(1, pos, 2)
+        pos += 1
+        t0 = time.perf_counter()
+        for _ in range(new):
+            nxt = eng.forward(int(nxt), pos, 2)
+            pos += 1
+        e2e_s = time.perf_counter() - t0
+    finally:
+        eng.close()
+    ctx = prompt + 3 + new // 2
+    kv = sum(2 * model.shape.n_kv_heads * (model.shape.head_dim_swa if S.is_swa(model.shape, l)
+                                           else model.shape.head_dim_full) * 4 *
+             (min(ctx, model.shape.sliding_window) if S.is_swa(model.shape, l) else ctx)
+             for l in range(model.shape.n_layers))
+    byts = model.streamed_bytes(1) + kv
+    hbm_peak, _, kind = measured_peaks()
+    gbs = byts / (ms / new * 1e-3) / 1e9
+    return {"workload": "batch-1 greedy decode, %d-token prompt run position by position, %d tokens timed" % (prompt, new),
+            "value": new / (ms * 1e-3), "unit": "tok/s", "ms_per_token": ms / new, "prefill_s": prefill_s,
+            "prefill_tok_s": prompt / prefill_s,
+            "step_roofline": {"bound": "hbm", "algorithmic_bytes_per_token": byts, "achieved": gbs,
+                              "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": kind},
+            "e2e": {"value": new / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "api": "g4_forward (host token in, host argmax out, lm_mode 2), one call per position"}}
+
+
+def gpu_attention_configs(g4, reps: int = 20):
+    """Decode attention of one sequence (8 query / 2 KV heads, head dim 256)
+    over a 512-row sliding window and an 8192-row global context, through
+    g4d_attn_decode_noalloc on device buffers rotated over > 126 MB (L2)."""
+    import ctypes as C_
+    import torch
+    L = g4.lib()
+    res = {}
+    for nwin in (512, 8192):
+        per = 2 * 2 * nwin * 256 * 4
+        copies = max(2, int(np.ceil(300e6 / per)))
+        kv = [torch.randn(2, 2, nwin, 256, device="cuda") for _ in range(copies)]
+        q = torch.randn(8 * 256, device="cuda") * 0.2
+        out = torch.empty(8 * 256, device="cuda")
+
+        def run(i):
+            rc = L.g4d_attn_decode_noalloc(C_.c_void_p(out.data_ptr()), C_.c_void_p(q.data_ptr()),
+                                           C_.c_void_p(kv[i % copies][0].data_ptr()),
+                                           C_.c_void_p(kv[i % copies][1].data_ptr()), nwin, 8, 2, 256, None)
+            assert rc == 0, g4.last_error()
+        for i in range(3):
+            run(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            run(i)
+        e1.record()
+        e1.synchronize()
+        us = 1e3 * e0.elapsed_time(e1) / reps
+        res["window_%d" % nwin] = {"us": us, "kv_bytes": per, "gbs": per / (us * 1e-6) / 1e9}
+        del kv
+    return res
+
+
+def cpu_configs(g4, threads: int):
+    """The reference's CPU path on the single-GEMV, one-layer and attention
+    shapes: mm() of main.c (Q8_K quantization + AVX2 integer dots for Q4_K,
+    fp32 dequant-dot for Q6_K, OpenMP rows) from oracle/_ref, median of 5
+    after a warm-up; the decode attention block has no callable function in
+    main.c (it is inline in forward, main.c:1909-1950), so it is timed on the
+    C restatement (oracle/g4_oracle.c, one thread)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    if not oracle.have_reference():
+        return None
+    ref = oracle.Reference(threads=threads)
+    orc = oracle.Oracle()
+    S = g4.synth
+    rng = np.random.default_rng(1)
+
+    def med(fn, n=5):
+        fn()
+        ts = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return float(np.median(ts))
+    out = {"threads": ref.max_threads, "blas": ref.blas, "kind": "reference"}
+    w0, x0 = S.config0_weights(seed=0)
+    t = med(lambda: ref.mm(x0, w0, 2560, 10240, S.Q4_K))
+    out["q4k_gemv_10240x2560"] = {"ms": 1e3 * t, "gbs": (w0.nbytes + 2920 + 40960) / t / 1e9}
+    mats = [(S.Q4_K, 2048, 2560), (S.Q4_K, 512, 2560), (S.Q6_K, 512, 2560), (S.Q4_K, 2560, 2048),
+            (S.Q4_K, 10240, 2560), (S.Q4_K, 10240, 2560), (S.Q6_K, 2560, 10240)]
+    ws = [(S._qmat(rng, tt, r, n, 0.02), tt, r, n) for tt, r, n in mats]
+    xs = {n: rng.standard_normal(n).astype(np.float32) for n in (2048, 2560, 10240)}
+    t = med(lambda: [ref.mm(xs[n], w, n, r, tt) for w, tt, r, n in ws])
+    lb = sum(w.nbytes for w, *_ in ws)
+    out["layer_gemvs_q4km"] = {"ms": 1e3 * t, "weight_bytes": lb, "gbs": lb / t / 1e9}
+    for nwin in (512, 8192):
+        q = (rng.standard_normal(8 * 256) * 0.2).astype(np.float32)
+        k = rng.standard_normal(nwin * 512).astype(np.float32)
+        v = rng.standard_normal(nwin * 512).astype(np.float32)
+        t = med(lambda: orc.attention(q, k, v, nwin, 512, 8, 2, 256))
+        out["attention_window_%d" % nwin] = {"us": 1e6 * t, "kind": "port (C restatement, 1 thread)",
+                                             "gbs": 2 * 2 * nwin * 256 * 4 / t / 1e9}
+    return out
+
+
+def kernel_case(g4, which: str, reps: int) -> dict:
+    """One kernel family on a small case for profiler captures (see the module doc)."""
+    import dataclasses
+
+    import torch
+    S = g4.synth
+    if which == "attn":
+        shape = dataclasses.replace(S.E4B, n_layers=6)
+        m = S.make_model(shape, seed=3)
+        B, ctx = 64, 2048
+        eng = g4.Engine(m, 0, max_seq=ctx + reps + 8, max_batch=B)
+        try:
+            eng.fill_kv(ctx - 1, seed=5)
+            toks = np.arange(B, dtype=np.int32) % shape.vocab_size
+            t0 = time.perf_counter()
+            for i in range(max(reps, 3)):
+                toks = eng.decode_batch(toks, ctx - 1 + i, 1)
+            eng.sync()
+            dt = time.perf_counter() - t0
+        finally:
+            eng.close()
+        return {"case": "attn", "steps": max(reps, 3), "s": dt}
+    t, rows, n, B = {"q4": (S.Q4_K, 10240, 2560, 64), "q6": (S.Q6_K, 2560, 10240, 64),
+                     "gemv": (S.Q4_K, 10240, 2560, 1)}[which]
+    copies = max(2, int(np.ceil(300e6 / (S.row_bytes(t, n) * rows))))
+    rng = np.random.default_rng(1)
+    ws = [g4.weight_upload(S.rand_blocks(rng, t, rows, n, 1e-3, 2e-2), t, n, rows) for _ in range(copies)]
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.randn(B, n, device="cuda")
+    q8 = torch.zeros(B * (n // 256) * 292, dtype=torch.uint8, device="cuda")
+    o = torch.zeros(B, rows, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        g4.mm_device(o.data_ptr(), x.data_ptr(), ws[i % copies], n, rows, t, q8.data_ptr(), 0, B, st)
+    e1.record()
+    e1.synchronize()
+    for w in ws:
+        g4.free(w)
+    assert torch.isfinite(o).all().item()
+    return {"case": which, "launches": reps, "us_per_call": 1e3 * e0.elapsed_time(e1) / max(reps, 1)}
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -364,7 +557,8 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
-    ap.add_argument("--workload", default="batch64", choices=["batch64", "batch1", "gemv0"])
+    ap.add_argument("--workload", default="batch64",
+                    choices=["batch64", "batch1", "gemv0", "kernel-q4", "kernel-q6", "kernel-gemv", "kernel-attn"])
     ap.add_argument("--seqs", type=int, default=None, help="total sequences (default 64 / 1)")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
     ap.add_argument("--no-extras", action="store_true")
@@ -381,14 +575,23 @@ def main():
     g4 = load_pkg()
     S = g4.synth
     metric = "decode tok/s"
-    cfg = {"workload": "config4 batched greedy decode" if a.workload == "batch64" else "config3 batch-1 greedy decode",
+    cfg = {"workload": ("batched greedy decode, %d sequences at context %d" % (seqs, prompt)) if a.workload == "batch64"
+           else "batch-1 greedy decode after a %d-token prompt" % prompt,
            "model": "Gemma-4-E4B-shaped Q4_K_M (random init, 42 layers, d 2560, ffn 10240, 8:2 GQA, hd 256, "
                     "vocab 262144, tied Q6_K head)",
            "sequences": seqs, "prompt_tokens": prompt, "global_batch": seqs, "seq_len": prompt,
            "parallelism": "sequence shards (dp%d), no collective" % a.gpus,
            "l2": "no flush needed: each step streams 3.2 GB of weights (> 126 MB L2)"}
 
-    if a.workload == "gemv0":  # BASELINE config 0 alone (used for kernel profiling)
+    if a.workload.startswith("kernel-"):  # profiler cases: one kernel family, small, exits 0
+        import torch
+        torch.cuda.set_device(0)
+        if g4.lib().g4_set_device(0) != 0:
+            raise SystemExit("g4_set_device(0) failed: %s" % (g4.last_error(),))
+        r = kernel_case(g4, a.workload[len("kernel-"):], max(a.steps, 1))
+        print(json.dumps({"kernel_case": r}))
+        return
+    if a.workload == "gemv0":  # the single Q4_K GEMV alone (used for kernel profiling)
         import torch
         torch.cuda.set_device(0)
         r = config0_gemv(g4, reps=max(a.steps, 1), rows=a.gemv_rows)
@@ -396,7 +599,7 @@ def main():
         print(json.dumps({"metric": "Q4_K GEMV HBM GB/s", "value": r["gbs"], "unit": "GB/s", "n_gpus": 1,
                           "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["us_per_gemv"] / 1e3,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4",
-                          "data": "synthetic", "config": {"workload": "config0 Q4_K %dx2560 GEMV" % a.gemv_rows},
+                          "data": "synthetic", "config": {"workload": "Q4_K %dx2560 GEMV, batch 1" % a.gemv_rows},
                           "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": hbm_peak, "unit": "GB/s",
                                        "frac": r["gbs"] / hbm_peak, "peak_kind": kind, "traffic": None}}))
         return
@@ -506,7 +709,7 @@ def main():
         lay = rl["layer"]
         gemm_kernel = ("tensor-core GEMMs gemm_q4tc_kernel / gemm_q6tc_kernel with their operand and merge kernels"
                        if B >= 16 else "gemv_tma_kernel (streaming K-quant GEMV)")
-        gemm = {"kernel": gemm_kernel + ", config-1 layer matrices at batch %d" % B, "bound": "hbm",
+        gemm = {"kernel": gemm_kernel + ", one layer's matrices at batch %d" % B, "bound": "hbm",
                 "achieved": lay["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": lay["gbs"] / hbm_peak,
                 "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": lay["bytes_per_launch"],
                 "us_per_launch": lay["us_per_launch"], "parts": rl}
@@ -525,6 +728,12 @@ def main():
             out["step_roofline"] = {"bound": "hbm", "algorithmic_bytes_per_step": sb,
                                     "achieved": sb / (ms_max / a.steps * 1e-3) / 1e9, "peak": hbm_peak,
                                     "unit": "GB/s", "frac": sb / (ms_max / a.steps * 1e-3) / 1e9 / hbm_peak}
+            # where the step's time goes: attention measured live; the rest is the weight GEMMs and their
+            # operand / merge / norm launches (split by kernel in the launch-list summaries under profiles/)
+            step_ms = ms_max / a.steps
+            out["time_share"] = {"step_ms": step_ms, "attention_ms": at["step_ms"],
+                                 "attention": at["step_ms"] / step_ms, "gemms_and_glue": 1.0 - at["step_ms"] / step_ms,
+                                 "gemms_and_glue_gbs": model.streamed_bytes(B) / ((step_ms - at["step_ms"]) * 1e-3) / 1e9}
         else:
             out["roofline"] = gemm
         out["q4k_gemv_config0"] = config0_gemv(g4)
@@ -538,6 +747,23 @@ def main():
                                        "sample": "%d greedy decode steps of one sequence at context %d, %.1f s "
                                                  "(BLAS: %s)" % (a.cpu_steps, prompt, dt, blas)}
     eng.close()
+    if dist.rank == 0 and dist.world == 1 and not a.no_extras and a.workload == "batch64":
+        # the batch-1 half of the metric on the same model, and the per-shape GPU / CPU timings
+        b1 = batch1_decode(g4, model, 512, 128, dist.local)
+        r = reference_sample(g4, model, 512, a.cpu_steps, os.cpu_count() or 1)
+        if r:
+            tps, dt, thr, blas = r
+            b1["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": thr, "kind": "reference",
+                                  "sample": "%d greedy decode steps of one sequence at context 512, %.1f s; the "
+                                            "reference's own decode formula (generated tokens / decode seconds, "
+                                            "main.c:2279-2280) (BLAS: %s)" % (a.cpu_steps, dt, blas)}
+        out["batch1"] = b1
+        gl = gemv_roofline(g4, 1)["layer"]
+        out["shapes_gpu"] = {"q4k_gemv_10240x2560_us": out.get("q4k_gemv_config0", {}).get("us_per_gemv"),
+                             "layer_gemvs_batch1": {"us_per_matrix": gl["us_per_launch"], "gbs": gl["gbs"],
+                                                    "frac": gl["gbs"] / hbm_peak},
+                             "attention_batch1": gpu_attention_configs(g4)}
+        out["shapes_cpu"] = cpu_configs(g4, os.cpu_count() or 1)
     del model_keep
     if dist.rank == 0:
         print(json.dumps(out))
