@@ -185,10 +185,21 @@ int gemv(g4_engine *e, const void *w, int type, int n, int rows, const float *ac
 
 bool is_kq(int t) { return t == G4_Q4_K || t == G4_Q5_K || t == G4_Q6_K; }
 
-// Whether a GEMM of this step runs on the tensor cores.
+// Q and K of a layer share one tensor-core launch when both are Q4_K (tc_gemm_q4_pair); a GEMV of
+// either matrix then follows the row order of that shared launch, so that the projections of a
+// sequence are bit-identical at every batch size.
+void qk_pair_orders(const g4_engine *e, const LayerDev &ly, GemvJob &J, int which) {
+    J.ord = q4_row_order(ly.qd, ly.kvd, e->dim, e->nsm, which);
+    J.ord2 = J.ord;
+    J.explicit_order = 1;
+}
+bool qk_paired(const LayerDev &ly, bool has_kv) { return has_kv && ly.wq_t == G4_Q4_K && ly.wk_t == G4_Q4_K; }
+
+// Whether a GEMM of this step runs on the tensor cores.  Dense (F32/F16/BF16) matrices always
+// take the multi-sequence dense GEMV, whose per-row summation order does not depend on the batch
+// (the per-layer-embedding matrices are small: 55 MB once per step, 1.3 MB per layer).
 bool use_tc(const g4_engine *e, int B, int type, int epi) {
     if (!e->tcq || B < e->tc_min_batch) return false;
-    if (type == G4_BF16) return epi == EPI_STORE || epi == EPI_GELU_SCALE;
     if (!is_kq(type)) return false;
     return epi == EPI_STORE || (epi == EPI_SOFTCAP_ARGMAX && type == G4_Q6_K);
 }
@@ -368,6 +379,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                 J.w = pr[i].w; J.type = pr[i].t; J.n = dim; J.rows = pr[i].rows;
                 J.act = is_q8_type(pr[i].t) ? (const void *)e->q8 : (const void *)e->xn;
                 J.act_stride = dim; J.out = pr[i].out; J.out_stride = pr[i].rows; J.epi = EPI_STORE;
+                if (i < 2 && qk_paired(ly, has_kv)) qk_pair_orders(e, ly, J, i);
             }
             jobs.err = e->d_err;
             if (jobs.njobs) TRY(launch_gemv_kquant(jobs, B, e->st));
@@ -525,6 +537,7 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
                 GemvJob &J = jobs.j[jobs.njobs++];
                 J.w = pr[i].w; J.type = kt; J.n = dim; J.rows = pr[i].rows; J.out = pr[i].out;
                 J.out_stride = pr[i].rows; J.epi = EPI_STORE;
+                if (i < 2 && qk_paired(ly, has_kv)) qk_pair_orders(e, ly, J, i);
             }
             if (!jobs.njobs) continue;
             jobs.has_pro = 1; jobs.pro = pa; jobs.pro_writer = writer; jobs.err = e->d_err;
@@ -808,8 +821,8 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     e->max_chunks = (max_seq + attn_chunk_size() - 1) / attn_chunk_size();
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
+    G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
     if (max_batch > kFusedMaxBatch) {  // tensor-core path of the batched step
-        G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
         int nmax = std::max(std::max(dim, e->hidden), std::max(e->qd_max, pd));
         size_t part = 0;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},

@@ -128,6 +128,14 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t dtmem, uint32_t atmem, ui
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(dtmem), "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
 }
+// A operand in TMEM (kind::i8, s32 accumulate): D[128 x N] (+)= A[128 x 32] * B[N x 32]^T, A as 4 int8 per column
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accum) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(dtmem), "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
+}
 __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
                  ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])

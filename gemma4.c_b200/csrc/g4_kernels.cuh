@@ -16,6 +16,33 @@ enum Epilogue {
 
 constexpr int kMaxJobs = 3;
 
+// Canonical summation order of one output row of a K-quant matrix, shared by
+// the streaming GEMV and the tensor-core GEMMs so that a sequence gets
+// bit-identical results whether it is decoded alone or in a batch.  Each
+// super-block b of the row contributes an exact term pair (a_b, c_b) (Q4_K/
+// Q5_K: a = Q8_K block scale, c = d*float(sumi_s) - dmin*sumi_m; Q6_K: a =
+// float of the exact integer dot, c = d * activation block scale), and
+//   v = 0; P = 0
+//   for b = 0 .. nb-1:
+//       if b > 0 and seg_start(b): v = v + P; P = 0
+//       P = fma(a_b, c_b, P)
+//   v = v + P
+// The segments are the K ranges a tensor-core launch hands to different
+// CTAs: stream-K units of `share` consecutive (row tile, super-block) units
+// with this matrix's row tile 0 at unit index tile0 * nb (Q4_K), or uniform
+// slices of `kslice` super-blocks (Q5_K, Q6_K).  The plan depends only on the
+// matrix shapes and the SM count, never on the batch.
+struct RowOrder {
+    int tile0;   // global row-tile index of this matrix's row 0 in its tensor-core launch
+    int share;   // stream-K units per CTA, or 0
+    int kslice;  // super-blocks per uniform K slice, or 0
+};
+__host__ __device__ __forceinline__ bool seg_start(const RowOrder &o, int row, int nb, int b) {
+    if (b == 0) return false;
+    if (o.share > 0 && ((long long)(o.tile0 + row / 128) * nb + b) % o.share == 0) return true;
+    return o.kslice > 0 && b % o.kslice == 0;
+}
+
 // One matrix of a grouped K-quant GEMV launch.
 struct GemvJob {
     const void *w;       // device tensor (GGUF blocks; Q6_K as planes)
@@ -26,6 +53,8 @@ struct GemvJob {
     const float *evec;   // [B][ld_evec] multiplier of EPI_GELU_SCALE
     int type, n, rows, act_stride, out_stride, epi, rt, cta_begin, ld_evec, ctas;
     float cap;
+    RowOrder ord, ord2;  // canonical row order of w (and w2)
+    int explicit_order;  // 0: the launcher sets ord (and ord2) for w alone in its own tensor-core launch
 };
 struct GemvJobs {
     GemvJob j[kMaxJobs];
@@ -143,6 +172,12 @@ struct Q4Plan {
     int share, grid, nseg_max;        // units per CTA, CTAs, most CTAs sharing one row tile
 };
 Q4Plan q4_plan(int tiles, int nb, int nsm);
+// Row orders of the tensor-core launches (the GEMV follows the same order):
+//   Q4_K alone, or the first / second matrix of a pair sharing one launch;
+RowOrder q4_row_order(int rows_a, int rows_b, int n, int nsm, int which);  // which: 0 = a, 1 = b (rows_b 0: no pair)
+//   Q5_K (uniform K slices of tc_plan);  Q6_K (its own uniform plan; argmax: whole rows).
+RowOrder q5_row_order(int rows, int n, int nsm);
+RowOrder q6_row_order(int rows, int n, int nsm, bool argmax);
 // Q4_K GEMM of one or two matrices (same n, same activation; w2 = null for one) in one launch,
 // plus the merge of split row tiles.  epi: EPI_STORE, or EPI_GELU_MUL for a gate/up pair
 // (out = GELU(gate) * up; out2 unused).

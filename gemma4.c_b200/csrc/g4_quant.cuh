@@ -59,3 +59,66 @@ __device__ __forceinline__ void store_q8_block(uint8_t *yb, int lane, const uint
 }
 
 }  // namespace g4
+
+namespace g4 {
+
+// ---------------------------------------------------------------- Q6_K activation pieces
+//
+// The Q6_K weights are multiplied against the fp32 activation (mm_quant_rows,
+// gemma4-4b/cpu-blas/main.c:1539-1556).  To make that dot product exact and
+// independent of summation order (so the streaming GEMV and the tensor-core
+// GEMM agree bit for bit), each 256-element block of the activation is put on
+// a fixed-point grid: with E the exponent that bounds the block (max|x| < 2^E),
+//   X_i = rint(x_i * 2^(22-E))          |X_i| <= 2^22
+//   X_i = a0_i * 2^16 + a1_i * 2^8 + a2_i   (signed bytes, |a0| <= 64)
+// and the block's scale is 2^(E-22).  The integer dot sum_i v_i X_i of the
+// weight integers v = sc*(q-32) with the X is then exact (it fits in 44 bits),
+// and is turned into a float once per block.  Elements far below the block
+// maximum keep 22 bits relative to that maximum.
+
+// 2^e as a float, exact for e in [-149, 127] (subnormal below -126), 0 below.
+__device__ __forceinline__ float pow2f(int e) {
+    if (e >= -126) return __uint_as_float((uint32_t)(e + 127) << 23);
+    if (e >= -149) return __uint_as_float(1u << (e + 149));
+    return 0.0f;
+}
+
+// One block: lane l holds elements 8l..8l+7 in v.  Returns the lane's three
+// byte planes (p[2*j], p[2*j+1] = elements 8l..8l+3, 8l+4..8l+7 of piece j) and
+// the block scale 2^(E-22) (0 for an all-zero block).
+__device__ __forceinline__ void q6x_block(const float (&v)[8], uint32_t (&p)[6], float &ys) {
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+#pragma unroll
+    for (int j = 0; j < 6; j++) p[j] = 0u;
+    if (!(m > 0.0f)) { ys = 0.0f; return; }
+    const int be = (int)((__float_as_uint(m) >> 23) & 0xffu);
+    const int E = be ? be - 126 : -126;  // m < 2^E
+    const int k = 22 - E;                // scale up by 2^k (k may exceed 127 for tiny blocks: two steps, exact)
+    const float s1 = pow2f(k > 127 ? 127 : k), s2 = pow2f(k > 127 ? k - 127 : 0);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int X = __float2int_rn(__fmul_rn(__fmul_rn(v[j], s1), s2));
+        const int a2 = (int)(int8_t)(X & 0xff);
+        const int X1 = (X - a2) >> 8;
+        const int a1 = (int)(int8_t)(X1 & 0xff);
+        const int a0 = (X1 - a1) >> 8;
+        const int w = j >> 2, sh = 8 * (j & 3);
+        p[w] |= ((uint32_t)a0 & 0xffu) << sh;
+        p[2 + w] |= ((uint32_t)a1 & 0xffu) << sh;
+        p[4 + w] |= ((uint32_t)a2 & 0xffu) << sh;
+    }
+    ys = pow2f(E - 22);
+}
+
+// The exact block dot from its three piece dots D_j = sum_i v_i * a_j,i:
+// the float of D0*2^16 + D1*2^8 + D2 (|D_j| < 2^27), rounded once.
+__device__ __forceinline__ float q6x_dot(int D0, int D1, int D2) {
+    const long long D = (long long)D0 * 65536ll + (long long)D1 * 256ll + (long long)D2;
+    return __ll2float_rn(D);
+}
+
+}  // namespace g4

@@ -7,6 +7,7 @@
 
 #include "g4_async.cuh"
 #include "g4_internal.cuh"
+#include "g4_quant.cuh"
 
 namespace g4 {
 
@@ -104,43 +105,25 @@ __device__ __forceinline__ void tc4_store_q8(uint8_t *blk, float *ydk, int NP, i
     if (lane == 0) ydk[s] = d;
 }
 
-// B operand of gemm_q6tc for super-block k of sequence s, from this lane's elements 8*lane ..
-// 8*lane+7 (one warp per block and sequence): the block scaled by a power of two 2^e (largest |x|
-// in [2^13, 2^14)) and split into fp16 x1 + x2, as 2*NP rows (x1 of sequence s in row s, x2 in row
-// NP+s) of K-major core matrices: byte (k'/8)*(2*NP*16) + row*16 + (k'%8)*2, with k' = weight
-// index with positions 1 and 2 of every 4 swapped (the order the expand warps write A in).
-// ys[k][s] = 2^-e (0 when !valid).
+// B operand of gemm_q6tc for super-block k (768*NP bytes): the three fixed-point pieces of every
+// sequence's block (q6x_block) as int8 K-major core matrices,
+//   byte (kk/16)*(3*NP*16) + row*16 + kk%16,   row = (s/NPP)*3*NPP + j*NPP + s%NPP
+// (MMA pass s/NPP, then piece j, then sequence; NPP = min(NP, 32)), from this lane's elements
+// 8*lane .. 8*lane+7 (one warp per block and sequence).  ys[k][s] = 2^(E-22) (0 when !valid).
 __device__ __forceinline__ void tc6_store_block(uint8_t *bq, float *ys, int k, int NP, int s, int lane, const float (&v)[8],
                                                 bool valid) {
-    float m = 0.0f;
+    float w[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+    for (int j = 0; j < 8; j++) w[j] = valid ? v[j] : 0.0f;
+    uint32_t p[6];
+    float y;
+    q6x_block(w, p, y);
+    const int npp = NP < 32 ? NP : 32, pass = s / npp, sl = s % npp;
+    uint8_t *blk = bq + (size_t)k * 768 * NP + (size_t)(lane >> 1) * (3 * NP * 16) + 8 * (lane & 1);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    int e = 0;
-    if (m > 0.0f) {
-        int E = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;  // floor(log2 m) for normal m
-        if (E < -126) E = -126;
-        e = 13 - E;
-        if (e > 126) e = 126;
-    }
-    const float up = __uint_as_float((uint32_t)(127 + e) << 23), down = __uint_as_float((uint32_t)(127 - e) << 23);
-    uint16_t h1[8], h2[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float t = v[j] * up;  // exact (power of two)
-        const __half a = __float2half_rn(t);
-        h1[j] = __half_as_ushort(a);
-        h2[j] = __half_as_ushort(__float2half_rn(t - __half2float(a)));  // the difference is exact in fp32
-    }
-    uint8_t *blk = bq + (size_t)k * 1024 * NP + (size_t)lane * (2 * NP * 16);
-    *reinterpret_cast<uint4 *>(blk + s * 16) =
-        make_uint4(h1[0] | ((uint32_t)h1[2] << 16), h1[1] | ((uint32_t)h1[3] << 16), h1[4] | ((uint32_t)h1[6] << 16),
-                   h1[5] | ((uint32_t)h1[7] << 16));
-    *reinterpret_cast<uint4 *>(blk + (NP + s) * 16) =
-        make_uint4(h2[0] | ((uint32_t)h2[2] << 16), h2[1] | ((uint32_t)h2[3] << 16), h2[4] | ((uint32_t)h2[6] << 16),
-                   h2[5] | ((uint32_t)h2[7] << 16));
-    if (lane == 0) ys[(size_t)k * NP + s] = valid ? down : 0.0f;
+    for (int j = 0; j < 3; j++)
+        *reinterpret_cast<uint2 *>(blk + (size_t)((pass * 3 + j) * npp + sl) * 16) = make_uint2(p[2 * j], p[2 * j + 1]);
+    if (lane == 0) ys[(size_t)k * NP + s] = valid ? y : 0.0f;
 }
 
 // B operand of gemm_bf16tc for the 64-element group g of sequence s, from this lane's elements

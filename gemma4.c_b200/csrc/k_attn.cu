@@ -637,21 +637,12 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     dim3 grid(nch, L.n_kv, B);
     int rc;
     if (L.hd <= 256) {
-        // split length sp = kChunk * 2^j (whole kChunk rows keep the partials within max_chunks),
-        // minimising waves * (fixed cost of a CTA + rows streamed per CTA) over two CTAs per SM.
-        // A CTA's fixed cost (q/k/v prologue, first copy latency, combine and merge) is about
-        // the time it takes to stream kFixedRows rows.
-        constexpr long kFixedRows = 64;
-        int dev = 0, nsm = 148;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-        const long slots = 2L * nsm, pairs = (long)B * L.n_kv;
-        int sp = kChunk;
-        long best = -1;
-        for (int cand = kChunk; cand <= 1024 && cand < 2 * span; cand *= 2) {
-            const long ctas = (long)((span + cand - 1) / cand) * pairs;
-            const long cost = (ctas + slots - 1) / slots * (kFixedRows + std::min(cand, span));
-            if (best < 0 || cost < best) { best = cost; sp = cand; }
-        }
+        // Split length: a fixed number of rows per CTA for each layer kind (128 for a sliding
+        // window, 256 for the global context), never derived from the batch or the cache length.
+        // The float sums of a sequence then follow the same split boundaries whether it is decoded
+        // alone or in a batch, so batched and single-sequence decoding give identical results.
+        // (Both are multiples of kChunk, which keeps the partials within max_chunks.)
+        const int sp = L.window > 0 ? 128 : 256;
         const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
         switch (L.hd) {
         case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;

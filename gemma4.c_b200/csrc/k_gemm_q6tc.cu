@@ -1,31 +1,32 @@
 // k_gemm_q6tc.cu — batched Q6_K GEMM on the tensor cores (tcgen05.mma
-// kind::f16, accumulators and the A operand in tensor memory), for decode
-// steps with 16..64 sequences per GPU: the FFN down projection, V, and the
-// tied LM head (with the softcap + argmax epilogue).
+// kind::i8, int32 accumulators and the A operand in tensor memory), for decode
+// steps with 2..64 sequences per GPU: the FFN down projection, V, and the tied
+// LM head (with the softcap + argmax epilogue).
 //
 // The reference computes Q6_K rows as an fp32 dequant-dot against the fp32
 // activation (mm_quant_rows, gemma4-4b/cpu-blas/main.c:1539-1556; the weight
 // of element k of block b is d * sc_j * (q_k - 32), dequant_q6_k, main.c:
-// 213-237).  Here, per row r, sequence s and super-block b:
-//   v_k = sc_j * (q_k - 32)             integer in [-4064, 4096]
-//       = 64 * (h_k + l_k),  h_k = (v_k + 4096) / 64 - 64 in [-64, 64],
-//                            l_k = ((v_k + 4096) mod 64) / 64
-//   (both exact in fp16), and the activation of block b of sequence s is
-//   scaled by a power of two 2^e (largest |x| in [2^13, 2^14)) and split
-//   into two fp16 parts, x * 2^e = x1 + x2 (to 2^-22 relative).
-//   out[s][r] += 64 * d * 2^-e * sum_k (h_k + l_k) * (x1_k + x2_k).
-// The MMA B operand stacks x1 (rows 0..NP-1) and x2 (rows NP..2NP-1), so
-// every MMA is N = 2*NP (128 at 64 sequences, full tensor rate) and the two
-// halves of the accumulator are added in the epilogue.  All products are
-// exact in fp32; the float sum differs from the reference's sequential
-// fp32 dot only in order and rounding (checked at 1e-5 of the term scale).
+// 213-237).  Here every block product is an exact integer:
+//   v_k = sc_j * (q_k - 32) = 64*h_k + l_k,   h in [-63, 64], l in [0, 63]
+//   X_k = a0_k*2^16 + a1_k*2^8 + a2_k         (the activation on the block's
+//                                             fixed-point grid, q6x_block)
+//   D_j = sum_k v_k a_jk = 64*sum h a_j + sum l a_j   (int32, exact)
+// so two weight planes (h, l) times three activation pieces give the block
+// dot sum_k v_k X_k = D_0*2^16 + D_1*2^8 + D_2 exactly, in any order.  The
+// epilogue rounds it to float once per block and accumulates
+//   P = fma(float(dot), d * 2^(E-22), P)
+// block by block in the canonical row order (RowOrder), exactly as the
+// streaming GEMV does: batched and single-sequence results are identical.
 //
-// CTA layout (one per SM, persistent) as in the Q4_K kernel: warp 0 bulk
-// tensor copies (TMA) of 128-row x 1-super-block weight tiles and bulk copies
-// of the B operand; warp 1 owns TMEM, one lane issues the MMAs; warps 2..9
-// expand the 6-bit quants into the A operand in TMEM (tcgen05.st), warp
-// group e = half e of the block; warps 10..17 run the per-block epilogue
-// for half of the sequences each.  Every wait is bounded (2 s).
+// CTA layout (one per SM, persistent): warp 0 bulk tensor copies (TMA) of
+// 128-row x 1-super-block weight tiles and bulk copies of the B operand;
+// warp 1 owns TMEM, one lane issues the MMAs; warps 2..9 expand the 6-bit
+// quants into the int8 planes of A in TMEM (tcgen05.st), warp group e = half
+// e of the block; warps 10..17 run the per-block epilogue for half of the
+// sequences of each MMA pass.  The MMA N is 3 pieces x NPP sequences
+// (NPP = 32, two passes at 64 sequences), and the accumulators of
+// consecutive passes alternate between two TMEM buffers.  Every wait is
+// bounded (2 s).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -33,6 +34,7 @@
 #include "g4_async.cuh"
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
+#include "g4_quant.cuh"
 #include "g4_tc.cuh"
 
 namespace g4 {
@@ -41,6 +43,7 @@ namespace {
 
 constexpr int kQ6Threads = 576;
 constexpr int kQ6RawStages = 3;
+constexpr int kQ6BStages = 2;
 
 // The device row of a Q6_K matrix is stored as planes: ql (128 B per
 // super-block), qh (64 B), scales (16 B), d (2 B).  A raw tile (128 rows x
@@ -53,27 +56,28 @@ struct Q6Maps {
 constexpr int kQ6QhOff = 16384, kQ6ScOff = 24576;
 
 template <int NP>
-struct Q6Smem {
-    static constexpr int raw = 128 * 208;            // ql, qh, sc of one super-block for 128 rows
-    static constexpr int bst = 1024 * NP;            // 256 x 2*NP fp16
-    static constexpr int bstages = NP == 64 ? 2 : 3;
+struct Q6Cfg {
+    static constexpr int NPP = NP < 32 ? NP : 32;  // sequences per MMA pass
+    static constexpr int NPASS = NP / NPP;          // passes per super-block
+    static constexpr int N = 3 * NPP;               // MMA N: three activation pieces
+    static constexpr int SP = NPP / 2;              // sequences per epilogue warp and pass
+    static constexpr int raw = 128 * 208;           // ql, qh, sc of one super-block for 128 rows
+    static constexpr int bst = 768 * NP;            // B operand of one super-block
     static constexpr int b_off = kQ6RawStages * raw;
-    static constexpr int total = b_off + bstages * bst + 1024;
-};
-// TMEM columns: two accumulators of N = 2*NP, then four quarters of A
-// (64 weights: 32 columns of h, 32 of l).
-template <int NP>
-struct Q6Tmem {
-    static constexpr uint32_t a = 4 * NP;
-    static_assert(a + 256 <= 512, "TMEM columns");
+    static constexpr int total = b_off + kQ6BStages * bst + 1024;
+    // TMEM: two accumulator buffers [D_h | D_l] of N columns each, then A: plane h (64 columns of
+    // 4 int8 weights), plane l (64)
+    static constexpr uint32_t acc = 2 * N;
+    static constexpr uint32_t a = 2 * acc;
+    static_assert(a + 128 <= 512, "TMEM columns");
 };
 
 struct Q6State {
-    uint64_t raw_full[kQ6RawStages], raw_empty[kQ6RawStages], b_full[3], b_empty[3];
+    uint64_t raw_full[kQ6RawStages], raw_empty[kQ6RawStages], b_full[kQ6BStages], b_empty[kQ6BStages];
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
-    float ys[8][2][32];  // per epilogue warp: 64*d-free activation scales 2^-e of its sequences, by parity
+    float ys[8][2][16];  // per epilogue warp: activation block scales of its sequences, by item parity
 };
 
 __device__ __forceinline__ bool q6_wait(Q6State &S, uint64_t *bar, uint32_t parity) {
@@ -90,30 +94,26 @@ __device__ __forceinline__ void q6_fail(Q6State &S, int *err) {
     if (err) atomicExch(err, G4_ERR_TIMEOUT);
 }
 
-// 4 quants (bytes of qb, values 0..63) of one sub-block with scale sc ->
-// columns (h, l) for the byte pairs (0, 2) and (1, 3).
-__device__ __forceinline__ void q6_expand4(uint32_t qb, int sc, uint32_t C, uint32_t &h0, uint32_t &h1, uint32_t &l0,
-                                           uint32_t &l1) {
-    // u = sc*(q-32) + 4096 in [32, 8192], two 16-bit lanes per word (exact: the sum of the lanes is
-    // non-negative and below 2^32 even when sc*q borrows)
-    const uint32_t u0 = (qb & 0x00FF00FFu) * (uint32_t)sc + C;
-    const uint32_t u1 = ((qb >> 8) & 0x00FF00FFu) * (uint32_t)sc + C;
-    // h = (1024 + u/64) - 1088; l = (1024 + u%64)/64 - 16   (fp16, exact)
-    h0 = hadd2_u(((u0 >> 6) & 0x00FF00FFu) | 0x64006400u, 0xE440E440u);
-    h1 = hadd2_u(((u1 >> 6) & 0x00FF00FFu) | 0x64006400u, 0xE440E440u);
-    l0 = hfma2_u((u0 & 0x003F003Fu) | 0x64006400u, 0x24002400u, 0xCC00CC00u);
-    l1 = hfma2_u((u1 & 0x003F003Fu) | 0x64006400u, 0x24002400u, 0xCC00CC00u);
+// 4 quants q (bytes of qb, 0..63) of one sub-block with scale sc -> the int8 columns of the two
+// weight planes: v = sc*(q-32) = 64*h + l.  u = v + 4096 in [32, 8192] is formed in two 16-bit
+// lanes per word (exact: each lane's value is non-negative and below 2^16).
+__device__ __forceinline__ void q6_planes(uint32_t qb, int sc, uint32_t &h, uint32_t &l) {
+    const uint32_t C = (uint32_t)(4096 - 32 * sc) * 0x00010001u;
+    const uint32_t u0 = (qb & 0x00FF00FFu) * (uint32_t)sc + C;         // quants 0, 2
+    const uint32_t u1 = ((qb >> 8) & 0x00FF00FFu) * (uint32_t)sc + C;  // quants 1, 3
+    h = __vsub4(((u0 >> 6) & 0x00FF00FFu) | (((u1 >> 6) & 0x00FF00FFu) << 8), 0x40404040u);
+    l = (u0 & 0x003F003Fu) | ((u1 & 0x003F003Fu) << 8);
 }
 
 template <int NP>
 __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_constant__ Q6Maps maps, TcArgs a) {
-    constexpr int RAW = Q6Smem<NP>::raw, BST = Q6Smem<NP>::bst, BS = Q6Smem<NP>::bstages, RS = kQ6RawStages;
-    constexpr int SP = NP / 2;  // sequences per epilogue warp
-    using TM = Q6Tmem<NP>;
+    using CF = Q6Cfg<NP>;
+    constexpr int RAW = CF::raw, BST = CF::bst, BS = kQ6BStages, RS = kQ6RawStages;
+    constexpr int NPP = CF::NPP, NPASS = CF::NPASS, N = CF::N, SP = CF::SP;
     extern __shared__ uint8_t smem_dyn[];
     __shared__ Q6State S;
     uint8_t *smem = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
-    uint8_t *raw = smem, *bst = smem + Q6Smem<NP>::b_off;
+    uint8_t *raw = smem, *bst = smem + CF::b_off;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_trigger();
     if (tid == 0) {
@@ -181,40 +181,41 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc(1, 0, 0, 2 * NP);  // f32 += f16 * f16, N = 2*NP
+            constexpr uint32_t idesc = umma_idesc(2, 1, 1, N);  // s32 += s8 * s8, N = 3 * NPP
             int i = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
                 const int b0 = (u % a.ksplit) * a.kslice, b1 = min(a.nb, b0 + a.kslice);
                 for (int b = b0; b < b1 && ok; b++, i++) {
-                    const int abuf = i & 1, bs = i % BS;
-                    const uint32_t pa = i & 1;
-                    {   // accumulator and B stage tested together; each A quarter just before its MMAs
-                        const bool r0 = mbar_try_wait(&S.acc_empty[abuf], ((i >> 1) & 1) ^ 1);
-                        const bool r1 = mbar_try_wait(&S.b_full[bs], (i / BS) & 1);
-                        if (!(r0 && r1)) {
-                            if (!q6_wait(S, &S.acc_empty[abuf], ((i >> 1) & 1) ^ 1) ||
-                                !q6_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
-                        }
-                    }
+                    const int bs = i % BS;
+                    if (!q6_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
                     const uint32_t bsa = smem_u32(bst + bs * BST);
-                    const uint32_t d = tbase + abuf * 2 * NP;
-                    for (int qi = 0; qi < 4; qi++) {
-                        const int q = ((qi & 1) << 1) | (qi >> 1);  // 0, 2, 1, 3: the order the expand warps finish
-                        if (!mbar_try_wait(&S.a_full[q], pa) && !q6_wait(S, &S.a_full[q], pa)) { ok = false; break; }
+                    for (int ps = 0; ps < NPASS && ok; ps++) {
+                        const int it = i * NPASS + ps, buf = it & 1;
+                        if (!q6_wait(S, &S.acc_empty[buf], ((it >> 1) & 1) ^ 1)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t acol = tbase + TM::a + 64 * q;
+                        const uint32_t dh = tbase + buf * CF::acc, dl = dh + N;
+                        for (int qi = 0; qi < 4; qi++) {
+                            const int q = ((qi & 1) << 1) | (qi >> 1);  // 0, 2, 1, 3: the order the expand warps finish
+                            if (ps == 0) {
+                                if (!mbar_try_wait(&S.a_full[q], i & 1) && !q6_wait(S, &S.a_full[q], i & 1)) { ok = false; break; }
+                                tc_fence_after();
+                            }
 #pragma unroll
-                        for (int ks = 0; ks < 4; ks++) {
-                            const uint64_t bd = umma_desc(bsa + (8 * q + 2 * ks) * (2 * NP) * 16, 2 * NP * 16, 128);
-                            tc_mma_f16_ts(d, acol + 8 * ks, bd, idesc, (qi | ks) != 0);  // h
-                            tc_mma_f16_ts(d, acol + 32 + 8 * ks, bd, idesc, 1);           // l
+                            for (int ks = 0; ks < 2; ks++) {
+                                const uint64_t bd = umma_desc(bsa + (4 * q + 2 * ks) * (3 * NP * 16) + ps * N * 16,
+                                                              3 * NP * 16, 128);
+                                const uint32_t acc = (qi | ks) != 0;
+                                tc_mma_i8_ts(dh, tbase + CF::a + 16 * q + 8 * ks, bd, idesc, acc);
+                                tc_mma_i8_ts(dl, tbase + CF::a + 64 + 16 * q + 8 * ks, bd, idesc, acc);
+                            }
+                            if (ps == NPASS - 1) tc_commit(&S.a_empty[q]);
                         }
-                        tc_commit(&S.a_empty[q]);
+                        if (!ok) break;
+                        tc_commit(&S.acc_full[buf]);
                     }
                     if (!ok) break;
                     tc_commit(&S.b_empty[bs]);
-                    tc_commit(&S.acc_full[abuf]);
                 }
             }
             if (!ok) q6_fail(S, a.err);
@@ -255,37 +256,23 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                 if (lane == 0) mbar_arrive(&S.raw_empty[rs]);
 #pragma unroll
                 for (int qq = 0; qq < 2; qq++) {
+                    // quarter q = weights 128e + 64qq + [0, 64): column c' = 8t' + w holds weights l = 4w..4w+3 of
+                    // group t = 2qq + t' (quant from ql[l + 32t'], low nibble for qq 0 / high for qq 1, bits 2t of
+                    // qh[l], scale sc[l/16 + 2t])
                     const int q = 2 * e + qq;
-                    // qq = 0: weights l, l+32 (low nibbles, qh bits 0-1 / 2-3), scales sc[0..3] of the half;
-                    // qq = 1: weights l+64, l+96 (high nibbles, qh bits 4-5 / 6-7), scales sc[4..7]
-                    const uint32_t swq = qq ? sw1 : sw0;
-                    int scs[4];
-                    uint32_t cs[4];
-#pragma unroll
-                    for (int t = 0; t < 4; t++) {
-                        scs[t] = (int)(int8_t)(swq >> (8 * t));
-                        cs[t] = (uint32_t)(4096 - 32 * scs[t]) * 0x00010001u;
-                    }
                     if (!q6_wait(S, &S.a_empty[q], (i & 1) ^ 1)) { ok = false; break; }
+                    uint32_t ch[16], cl[16];
 #pragma unroll
-                    for (int set = 0; set < 2; set++) {  // set 0: weights l (scales t=0,1); set 1: l+32 (t=2,3)
-#pragma unroll
-                        for (int hf = 0; hf < 2; hf++) {  // 16 weights of scale t = 2*set + hf: 8 columns of h, of l
-                            const int t = 2 * set + hf;
-                            uint32_t ch[8], cl[8];
-#pragma unroll
-                            for (int ww = 0; ww < 4; ww++) {
-                                const int w = 4 * hf + ww;
-                                const uint32_t lw = ql[8 * set + w], hw = qh[w];
-                                uint32_t qb;
-                                if (qq == 0) qb = (lw & 0x0F0F0F0Fu) | ((set ? (hw << 2) : (hw << 4)) & 0x30303030u);
-                                else qb = ((lw >> 4) & 0x0F0F0F0Fu) | ((set ? (hw >> 2) : hw) & 0x30303030u);
-                                q6_expand4(qb, scs[t], cs[t], ch[2 * ww], ch[2 * ww + 1], cl[2 * ww], cl[2 * ww + 1]);
-                            }
-                            tc_st8(tl + TM::a + 64 * q + 16 * set + 8 * hf, ch);
-                            tc_st8(tl + TM::a + 64 * q + 32 + 16 * set + 8 * hf, cl);
-                        }
+                    for (int cc = 0; cc < 16; cc++) {
+                        const int tp = cc >> 3, w = cc & 7, t = 2 * qq + tp;
+                        const uint32_t lw = ql[w + 8 * tp];
+                        const uint32_t qb = ((qq ? (lw >> 4) : lw) & 0x0F0F0F0Fu) | (((qh[w] >> (2 * t)) & 0x03030303u) << 4);
+                        const int sidx = (w >> 2) + 2 * t;
+                        const int sc = (int)(int8_t)(((sidx < 4 ? sw0 : sw1) >> (8 * (sidx & 3))) & 0xffu);
+                        q6_planes(qb, sc, ch[cc], cl[cc]);
                     }
+                    tc_st16(tl + CF::a + 16 * q, ch);
+                    tc_st16(tl + CF::a + 64 + 16 * q, cl);
                     tc_wait_st();
                     tc_fence_before();
                     __syncwarp();
@@ -300,107 +287,93 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
         const int quad = warp & 3, p = (warp - 10) >> 2, pw = warp - 10, r = 32 * quad + lane;
         const uint32_t tl = tbase + ((uint32_t)(32 * quad) << 16);
         pdl_wait();
-        unsigned long long acc[SP / 2];
+        float P[NPASS][SP];
 #pragma unroll
-        for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
+        for (int ps = 0; ps < NPASS; ps++)
+#pragma unroll
+            for (int s = 0; s < SP; s++) P[ps][s] = 0.0f;
         int i = 0;
         bool ok = true;
-        // per block: d of row r (fp16 after the quant planes of the row) and the activation scale of
-        // sequence p*SP + lane, loaded one block ahead and converted only when used, so the load
-        // latency overlaps the current block
-        auto fetch = [&](int u, int b, uint16_t &hd, float &yl) {
-            const int row = (u / a.ksplit) * 128 + r;
-            hd = 0;
-            if (row < a.rows) hd = __ldg(reinterpret_cast<const uint16_t *>(a.w + (size_t)row * a.row_bytes + (size_t)a.nb * 208) + b);
-            yl = lane < SP ? __ldg(a.yd + (size_t)b * NP + p * SP + lane) : 0.0f;
-        };
-        // final values of sequences p*SP + 2s, +1 for row `row`
-        auto emit = [&](int row, int s, float v0, float v1) {
-            const int seq = p * SP + 2 * s;
+        // final value v of sequence seq for row `row`
+        auto emit = [&](int row, int seq, float v, unsigned long long &key) {
             if (a.epi == EPI_SOFTCAP_ARGMAX) {  // logits softcap (main.c:1780-1796), then argmax over rows
-                if (a.cap > 0.0f) {
-                    v0 = a.cap * tanhf(v0 / a.cap);
-                    v1 = a.cap * tanhf(v1 / a.cap);
-                }
-                unsigned long long k0 = row < a.rows ? argmax_key(v0, row) : 0ull;
-                unsigned long long k1 = row < a.rows ? argmax_key(v1, row) : 0ull;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long t0 = __shfl_xor_sync(0xffffffffu, k0, o);
-                    const unsigned long long t1 = __shfl_xor_sync(0xffffffffu, k1, o);
-                    k0 = t0 > k0 ? t0 : k0;
-                    k1 = t1 > k1 ? t1 : k1;
-                }
-                if (lane == 0) {
-                    if (seq < a.B) atomicMax(a.keys + seq, k0);
-                    if (seq + 1 < a.B) atomicMax(a.keys + seq + 1, k1);
-                }
+                if (a.cap > 0.0f) v = a.cap * tanhf(v / a.cap);
+                key = row < a.rows ? argmax_key(v, row) : 0ull;
                 if (!a.out) return;
             }
-            if (row < a.rows) {
-                if (seq < a.B) a.out[(size_t)seq * a.ldo + row] = v0;
-                if (seq + 1 < a.B) a.out[(size_t)(seq + 1) * a.ldo + row] = v1;
-            }
+            if (row < a.rows && seq < a.B) a.out[(size_t)seq * a.ldo + row] = v;
         };
-        auto finish = [&](int u) {  // final values, or this K slice's partial (summed by tc_merge_kernel)
+        auto finish = [&](int u) {  // end of this CTA's K slice of a row tile: final values or the slice's partial
             const int ks = u % a.ksplit, row = (u / a.ksplit) * 128 + r;
-            if (a.ksplit == 1) {
 #pragma unroll
-                for (int s = 0; s < SP / 2; s++) {
-                    const float2 f = f2_unpack(acc[s]);
-                    emit(row, s, f.x, f.y);
-                    acc[s] = 0ull;
+            for (int ps = 0; ps < NPASS; ps++)
+#pragma unroll
+                for (int s = 0; s < SP; s++) {
+                    const int seq = ps * NPP + p * SP + s;
+                    if (a.ksplit == 1) {
+                        unsigned long long key = 0ull;
+                        emit(row, seq, P[ps][s], key);
+                        if (a.epi == EPI_SOFTCAP_ARGMAX) {
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+                                key = t > key ? t : key;
+                            }
+                            if (lane == 0 && seq < a.B && key) atomicMax(a.keys + seq, key);
+                        }
+                    } else if (row < a.rows) {  // all NP slots of the partial exist: no per-sequence bound
+                        a.part[((size_t)ks * NP + seq) * a.rows + row] = P[ps][s];
+                    }
+                    P[ps][s] = 0.0f;
                 }
-                return;
-            }
-            if (row < a.rows) {  // all NP slots of the partial exist: no per-sequence bound
-                float *dst = a.part + ((size_t)ks * NP + p * SP) * a.rows + row;
-                const size_t st = (size_t)a.rows;
-#pragma unroll
-                for (int s = 0; s < SP / 2; s++) {
-                    const float2 f = f2_unpack(acc[s]);
-                    dst[(size_t)(2 * s) * st] = f.x;
-                    dst[(size_t)(2 * s + 1) * st] = f.y;
-                }
-            }
-#pragma unroll
-            for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
         };
         int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
-        uint16_t nhd = 0;
-        float nyl = 0.f;
-        if (u < a.units) fetch(u, b, nhd, nyl);
+        // d of row r for the block (fp16 after the quant planes of the row), loaded one block ahead
+        auto fetch_d = [&](int uu, int bb) -> uint16_t {
+            const int row = (uu / a.ksplit) * 128 + r;
+            return row < a.rows ? __ldg(reinterpret_cast<const uint16_t *>(a.w + (size_t)row * a.row_bytes + (size_t)a.nb * 208) + bb)
+                                : (uint16_t)0;
+        };
+        uint16_t nhd = u < a.units ? fetch_d(u, b) : (uint16_t)0;
         while (u < a.units && ok) {
             const int b1 = min(a.nb, (u % a.ksplit) * a.kslice + a.kslice);
-            const uint16_t hd = nhd;
-            if (lane < SP) S.ys[pw][i & 1][lane] = nyl;
-            __syncwarp();
+            const float dw = f16_to_f32(nhd);
             int nu = u, nbk = b + 1;
             if (nbk >= b1) { nu = u + gridDim.x; nbk = nu < a.units ? (nu % a.ksplit) * a.kslice : 0; }
-            if (nu < a.units) fetch(nu, nbk, nhd, nyl);
-            if (!q6_wait(S, &S.acc_full[i & 1], (i >> 1) & 1)) { ok = false; break; }
-            const float dw = 64.0f * f16_to_f32(hd);
-            tc_fence_after();
-            const float *yv = S.ys[pw][i & 1];
-            const unsigned long long dw2 = f2_pack(dw, dw);
+            if (nu < a.units) nhd = fetch_d(nu, nbk);
 #pragma unroll
-            for (int c = 0; c < SP / 8; c++) {
-                uint32_t v1[8], v2[8];
-                tc_ld8(tl + (i & 1) * 2 * NP + p * SP + 8 * c, v1);       // products with x1
-                tc_ld8(tl + (i & 1) * 2 * NP + NP + p * SP + 8 * c, v2);  // products with x2
-                tc_wait_ld();
-                if (c == SP / 8 - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.acc_empty[i & 1]);
-                }
+            for (int ps = 0; ps < NPASS; ps++) {
+                const int it = i * NPASS + ps, buf = it & 1;
+                if (lane < SP) S.ys[pw][it & 1][lane] = __ldg(a.yd + (size_t)b * NP + ps * NPP + p * SP + lane);
+                __syncwarp();
+                if (!q6_wait(S, &S.acc_full[buf], (it >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const float *yv = S.ys[pw][it & 1];
+                const uint32_t col = tl + buf * CF::acc + p * SP;
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const unsigned long long t = f2_add(f2_pack_u(v1[2 * k], v1[2 * k + 1]), f2_pack_u(v2[2 * k], v2[2 * k + 1]));
-                    const float2 y = *reinterpret_cast<const float2 *>(yv + 8 * c + 2 * k);
-                    acc[4 * c + k] = f2_fma(f2_mul(dw2, f2_pack(y.x, y.y)), t, acc[4 * c + k]);
+                for (int c = 0; c < SP / 8; c++) {
+                    uint32_t h0[8], h1[8], h2[8], l0[8], l1[8], l2[8];
+                    tc_ld8(col + 8 * c, h0);
+                    tc_ld8(col + NPP + 8 * c, h1);
+                    tc_ld8(col + 2 * NPP + 8 * c, h2);
+                    tc_ld8(col + N + 8 * c, l0);
+                    tc_ld8(col + N + NPP + 8 * c, l1);
+                    tc_ld8(col + N + 2 * NPP + 8 * c, l2);
+                    tc_wait_ld();
+                    if (c == SP / 8 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        const float dot = q6x_dot(64 * (int)h0[k] + (int)l0[k], 64 * (int)h1[k] + (int)l1[k],
+                                                  64 * (int)h2[k] + (int)l2[k]);
+                        P[ps][8 * c + k] = __fmaf_rn(dot, __fmul_rn(dw, yv[8 * c + k]), P[ps][8 * c + k]);
+                    }
                 }
             }
+            if (!ok) break;
             if (nu != u) finish(u);
             u = nu; b = nbk; i++;
         }
@@ -414,12 +387,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
     }
 }
 
-// B operand of gemm_q6tc for super-block k: the activation of every sequence
-// scaled by 2^e_s (largest |x| of the block in [2^13, 2^14)) and split into
-// fp16 x1 + x2, as 2*NP rows (x1 of sequence s in row s, x2 in row NP+s) of
-// K-major core matrices: byte (k'/8)*(2*NP*16) + row*16 + (k'%8)*2, with
-// k' = weight index with positions 1 and 2 of every 4 swapped (the order the
-// expand warps write A in).  ys[k][s] = 2^-e_s (0 for padding sequences).
+// B operand of gemm_q6tc (tc6_store_block layout) from fp32 activations.
 // grid (nb, NP/8), 256 threads: warp w handles sequence 8*blockIdx.y + w.
 __global__ void tc6_split_kernel(const float *__restrict__ x, int ldx, int B, int NP, uint8_t *__restrict__ bq,
                                  float *__restrict__ ys) {
@@ -473,8 +441,14 @@ int tc6_weight_maps(void *maps_out, const void *w, int n, int rows) {
 }
 size_t tc6_maps_bytes() { return sizeof(Q6Maps); }
 
-size_t tc6_operand_bytes(int n) { return (size_t)(n / G4_QK) * (1024 * 64 + 64 * 4); }
-size_t tc6_ys_offset(int n) { return (size_t)(n / G4_QK) * 1024 * 64; }
+RowOrder q6_row_order(int rows, int n, int nsm, bool argmax) {
+    if (argmax) return RowOrder{0, 0, 0};  // the argmax epilogue keeps whole rows in one CTA
+    const TcPlan p = tc_plan(rows, n / G4_QK, nsm);
+    return RowOrder{0, 0, p.ksplit > 1 ? p.kslice : 0};
+}
+
+size_t tc6_operand_bytes(int n) { return (size_t)(n / G4_QK) * (768 * 64 + 64 * 4); }
+size_t tc6_ys_offset(int n) { return (size_t)(n / G4_QK) * 768 * 64; }
 
 int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *ys, cudaStream_t st) {
     if (n % G4_QK || (ldx % 4) || ((uintptr_t)x & 15u)) { set_error(G4_ERR_ARG, "tc6 split: bad shape/alignment"); return G4_ERR_ARG; }
@@ -503,7 +477,7 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
              p.ksplit, p.kslice, p.units, epi, cap, keys};
 #define G4_Q6TC_CASE(N)                                                                             \
     if (np == N) {                                                                                   \
-        const size_t smem = Q6Smem<N>::total;                                                        \
+        const size_t smem = Q6Cfg<N>::total;                                                         \
         G4_CUDA(launch_pdl(gemm_q6tc_kernel<N>, dim3(p.grid), dim3(kQ6Threads), smem, st, *(const Q6Maps *)maps, a)); \
     }
     G4_Q6TC_CASE(16) else G4_Q6TC_CASE(32) else G4_Q6TC_CASE(64)
@@ -514,9 +488,9 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
 }
 
 int prime_tc6_attrs() {
-    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<16>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<16>::total));
-    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<32>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<32>::total));
-    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<64>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Smem<64>::total));
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<16>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Cfg<16>::total));
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<32>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Cfg<32>::total));
+    G4_CUDA(cudaFuncSetAttribute(q6tc_kernel_ptr<64>(), cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Cfg<64>::total));
     return G4_OK;
 }
 

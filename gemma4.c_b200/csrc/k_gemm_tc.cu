@@ -944,6 +944,17 @@ Q4Plan q4_plan(int tiles, int nb, int nsm) {
     return best;
 }
 
+RowOrder q4_row_order(int rows_a, int rows_b, int n, int nsm, int which) {
+    const int nb = n / G4_QK, ta = (rows_a + 127) / 128, tb = rows_b > 0 ? (rows_b + 127) / 128 : 0;
+    const Q4Plan p = q4_plan(ta + tb, nb, nsm);
+    return RowOrder{which ? ta : 0, p.share, 0};
+}
+
+RowOrder q5_row_order(int rows, int n, int nsm) {
+    const TcPlan p = tc_plan(rows, n / G4_QK, nsm);
+    return RowOrder{0, 0, p.ksplit > 1 ? p.kslice : 0};
+}
+
 size_t tc_part_bytes(int rows, int n, int nsm) {
     const TcPlan p = tc_plan(rows, n / G4_QK, nsm);
     const int tiles = (rows + 127) / 128;

@@ -37,16 +37,13 @@ constexpr int kTmGroups = kTmConsumerWarps * 4;       // consumer lane groups
 constexpr int kTmThreads = (kTmConsumerWarps + 1) * 32;  // + producer warp
 constexpr int kTmMaxStages = 6;
 
-__device__ __forceinline__ float tm_q6(uint32_t w, int i) {  // byte i (0..63) -> q - 32, exact
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + i)) - 8388640.0f;
-}
-
 // ---------------------------------------------------------------- activation
 struct TmAct {
     int8_t *qs;   // [NB][n]      Q8_K quants           (Q4/Q5)
-    float *dx;    // [NB][nb]     Q8_K block scales
-    int *bs2;     // [NB][nb][8]  sums of 32 quants per sub-block
-    float *x;     // [NB][n]      fp32 activation       (Q6)
+    float *dx;    // [NB][nb]     Q8_K block scales     (Q4/Q5)
+    int *bs2;     // [NB][nb][8]  sums of 32 quants per sub-block (Q4/Q5)
+    int8_t *pc;   // [NB][3][n]   fixed-point activation pieces (Q6, q6x_block)
+    float *ys;    // [NB][nb]     their block scales 2^(E-22) (Q6)
 };
 
 // Q4_K/Q5_K block meta (d, dmin, 12 scale bytes) -> this lane's two 6-bit
@@ -63,44 +60,61 @@ __device__ __forceinline__ void tm_scales(const uint4 &m, int j, int c, int &sc_
     mn_c = (int)__byte_perm(mn03, mn47, 0x4440 | c) & 0xff;
 }
 
-// One super-block k of one row (in shared memory) against NB activations.
+// Sum over the 8 lanes of this lane's group (lanes 8q..8q+7); exact for ints.
+__device__ __forceinline__ int grp_sum(int v, unsigned mask) {
+    v += __shfl_xor_sync(mask, v, 1);
+    v += __shfl_xor_sync(mask, v, 2);
+    v += __shfl_xor_sync(mask, v, 4);
+    return v;
+}
+
+// One super-block k of one row (in shared memory) against NB activations:
+// the 8 lanes of the group each cover 32 weights, their integer partial sums
+// are added across the group (exact), and lane c == 0 writes the block's
+// canonical term pair (a, c) of every sequence to tw[s] (RowOrder):
+//   Q4_K/Q5_K: a = d_x, c = fma(d, float(sumi_s), -(dmin * sumi_m))
+//              (vec_dot_q4_K_q8_K / q5, main.c:347-593, integer sums exact);
+//   Q6_K:      a = float(sum_i v_i X_i), c = d * 2^(E-22)
+//              (v = sc*(q-32) of dequant_q6_k, main.c:213-237; X = q6x_block).
 template <int TYPE, int NB>
 __device__ __forceinline__ void tm_block(const uint8_t *row, int nb, int n, int k, const TmAct &A, int nbc,
-                                         float (&acc)[NB], int c) {
+                                         float2 *tw, int c, unsigned gmask) {
     if (TYPE == G4_Q6_K) {
         const int n6 = c >> 2, second = (c >> 1) & 1, par = c & 1, sidx = 2 * second + par;
         const uint4 ql4 = reinterpret_cast<const uint4 *>(row)[k * 8 + c];
         const uint4 qh4 = reinterpret_cast<const uint4 *>(row + (size_t)nb * 128)[k * 4 + 2 * n6 + par];
         const uint2 sc = reinterpret_cast<const uint2 *>(row + (size_t)nb * 192)[k * 2 + n6];
         const float d = f16_to_f32(reinterpret_cast<const uint16_t *>(row + (size_t)nb * 208)[k]);
-        const float dsl = d * (float)(int)(int8_t)((sc.x >> (8 * sidx)) & 0xffu);
-        const float dsh = d * (float)(int)(int8_t)((sc.y >> (8 * sidx)) & 0xffu);
+        const int sl = (int)(int8_t)((sc.x >> (8 * sidx)) & 0xffu);
+        const int sh = (int)(int8_t)((sc.y >> (8 * sidx)) & 0xffu);
         const uint32_t ql[4] = {ql4.x, ql4.y, ql4.z, ql4.w}, qh[4] = {qh4.x, qh4.y, qh4.z, qh4.w};
-        uint32_t lo[4], hi[4];
+        uint32_t lo[4], hi[4];  // q - 32 as signed bytes
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            lo[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * second)) & 0x03030303u) << 4);
-            hi[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (4 + 2 * second)) & 0x03030303u) << 4);
+            lo[i] = __vsub4((ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * second)) & 0x03030303u) << 4), 0x20202020u);
+            hi[i] = __vsub4(((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (4 + 2 * second)) & 0x03030303u) << 4), 0x20202020u);
         }
         const int e_lo = k * G4_QK + 128 * n6 + 32 * second + 16 * par;
 #pragma unroll
         for (int s = 0; s < NB; s++) {
             if (s >= nbc) break;
-            const float4 *xl = reinterpret_cast<const float4 *>(A.x + (size_t)s * n + e_lo);
-            float a = acc[s];
+            int D[3];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float4 vl = xl[i], vh = xl[16 + i];  // +64 elements
-                a = fmaf(vl.x, dsl * tm_q6(lo[i], 0), a);
-                a = fmaf(vl.y, dsl * tm_q6(lo[i], 1), a);
-                a = fmaf(vl.z, dsl * tm_q6(lo[i], 2), a);
-                a = fmaf(vl.w, dsl * tm_q6(lo[i], 3), a);
-                a = fmaf(vh.x, dsh * tm_q6(hi[i], 0), a);
-                a = fmaf(vh.y, dsh * tm_q6(hi[i], 1), a);
-                a = fmaf(vh.z, dsh * tm_q6(hi[i], 2), a);
-                a = fmaf(vh.w, dsh * tm_q6(hi[i], 3), a);
+            for (int j = 0; j < 3; j++) {
+                const int8_t *pj = A.pc + ((size_t)s * 3 + j) * n;
+                const uint4 xl = *reinterpret_cast<const uint4 *>(pj + e_lo);
+                const uint4 xh = *reinterpret_cast<const uint4 *>(pj + e_lo + 64);
+                int dl = __dp4a((int)lo[0], (int)xl.x, 0);
+                dl = __dp4a((int)lo[1], (int)xl.y, dl);
+                dl = __dp4a((int)lo[2], (int)xl.z, dl);
+                dl = __dp4a((int)lo[3], (int)xl.w, dl);
+                int dh = __dp4a((int)hi[0], (int)xh.x, 0);
+                dh = __dp4a((int)hi[1], (int)xh.y, dh);
+                dh = __dp4a((int)hi[2], (int)xh.z, dh);
+                dh = __dp4a((int)hi[3], (int)xh.w, dh);
+                D[j] = grp_sum(sl * dl + sh * dh, gmask);
             }
-            acc[s] = a;
+            if (c == 0) tw[s] = make_float2(q6x_dot(D[0], D[1], D[2]), __fmul_rn(d, A.ys[s * nb + k]));
         }
         return;
     }
@@ -142,11 +156,25 @@ __device__ __forceinline__ void tm_block(const uint8_t *row, int nb, int n, int 
         dh = __dp4a((int)hi[1], (int)ah.y, dh);
         dh = __dp4a((int)hi[2], (int)ah.z, dh);
         dh = __dp4a((int)hi[3], (int)ah.w, dh);
-        const float dx = A.dx[s * (n / G4_QK) + k];
-        const int ps = sc_lo * dl + sc_hi * dh;
-        const int pm = mn_c * A.bs2[(s * (n / G4_QK) + k) * 8 + c];
-        acc[s] = fmaf(dx * dw, (float)ps, fmaf(-(dx * dmw), (float)pm, acc[s]));
+        const int S = grp_sum(sc_lo * dl + sc_hi * dh, gmask);
+        const int M = grp_sum(mn_c * A.bs2[(s * (n / G4_QK) + k) * 8 + c], gmask);
+        if (c == 0)
+            tw[s] = make_float2(A.dx[s * (n / G4_QK) + k],
+                                __fmaf_rn(dw, __int2float_rn(S), __fmul_rn(-dmw, __int2float_rn(M))));
     }
+}
+
+// The canonical fold of one row's block terms (RowOrder): terms of block b of
+// sequence s at t[b * NB + s].
+template <int NB>
+__device__ __forceinline__ float tm_fold(const float2 *t, int nb, int s, const RowOrder &o, int row) {
+    float v = 0.0f, P = 0.0f;
+    for (int b = 0; b < nb; b++) {
+        if (seg_start(o, row, nb, b)) { v = __fadd_rn(v, P); P = 0.0f; }
+        const float2 ab = t[b * NB + s];
+        P = __fmaf_rn(ab.x, ab.y, P);
+    }
+    return __fadd_rn(v, P);
 }
 
 // Stage (or compute, with the fused prologue) the activation of sequences
@@ -155,36 +183,47 @@ template <int TYPE>
 __device__ __forceinline__ void tm_stage(const GemvJobs &jobs, const GemvJob &J, TmAct &A, float *pro_x, int s0,
                                          int nbc, bool writer, float *pred) {
     const int n = J.n, nb = n / G4_QK, tid = threadIdx.x, lane = tid & 31, nt = blockDim.x;
+    const int warp = tid >> 5, nw = nt >> 5;
     if (jobs.has_pro) {
         Prologue P = jobs.pro;
         P.x_in += (size_t)s0 * P.dim;
         if (P.delta) P.delta += (size_t)s0 * P.dim;
         if (P.x_out) P.x_out += (size_t)s0 * P.dim;
         if (P.xn_out) P.xn_out += (size_t)s0 * P.dim;
-        float *xs = TYPE == G4_Q6_K ? A.x : pro_x;
-        prologue_run(P, nbc, xs, nullptr, writer, pred);
-        if (TYPE != G4_Q6_K) {  // quantize into planes (quantize_row_q8_K, main.c:282-340)
-            const int warp = tid >> 5, nw = nt >> 5;
-            for (int t = warp; t < nbc * nb; t += nw) {
-                const int s = t / nb, k = t % nb;
-                uint32_t q[2];
-                float d;
-                int ls;
-                warp_quant_block(xs + (size_t)s * n + (size_t)k * G4_QK, lane, q, d, ls);
-                uint32_t *dst = reinterpret_cast<uint32_t *>(A.qs + (size_t)s * n + (size_t)k * G4_QK + 8 * lane);
-                dst[0] = q[0];
-                dst[1] = q[1];
-                int sub = ls + __shfl_xor_sync(0xffffffffu, ls, 1);
-                sub += __shfl_xor_sync(0xffffffffu, sub, 2);
-                if ((lane & 3) == 0) A.bs2[(s * nb + k) * 8 + (lane >> 2)] = sub;
-                if (lane == 0) A.dx[s * nb + k] = d;
-            }
+        prologue_run(P, nbc, pro_x, nullptr, writer, pred);
+    }
+    if (TYPE == G4_Q6_K) {  // fp32 (prologue output or the global activation) -> fixed-point pieces
+        for (int t = warp; t < nbc * nb; t += nw) {
+            const int s = t / nb, k = t % nb;
+            const float *src = jobs.has_pro ? pro_x + (size_t)s * n + (size_t)k * G4_QK
+                                            : (const float *)J.act + (size_t)(s0 + s) * J.act_stride + (size_t)k * G4_QK;
+            float v[8];
+            const float4 a = *reinterpret_cast<const float4 *>(src + 8 * lane);
+            const float4 b = *reinterpret_cast<const float4 *>(src + 8 * lane + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            uint32_t pw[6];
+            float ys;
+            q6x_block(v, pw, ys);
+#pragma unroll
+            for (int jj = 0; jj < 3; jj++)
+                *reinterpret_cast<uint2 *>(A.pc + ((size_t)s * 3 + jj) * n + (size_t)k * G4_QK + 8 * lane) =
+                    make_uint2(pw[2 * jj], pw[2 * jj + 1]);
+            if (lane == 0) A.ys[s * nb + k] = ys;
         }
-    } else if (TYPE == G4_Q6_K) {
-        for (int s = 0; s < nbc; s++) {
-            const float4 *src = reinterpret_cast<const float4 *>((const float *)J.act + (size_t)(s0 + s) * J.act_stride);
-            float4 *dst = reinterpret_cast<float4 *>(A.x + (size_t)s * n);
-            for (int i = tid; i < n / 4; i += nt) dst[i] = src[i];
+    } else if (jobs.has_pro) {  // quantize into planes (quantize_row_q8_K, main.c:282-340)
+        for (int t = warp; t < nbc * nb; t += nw) {
+            const int s = t / nb, k = t % nb;
+            uint32_t q[2];
+            float d;
+            int ls;
+            warp_quant_block(pro_x + (size_t)s * n + (size_t)k * G4_QK, lane, q, d, ls);
+            uint32_t *dst = reinterpret_cast<uint32_t *>(A.qs + (size_t)s * n + (size_t)k * G4_QK + 8 * lane);
+            dst[0] = q[0];
+            dst[1] = q[1];
+            int sub = ls + __shfl_xor_sync(0xffffffffu, ls, 1);
+            sub += __shfl_xor_sync(0xffffffffu, sub, 2);
+            if ((lane & 3) == 0) A.bs2[(s * nb + k) * 8 + (lane >> 2)] = sub;
+            if (lane == 0) A.dx[s * nb + k] = d;
         }
     } else {
         const uint8_t *src = (const uint8_t *)J.act + (size_t)s0 * nb * G4_Q8_BYTES;
@@ -209,7 +248,10 @@ struct TmPlan {   // per launch, computed on the host
     int stages;   // ring depth
     int row_bytes;
     int stage_bytes;  // R * tr * row_bytes, 128-aligned
-    int act_bytes;    // activation staging area (precedes the ring)
+    int act_bytes;    // activation staging + prologue scratch + term buffers (precedes the ring)
+    int pro_off;      // offset of the fp32 prologue scratch
+    int term_off;     // offset of the per-warp term buffers
+    int term_warp;    // bytes of one warp's term buffer: (4/gpr) rows x R x nb x NB float2
 };
 
 template <int TYPE, int NB, int R>
@@ -232,20 +274,16 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
     const bool producer = warp == kTmConsumerWarps;
     pdl_trigger();
 
-    TmAct A;
-    {
-        uint8_t *p = smem;
-        if (TYPE == G4_Q6_K) {
-            A.x = (float *)p;
-        } else {
-            A.qs = (int8_t *)p;
-            p += (size_t)NB * n;
-            A.dx = (float *)p;
-            p += (size_t)NB * nb * 4;
-            A.bs2 = (int *)p;
-        }
+    TmAct A{};
+    if (TYPE == G4_Q6_K) {
+        A.pc = (int8_t *)smem;
+        A.ys = (float *)(smem + (((size_t)NB * 3 * n + 15) & ~(size_t)15));
+    } else {
+        A.qs = (int8_t *)smem;
+        A.dx = (float *)(smem + (size_t)NB * n);
+        A.bs2 = (int *)(smem + (size_t)NB * n + (size_t)NB * nb * 4);
     }
-    float *pro_x = (float *)(smem + (TYPE == G4_Q6_K ? 0 : (((size_t)NB * n + (size_t)NB * nb * 36 + 15) & ~(size_t)15)));
+    float *pro_x = (float *)(smem + plan.pro_off);
 
     for (int s0 = 0; s0 < B; s0 += NB) {
         const int nbc = min(NB, B - s0);
@@ -304,6 +342,10 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
             const int bpg = (nb + GPR - 1) / GPR;
             const int kb = min(part * bpg, nb), ke = min(kb + bpg, nb);
             const bool grp_on = rl < TR;             // long rows: fewer tile rows than groups
+            const unsigned gmask = 0xffu << (lane & 24);
+            // this row's term buffer: [R][nb][NB] float2, one per tile row of this warp
+            float2 *terms = reinterpret_cast<float2 *>(smem + plan.term_off + (size_t)warp * plan.term_warp) +
+                            (size_t)(q / GPR) * R * nb * NB;
             for (int i = 0; i < my_tiles; i++) {
                 const int tile = cta + i * nctas, st = i % S;
                 if (!mbar_wait(&full[st], (i / S) & 1)) {
@@ -314,40 +356,24 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                 const uint8_t *stage = ring + (size_t)st * plan.stage_bytes;
                 const int row = tile * TR + rl;
                 const bool valid = grp_on && row < J.rows;
-                float acc[R][NB];
-#pragma unroll
-                for (int r = 0; r < R; r++)
-#pragma unroll
-                    for (int s = 0; s < NB; s++) acc[r][s] = 0.0f;
                 if (valid) {
 #pragma unroll
                     for (int r = 0; r < R; r++) {
                         const uint8_t *rowp = stage + (size_t)(r * TR + rl) * rb;
-                        for (int k = kb; k < ke; k++) tm_block<TYPE, NB>(rowp, nb, n, k, A, nbc, acc[r], c);
+                        for (int k = kb; k < ke; k++)
+                            tm_block<TYPE, NB>(rowp, nb, n, k, A, nbc, terms + ((size_t)r * nb + k) * NB, c, gmask);
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the slot
-#pragma unroll
-                for (int r = 0; r < R; r++)
-#pragma unroll
-                    for (int s = 0; s < NB; s++) {
-                        float v = acc[r][s];
-                        v += __shfl_xor_sync(0xffffffffu, v, 4);
-                        v += __shfl_xor_sync(0xffffffffu, v, 2);
-                        v += __shfl_xor_sync(0xffffffffu, v, 1);
-                        if (GPR >= 2) v += __shfl_xor_sync(0xffffffffu, v, 8);
-                        if (GPR >= 4) v += __shfl_xor_sync(0xffffffffu, v, 16);
-                        acc[r][s] = v;
-                    }
                 if (c == 0 && part == 0 && valid) {
 #pragma unroll
                     for (int s = 0; s < NB; s++) {
                         if (s >= nbc) break;
-                        float a = acc[0][s];
+                        float a = tm_fold<NB>(terms, nb, s, J.ord, row);
                         float *out = J.out ? J.out + (size_t)(s0 + s) * J.out_stride : nullptr;
                         if (J.epi == EPI_GELU_MUL) {
-                            out[row] = gelu_f32(a) * acc[R - 1][s];
+                            out[row] = gelu_f32(a) * tm_fold<NB>(terms + (size_t)nb * NB, nb, s, J.ord2, row);
                         } else if (J.epi == EPI_SOFTCAP_ARGMAX) {
                             if (J.cap > 0.0f) a = J.cap * tanhf(a * (1.0f / J.cap));
                             if (out) out[row] = a;
@@ -360,6 +386,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                         }
                     }
                 }
+                __syncwarp();  // the fold has read the terms before the next tile rewrites them
             }
             if (J.epi == EPI_SOFTCAP_ARGMAX) {
 #pragma unroll
@@ -389,11 +416,20 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
 static int g_tm_sms = 0;
 static constexpr int kTmSmemBudget = 220 * 1024;
 
+// Activation staging bytes of nbs sequences (Q4/Q5: Q8_K planes; Q6: fixed-point pieces), then the
+// fp32 prologue scratch when the launch runs the fused prologue.
 template <int TYPE>
-static size_t tm_act_bytes(int nbs, int n) {
+static size_t tm_stage_bytes(int nbs, int n) {
     const int nb = n / G4_QK;
-    if (TYPE == G4_Q6_K) return (size_t)nbs * n * 4;
-    return (((size_t)nbs * n + (size_t)nbs * nb * 36 + 15) & ~(size_t)15) + (size_t)nbs * n * 4;  // + prologue scratch
+    if (TYPE == G4_Q6_K) return (((size_t)nbs * 3 * n + 15) & ~(size_t)15) + (size_t)nbs * nb * 4;
+    return (size_t)nbs * n + (size_t)nbs * nb * 36;
+}
+template <int TYPE>
+static size_t tm_act_bytes(int nbs, int n, bool pro, int gpr, int R) {
+    const size_t a = (tm_stage_bytes<TYPE>(nbs, n) + 15) & ~(size_t)15;
+    const size_t p = pro ? (size_t)nbs * n * 4 : 0;
+    const size_t t = (size_t)kTmConsumerWarps * (4 / gpr) * R * (n / G4_QK) * nbs * sizeof(float2);
+    return a + p + t;
 }
 
 template <int TYPE, int NB, int R>
@@ -419,9 +455,14 @@ static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st) {
     TmPlan plan{};
     plan.gpr = nb <= 6 ? 1 : nb <= 12 ? 2 : 4;
     plan.row_bytes = (int)device_row_bytes(TYPE, n);
+    const bool pro = jobs.has_pro != 0;
     int nbs = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
-    while (nbs > 1 && tm_act_bytes<TYPE>(nbs, n) > (size_t)kTmSmemBudget / 3) nbs /= 2;
-    plan.act_bytes = (int)((tm_act_bytes<TYPE>(nbs, n) + 127) & ~(size_t)127);
+    while (nbs > 1 && tm_act_bytes<TYPE>(nbs, n, pro, plan.gpr, R) > (size_t)kTmSmemBudget / 3) nbs /= 2;
+    const size_t stage_a = (tm_stage_bytes<TYPE>(nbs, n) + 15) & ~(size_t)15;
+    plan.pro_off = (int)stage_a;
+    plan.term_off = (int)(stage_a + (pro ? (size_t)nbs * n * 4 : 0));
+    plan.term_warp = (int)((size_t)(4 / plan.gpr) * R * nb * nbs * sizeof(float2));
+    plan.act_bytes = (int)((tm_act_bytes<TYPE>(nbs, n, pro, plan.gpr, R) + 127) & ~(size_t)127);
     // rows per tile: one row per GPR groups, at most what lets >= 3 stages fit
     int tr = kTmGroups / plan.gpr;
     const int fit = (kTmSmemBudget - plan.act_bytes) / (3 * R * plan.row_bytes);
@@ -482,6 +523,16 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
         if (((uintptr_t)J.w & 15) || ((uintptr_t)J.w2 & 15)) {  // bulk copies need 16-byte aligned sources
             set_error(G4_ERR_ARG, "gemv: weight pointer not 16-byte aligned");
             return G4_ERR_ARG;
+        }
+        if (!J.explicit_order) {  // w alone in its own tensor-core launch
+            if (type == G4_Q4_K) J.ord = q4_row_order(J.rows, 0, J.n, g_tm_sms, 0);
+            else if (type == G4_Q5_K) J.ord = q5_row_order(J.rows, J.n, g_tm_sms);
+            else J.ord = q6_row_order(J.rows, J.n, g_tm_sms, J.epi == EPI_SOFTCAP_ARGMAX);
+            J.ord2 = J.ord;
+            if (J.w2 && type == G4_Q4_K) {  // a gate/up pair shares one launch
+                J.ord = q4_row_order(J.rows, J.rows, J.n, g_tm_sms, 0);
+                J.ord2 = q4_row_order(J.rows, J.rows, J.n, g_tm_sms, 1);
+            }
         }
         // persistent CTAs (1 per SM) shared out in proportion to the job's bytes
         const int nbj = J.n / G4_QK;

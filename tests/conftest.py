@@ -50,6 +50,17 @@ def ref():
 
 
 @pytest.fixture(scope="session")
+def ref_generic():
+    """The reference built with -DGEMMA4_USE_GENERIC_DOT (its scalar dot kernels): the spread
+    between the two reference builds is the reference's own float noise."""
+    import oracle
+    path = oracle.REF_SO.replace("libg4ref.so", "libg4ref_generic.so")
+    if not os.path.exists(path):
+        pytest.skip("generic reference build absent")
+    return oracle.Reference(path=path)
+
+
+@pytest.fixture(scope="session")
 def golden():
     path = os.path.join(ROOT, "tests", "golden", "golden.npz")
     return dict(np.load(path, allow_pickle=False))

@@ -27,7 +27,6 @@ global layers and the shared-KV layers 24-41.
   logit difference between the two reference builds.
 """
 import dataclasses
-import os
 
 import numpy as np
 import pytest
@@ -62,15 +61,6 @@ def _top2(a):
     return i, float(a[i] - b.max())
 
 
-@pytest.fixture(scope="module")
-def generic_ref():
-    import oracle
-    path = oracle.REF_SO.replace("libg4ref.so", "libg4ref_generic.so")
-    if not os.path.exists(path):
-        pytest.skip("generic reference build absent")
-    return oracle.Reference(path=path)
-
-
 def test_e4b_fp32_path_matches_reference(g4, gpu, ref):
     S = g4.synth
     shape = dataclasses.replace(S.E4B, wq_t=S.Q6_K, wk_t=S.Q6_K, wv_t=S.Q6_K, wo_t=S.Q6_K, gate_t=S.Q6_K,
@@ -102,14 +92,14 @@ def test_e4b_fp32_path_matches_reference(g4, gpu, ref):
         rm.close()
 
 
-def test_e4b_q4km_within_reference_spread(g4, gpu, ref, generic_ref):
+def test_e4b_q4km_within_reference_spread(g4, gpu, ref, ref_generic):
     S = g4.synth
     shape = S.E4B
     m = S.make_model(shape, seed=3)
     max_seq = CTX + 8
     eng = g4.Engine(m, 0, max_seq=max_seq)
     ra = ref.model(m.desc(), max_seq)
-    rg = generic_ref.model(m.desc(), max_seq)
+    rg = ref_generic.model(m.desc(), max_seq)
     try:
         _fill(shape, S, CTX, 5, eng, [ra, rg])
         toks = np.random.default_rng(9).integers(0, shape.vocab_size, 6)

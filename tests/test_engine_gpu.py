@@ -4,9 +4,9 @@
 * TINY_F (fp32-path projections, no Q8_K activation rounding): logits, hidden
   state and KV rows at pos >= 1 within 5e-5 of the reference, and the greedy
   stream token-identical to the reference's.
-* TINY (the Q4_K_M mix): logits within the reference's own AVX2-vs-generic
-  spread (Q8_K re-rounding of activations turns last-ulp differences into
-  ~1e-2 logit differences, in the reference too).
+* TINY (the Q4_K_M mix) and TINY_Q5: teacher-forced logits within twice the
+  reference's own spread (its AVX2 build, generic build and C restatement
+  disagree by ~10% once a last-ulp difference flips a Q8_K rounding).
 * batched decode: each sequence of a batch is bit-identical to decoding it alone.
 """
 import dataclasses
@@ -14,7 +14,7 @@ import dataclasses
 import numpy as np
 import pytest
 
-from _tol import assert_close
+from _tol import assert_close, normwise
 
 pytestmark = pytest.mark.gpu
 
@@ -85,23 +85,45 @@ def test_tinyf_against_live_reference_long_window(g4, gpu, ref):
     rm.close()
 
 
-def test_tiny_q4km_logits(g4, gpu, tiny, golden):
-    eng = g4.Engine(tiny, 0, max_seq=64)
-    _, lg = run_prefix(eng, golden["tiny_prompt"], 7)
-    assert_close(lg, golden["tiny_logits_p7"], rel=0.1, what="Q4_K_M-mix logits pos 7")
-    eng.close()
-
-
-def test_tiny_q5_mixed_types(g4, gpu, orc):
-    m = g4.synth.make_model(g4.synth.TINY_Q5, seed=8)
+@pytest.mark.parametrize("which,seed", [("TINY", 3), ("TINY_Q5", 8)])
+def test_q8_mix_within_reference_spread(g4, gpu, ref, ref_generic, orc, which, seed):
+    """Models whose Q4_K/Q5_K GEMVs re-round activations to int8 (the Q4_K_M
+    mix; Q5_K in mixed types).  Once a last-ulp difference flips one Q8_K
+    rounding, faithful implementations part by ~10% in the logits: the
+    reference's AVX2 build, its generic build and its C restatement
+    (oracle/g4_oracle.c) do so among themselves.  Teacher-forced over 16
+    positions, the engine's distance from the AVX2 build is held to twice the
+    largest distance among those three (mean over the run, and per step with
+    a 1e-4 floor for steps before any flip), and its greedy token must equal
+    the AVX2 build's wherever the AVX2 top-1/top-2 margin exceeds twice the
+    largest logit difference among them."""
+    m = g4.synth.make_model(getattr(g4.synth, which), seed=seed)
     eng = g4.Engine(m, 0, max_seq=32)
-    om = orc.model(m.desc(), 32)
-    toks = np.random.default_rng(8).integers(0, 4096, 6)
-    for pos, t in enumerate(toks):
-        _, lg = eng.forward(int(t), pos, 1, want_logits=True)
-        om.forward(int(t), pos, 1)
-        assert_close(lg, om.logits(), rel=0.1, what="TINY_Q5 pos %d" % pos)
-    eng.close()
+    ra, rg, ro = ref.model(m.desc(), 32), ref_generic.model(m.desc(), 32), orc.model(m.desc(), 32)
+    toks = np.random.default_rng(8).integers(0, m.shape.vocab_size, 16)
+    errs, spreads = [], []
+    try:
+        for pos, t in enumerate(toks):
+            am, lg = eng.forward(int(t), pos, 1, want_logits=True)
+            ra.forward(int(t), pos, 1)
+            rg.forward(int(t), pos, 1)
+            ro.forward(int(t), pos, 1)
+            la, lb, lo = ra.logits(), rg.logits(), ro.logits()
+            sp = max(normwise(lb, la), normwise(lo, la))
+            err = normwise(lg, la)
+            errs.append(err)
+            spreads.append(sp)
+            assert err <= 2.0 * max(spreads) + 1e-4, "%s pos %d: engine %.3g, reference spread so far %.3g" % (
+                which, pos, err, max(spreads))
+            i = int(np.argmax(la))
+            srt = np.sort(la)
+            if srt[-1] - srt[-2] > 2.0 * max(float(np.abs(lb - la).max()), float(np.abs(lo - la).max())):
+                assert am == i, (which, pos, am, i)
+        assert np.mean(errs) <= 2.0 * np.mean(spreads) + 1e-4, (which, np.mean(errs), np.mean(spreads))
+    finally:
+        eng.close()
+        for mm in (ra, rg, ro):
+            mm.close()
 
 
 def test_head_dim_512_global_layers(g4, gpu, ref):
