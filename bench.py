@@ -567,6 +567,7 @@ def main():
                          "(default: fill for batch64, run for batch1)")
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--gemv-rows", type=int, default=10240, help="gemv0 workload: matrix rows")
+    ap.add_argument("--tc-min", type=int, default=None, help="engine tensor-core batch threshold")
     a = ap.parse_args()
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -637,6 +638,8 @@ def main():
     wbytes = model.weight_bytes()
     max_seq = prompt + a.warmup + a.steps * 2 + 8
     eng = g4.Engine(model, dist.local, max_seq=max_seq, max_batch=B)
+    if a.tc_min:
+        eng.set_tc_min_batch(a.tc_min)
     model_keep = model  # host tensors stay alive until the end
     stream = eng.stream()
     # prompts: seeded per global sequence id

@@ -86,6 +86,7 @@ SIGNATURES = [
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
     ("g4_engine_time_attention", ip, [vp, vp, ip, ip, ip, vp]),
     ("g4_set_tc_min_batch", ip, [ip]),
+    ("g4_engine_set_tc_min_batch", ip, [vp, ip]),
 ]
 
 _lib = None
@@ -302,6 +303,12 @@ class Engine:
         ms = np.zeros(1, np.float32)
         _check(lib().g4_engine_time_attention(self.h, _p(ls), len(ls), batch, reps, _p(ms)))
         return float(ms[0])
+
+    def set_tc_min_batch(self, b: int) -> int:
+        r = lib().g4_engine_set_tc_min_batch(self.h, b)
+        if r < 0:
+            _check(G4_ERR_ARG)
+        return r
 
     def last_step_kernels(self) -> int:
         return int(lib().g4_engine_last_step_kernels(self.h))

@@ -614,7 +614,9 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
 }
 
 int enqueue_step(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
-    if (B <= kFusedMaxBatch && e->dim % G4_QK == 0) return enqueue_step_fused(e, B, lm_mode, from_keys, want_logits);
+    // below the tensor-core threshold every residual/norm/quantize step runs inside the GEMV that consumes it
+    if (B <= kFusedMaxBatch && (B < e->tc_min_batch || !e->tcq) && e->dim % G4_QK == 0)
+        return enqueue_step_fused(e, B, lm_mode, from_keys, want_logits);
     e->hidden_src = lm_mode ? e->xf : e->x;
     return enqueue_step_unfused(e, B, lm_mode, from_keys, want_logits);
 }
@@ -822,7 +824,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
     G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
-    if (max_batch > kFusedMaxBatch) {  // tensor-core path of the batched step
+    if (max_batch > 1) {  // tensor-core path of the batched step
         int nmax = std::max(std::max(dim, e->hidden), std::max(e->qd_max, pd));
         size_t part = 0;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
@@ -882,6 +884,22 @@ size_t g4_engine_device_bytes(const g4_engine *e) { return e ? e->dev_bytes : 0;
 size_t g4_model_desc_bytes(void) { return sizeof(g4_model_desc); }
 
 int g4_engine_last_step_kernels(const g4_engine *e) { return e ? e->last_step_kernels : -1; }
+
+int g4_engine_set_tc_min_batch(g4_engine *e, int min_batch) {
+    if (!e || min_batch < 1) { set_error(G4_ERR_ARG, "set_tc_min_batch: bad arguments"); return -1; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    const int prev = e->tc_min_batch;
+    if (min_batch != prev) {  // captured steps were built for the old threshold
+        cudaSetDevice(e->device);
+        cudaStreamSynchronize(e->st);
+        for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+        e->graphs.clear();
+        e->graph_kernels.clear();
+        e->graph_hidden.clear();
+    }
+    e->tc_min_batch = min_batch;
+    return prev;
+}
 
 void *g4_engine_stream(g4_engine *e) { return e ? (void *)e->st : nullptr; }
 

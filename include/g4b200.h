@@ -277,6 +277,13 @@ int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed);
  * is unchanged.  Not part of the reference interface. */
 int g4_engine_time_attention(g4_engine *e, const int *layers, int n, int batch, int reps, float *ms);
 
+/* Batch size from which the engine's step runs the K-quant projections and
+ * the LM head on the tensor cores (default 9; below it, streaming GEMVs with
+ * the residual/norm work fused in).  Results do not depend on it: both paths
+ * compute every row bit-identically.  Not part of the reference interface;
+ * returns the previous value, or -1 on a bad argument. */
+int g4_engine_set_tc_min_batch(g4_engine *e, int min_batch);
+
 /* Number of kernels in the most recent step (the nodes of its CUDA graph). */
 int g4_engine_last_step_kernels(const g4_engine *e);
 
