@@ -64,6 +64,7 @@ SIGNATURES = [
     ("g4_apply_rope_neox_ex", ip, [vp, ip, ip, ip, ip, fp, fp, vp]),
     ("g4_logits_tied", ip, [vp, vp, vp, vp, ip, ip, ip, fp]),
     ("g4_attn_decode", ip, [vp, vp, vp, vp, ip, ip, ip, ip, ip]),
+    ("g4_sample_token", ip, [vp, ip, fp, fp, ip, vp]),
     ("g4d_weight_upload", ip, [vp, ip, ip, ip, vp]),
     ("g4d_free", ip, [vp]),
     ("g4d_quantize_row_q8_K", ip, [vp, vp, ip, ip, vp]),
@@ -76,6 +77,8 @@ SIGNATURES = [
     ("g4_forward", ip, [vp, ip, ip, ip, vp]),
     ("g4_generate_greedy", ip, [vp, vp, ip, ip, ip, vp]),
     ("g4_decode_batch", ip, [vp, ip, vp, ip, ip, vp]),
+    ("g4_generate", ip, [vp, vp, ip, ip, fp, fp, ip, fp, ip, C.c_uint64, ip, vp]),
+    ("g4_decode_batch_sample", ip, [vp, ip, vp, ip, fp, fp, ip, fp, vp, ip, vp, vp, vp]),
     ("g4_decode_batch_device", ip, [vp, ip, vp, ip, ip, vp]),
     ("g4_engine_sync", ip, [vp]),
     ("g4_engine_stream", vp, [vp]),
@@ -199,6 +202,16 @@ def attn_decode(q, k, v, nwin, kv_stride, n_heads, n_kv, hd):
     return out
 
 
+def sample_token(logits, temp: float, topp: float, topk: int, rng_state: int):
+    """sample_token (main.c:2044-2112) on host logits; returns (token, new rng state)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    st = C.c_uint64(rng_state)
+    r = lib().g4_sample_token(_p(lg), lg.size, temp, topp, topk, C.byref(st))
+    if r < 0:
+        _check(lib().g4_last_error() or G4_ERR_ARG)
+    return r, st.value
+
+
 def weight_upload(host: np.ndarray, t: int, n: int, rows: int) -> int:
     """Device copy of a weight tensor (device layout); returns the pointer."""
     d = C.c_void_p()
@@ -260,6 +273,29 @@ class Engine:
         if n < 0:
             _check(lib().g4_last_error() or G4_ERR_CUDA)
         return out[:n]
+
+    def generate(self, prompt, max_new: int, temp: float, topp: float = 0.9, topk: int = 40,
+                 repeat_penalty: float = 1.0, penalty_last_n: int = 64, seed: int = 1, eos: int = -1) -> np.ndarray:
+        """generate with the reference's sampler (temp > 0: top-k / top-p / repetition penalty)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = lib().g4_generate(self.h, _p(p), p.size, max_new, temp, topp, topk, repeat_penalty, penalty_last_n, seed,
+                              eos, _p(out))
+        if n < 0:
+            _check(lib().g4_last_error() or G4_ERR_CUDA)
+        return out[:n]
+
+    def decode_batch_sample(self, tokens, pos: int, temp: float, topp: float, topk: int, rng,
+                            repeat_penalty: float = 1.0, recent=None, n_recent=None):
+        """One batched step with the sampler; rng is a uint64 array of per-sequence states (advanced in place)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = np.zeros(t.size, np.int32)
+        assert rng.dtype == np.uint64 and rng.size == t.size
+        rec = None if recent is None else np.ascontiguousarray(recent, dtype=np.int32)
+        nr = None if n_recent is None else np.ascontiguousarray(n_recent, dtype=np.int32)
+        _check(lib().g4_decode_batch_sample(self.h, t.size, _p(t), pos, temp, topp, topk, repeat_penalty, _p(rec),
+                                            0 if rec is None else rec.shape[1], _p(nr), _p(rng), _p(nxt)))
+        return nxt
 
     def decode_batch(self, tokens, pos: int, lm_mode: int = 1) -> np.ndarray:
         t = np.ascontiguousarray(tokens, dtype=np.int32)

@@ -654,6 +654,32 @@ static int mm_tcbf(float *o, const float *x, const void *w, int n, int d, int ba
 
 extern "C" {
 
+// sample_token (main.c:2044-2112) on host logits: the top-k candidates are selected on the GPU,
+// the temperature / top-p tail runs on the host with the reference's expressions.
+int g4_sample_token(const float *logits, int n, float temp, float topp, int topk, uint64_t *rng) {
+    if (!logits || n <= 0 || !rng) { set_error(G4_ERR_ARG, "sample_token: bad arguments"); return -1; }
+    const int k = temp <= 0.0f ? 1 : (topk <= 0 || topk > n ? n : topk);
+    if (k > 64) { set_error(G4_ERR_ARG, "sample_token: top-k %d above 64 is not supported", k); return -1; }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ctx_ready()) return -1;
+    Carve cv;
+    const size_t o_l = cv.take((size_t)n * 4), o_v = cv.take(64 * 4), o_i = cv.take(64 * 4);
+    if (scratch_reserve(cv.off)) return -1;
+    float *dl = (float *)(g_ctx.scratch + o_l), *dv = (float *)(g_ctx.scratch + o_v);
+    int *di = (int *)(g_ctx.scratch + o_i);
+    float hv[64], p[64];
+    int hi[64];
+    cudaError_t ce = cudaMemcpyAsync(dl, logits, (size_t)n * 4, cudaMemcpyHostToDevice, g_ctx.st);
+    if (ce != cudaSuccess) { cuda_fail(ce, "sample_token upload", __FILE__, __LINE__); return -1; }
+    if (launch_topk(dl, n, n, k, dv, di, 1, g_ctx.st) != G4_OK) return -1;
+    ce = cudaMemcpyAsync(hv, dv, (size_t)k * 4, cudaMemcpyDeviceToHost, g_ctx.st);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(hi, di, (size_t)k * 4, cudaMemcpyDeviceToHost, g_ctx.st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(g_ctx.st);
+    if (ce != cudaSuccess) { cuda_fail(ce, "sample_token", __FILE__, __LINE__); return -1; }
+    if (temp <= 0.0f) return hi[0];  // first index of the largest logit (main.c:2045-2050)
+    return sample_tail_host(hv, hi, k, temp, topp, rng, p);
+}
+
 int g4_set_tc_min_batch(int b) {
     if (b < 1) { set_error(G4_ERR_ARG, "tc min batch %d", b); return -1; }
     return g_tc_min_batch.exchange(b);

@@ -72,6 +72,9 @@ struct g4_engine {
     int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr, *attn_ctr = nullptr;
     int *h_pos = nullptr, *h_tok = nullptr, *h_err = nullptr;
     int *d_err = nullptr;  // bounded-wait status word written by the kernels
+    // sampler: top-k candidates per sequence (device and pinned host), recent tokens for the penalty
+    float *cand_v = nullptr, *h_cand_v = nullptr;
+    int *cand_i = nullptr, *h_cand_i = nullptr, *d_recent = nullptr, *d_nrec = nullptr;
     std::vector<void *> allocs;
     size_t dev_bytes = 0;
     std::map<long, cudaGraphExec_t> graphs;
@@ -154,6 +157,8 @@ void destroy(g4_engine *e) {
     if (e->h_pos) cudaFreeHost(e->h_pos);
     if (e->h_tok) cudaFreeHost(e->h_tok);
     if (e->h_err) cudaFreeHost(e->h_err);
+    if (e->h_cand_v) cudaFreeHost(e->h_cand_v);
+    if (e->h_cand_i) cudaFreeHost(e->h_cand_i);
     if (e->st) cudaStreamDestroy(e->st);
     delete e;
 }
@@ -694,6 +699,38 @@ int stage_tokens(g4_engine *e, const int *tokens, int B, int pos) {
     return G4_OK;
 }
 
+// After a step that wrote the softcapped logits of B sequences: the repetition penalty over each
+// sequence's recent tokens (recent[b][0..n_recent[b]) in order, host arrays; penalty <= 1: none),
+// the top-k candidates on the device, then the sampling tail per sequence on the host
+// (main.c:2044-2126).  k = 1 for temp <= 0 (the first largest logit).
+int sample_after_step(g4_engine *e, int B, float temp, float topp, int topk, float penalty, const int *recent,
+                      int recent_ld, const int *n_recent, uint64_t *rng, int *next) {
+    const int k = temp <= 0.0f ? 1 : (topk <= 0 || topk > e->vocab ? e->vocab : topk);
+    if (k > 64) { set_error(G4_ERR_ARG, "sampling: top-k %d above 64 is not supported", k); return G4_ERR_ARG; }
+    if (penalty > 1.0f && recent && n_recent) {
+        for (int b = 0; b < B; b++)
+            if (n_recent[b] < 0 || n_recent[b] > e->max_seq || n_recent[b] > recent_ld) {
+                set_error(G4_ERR_ARG, "sampling: %d recent tokens for sequence %d", n_recent[b], b);
+                return G4_ERR_ARG;
+            }
+        G4_CUDA(cudaMemcpy2DAsync(e->d_recent, sizeof(int) * e->max_seq, recent, sizeof(int) * recent_ld,
+                                  sizeof(int) * std::min(recent_ld, e->max_seq), B, cudaMemcpyHostToDevice, e->st));
+        G4_CUDA(cudaMemcpyAsync(e->d_nrec, n_recent, sizeof(int) * B, cudaMemcpyHostToDevice, e->st));
+        TRY(launch_rep_penalty(e->logits, e->vocab, e->d_recent, e->max_seq, e->d_nrec, e->vocab, penalty, B, e->st));
+    }
+    TRY(launch_topk(e->logits, e->vocab, e->vocab, k, e->cand_v, e->cand_i, B, e->st));
+    G4_CUDA(cudaMemcpyAsync(e->h_cand_v, e->cand_v, sizeof(float) * B * k, cudaMemcpyDeviceToHost, e->st));
+    G4_CUDA(cudaMemcpyAsync(e->h_cand_i, e->cand_i, sizeof(int) * B * k, cudaMemcpyDeviceToHost, e->st));
+    TRY(enqueue_err_check(e));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    TRY(err_after_sync(e));
+    float p[64];
+    for (int b = 0; b < B; b++)
+        next[b] = temp <= 0.0f ? e->h_cand_i[b * k]
+                               : sample_tail_host(e->h_cand_v + b * k, e->h_cand_i + b * k, k, temp, topp, rng + b, p);
+    return G4_OK;
+}
+
 int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     if (!m || max_seq <= 0 || max_batch <= 0) { set_error(G4_ERR_ARG, "engine: bad arguments"); return G4_ERR_ARG; }
     if (m->dim <= 0 || m->dim % G4_QK || m->hidden_dim <= 0 || m->n_layers <= 0 || m->n_heads <= 0 ||
@@ -849,6 +886,10 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     *e->h_err = 0;
     TRY(dalloc_t(e, &e->d_tokens, B)); TRY(dalloc_t(e, &e->d_next, B)); TRY(dalloc_t(e, &e->d_pos, 1));
     TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * B));
+    TRY(dalloc_t(e, &e->cand_v, B * 64)); TRY(dalloc_t(e, &e->cand_i, B * 64));
+    TRY(dalloc_t(e, &e->d_recent, B * (size_t)max_seq)); TRY(dalloc_t(e, &e->d_nrec, B));
+    G4_CUDA(cudaMallocHost((void **)&e->h_cand_v, sizeof(float) * B * 64));
+    G4_CUDA(cudaMallocHost((void **)&e->h_cand_i, sizeof(int) * B * 64));
     G4_CUDA(cudaMallocHost((void **)&e->h_pos, sizeof(int) * (size_t)max_seq));
     for (int i = 0; i < max_seq; i++) e->h_pos[i] = i;
     G4_CUDA(cudaMallocHost((void **)&e->h_tok, sizeof(int) * (size_t)max_seq * B));
@@ -1093,6 +1134,60 @@ int g4_engine_get_kv(g4_engine *e, int b, int layer, int pos, float *k, float *v
     }
     G4_CUDA(cudaStreamSynchronize(e->st));
     return G4_OK;
+}
+
+int g4_generate(g4_engine *e, const int *prompt, int n_prompt, int max_new, float temp, float topp, int topk,
+                float repeat_penalty, int penalty_last_n, uint64_t seed, int eos, int *out_tokens) {
+    if (!e || !prompt || n_prompt <= 0 || max_new < 0 || (max_new > 0 && !out_tokens)) {
+        set_error(G4_ERR_ARG, "generate: bad arguments");
+        return -1;
+    }
+    const bool plain_greedy = temp <= 0.0f && repeat_penalty <= 1.0f;
+    if (plain_greedy) return g4_generate_greedy(e, prompt, n_prompt, max_new, eos, out_tokens);
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (cudaSetDevice(e->device) != cudaSuccess) { set_error(G4_ERR_CUDA, "cudaSetDevice failed"); return -1; }
+    uint64_t rng = seed ? seed : 1;  // main.c:2341
+    int total = n_prompt + max_new - 1, token = prompt[0], gen = 0;
+    if (total > e->max_seq) total = e->max_seq;
+    for (int pos = 0; pos < total; pos++) {
+        const bool prefill = pos < n_prompt - 1;
+        if (set_pos(e, pos) || stage_tokens(e, &token, 1, pos)) return -1;
+        if (run_step(e, 1, prefill ? 0 : 1, false, !prefill)) return -1;
+        int next;
+        if (prefill) {
+            next = prompt[pos + 1];
+        } else {
+            // the penalty covers the generated tokens only, the last penalty_last_n of them (main.c:2117-2119)
+            const int start = (penalty_last_n > 0 && gen > penalty_last_n) ? gen - penalty_last_n : 0;
+            const int nrec = gen - start;
+            if (sample_after_step(e, 1, temp, topp, topk, repeat_penalty, out_tokens + start, nrec > 0 ? nrec : 1, &nrec,
+                                  &rng, &next))
+                return -1;
+            if (next == eos) break;
+            out_tokens[gen++] = next;
+        }
+        token = next;
+    }
+    if (!total || total <= n_prompt - 1) {  // prefill only: wait for it
+        if (enqueue_err_check(e) || cudaStreamSynchronize(e->st) != cudaSuccess || err_after_sync(e)) return -1;
+    }
+    return gen;
+}
+
+int g4_decode_batch_sample(g4_engine *e, int B, const int *tokens, int pos, float temp, float topp, int topk,
+                           float repeat_penalty, const int *recent, int recent_ld, const int *n_recent, uint64_t *rng,
+                           int *next) {
+    if (!e || !tokens || B <= 0 || !rng || !next || (repeat_penalty > 1.0f && (!recent || !n_recent || recent_ld <= 0))) {
+        set_error(G4_ERR_ARG, "decode_batch_sample: bad arguments");
+        return G4_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (B > e->max_batch) { set_error(G4_ERR_STATE, "batch %d > engine max_batch %d", B, e->max_batch); return G4_ERR_STATE; }
+    G4_CUDA(cudaSetDevice(e->device));
+    TRY(set_pos(e, pos));
+    TRY(stage_tokens(e, tokens, B, pos));
+    TRY(run_step(e, B, 1, false, true));
+    return sample_after_step(e, B, temp, topp, topk, repeat_penalty, recent, recent_ld, n_recent, rng, next);
 }
 
 }  // extern "C"

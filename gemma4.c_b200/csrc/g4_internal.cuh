@@ -148,6 +148,7 @@ __device__ __forceinline__ float gelu_f32(float x) {
 // (main.c:2045-2050).  NaN is not expected (softcapped logits are finite).
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     uint32_t b = __float_as_uint(v);
+    if ((b & 0x7fffffffu) == 0u) b = 0u;               // -0 and +0 compare equal, as floats do
     b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // order-preserving map
     return ((unsigned long long)b << 32) | (uint32_t)(0xffffffffu - (uint32_t)idx);
 }

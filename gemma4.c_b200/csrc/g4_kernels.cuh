@@ -143,6 +143,12 @@ int launch_ple_mix(const float *ple_tok, float *ple_ctx, const float *norm_w, in
 int launch_keys_to_tokens(const unsigned long long *keys, int *tokens, int B, cudaStream_t st);
 int launch_fill_kv(float *c, int B, int n_kv, int ring, int hd, int npos, uint64_t seed, cudaStream_t st);
 
+// ---- sampler (k_sample.cu)
+int launch_rep_penalty(float *logits, int ld, const int *recent, int rec_ld, const int *nrec, int vocab, float penalty,
+                       int B, cudaStream_t st);
+int launch_topk(const float *logits, int ld, int n, int k, float *out_v, int *out_i, int B, cudaStream_t st);
+int sample_tail_host(const float *vals, const int *idx, int k, float temp, float topp, uint64_t *rng, float *p);
+
 // ---- batched BF16-weight GEMM on tcgen05 (k_gemm_bf16tc.cu), 16..64 sequences
 size_t bf16tc_operand_bytes(int n);
 int bf16tc_weight_map(CUtensorMap *m, const void *w, int n, int rows);

@@ -137,6 +137,15 @@ int g4_apply_rope_neox_ex(float *vec, int n_heads, int head_dim, int n_rot, int 
 int g4_logits_tied(float *logits, int *argmax, const float *x, const void *embd, int embd_type,
                    int dim, int vocab, float softcap);
 
+/* sample_token (main.c:2044-2112) on host logits[n]: temp <= 0 returns the
+ * first index of the largest logit; otherwise the top-k candidates (value
+ * descending, index ascending, as the reference's insertion sort) are
+ * selected on the GPU and the temperature softmax, top-p and xorshift64*
+ * draws (*rng is advanced) run on the host with the reference's float
+ * expressions, so the token is the reference's.  topk <= 0 means n; k above
+ * 64 is rejected.  Returns the token id, or -1 on error. */
+int g4_sample_token(const float *logits, int n, float temp, float topp, int topk, uint64_t *rng);
+
 /* Decode attention for one query position over a caller-provided fp32 KV
  * window, laid out like the reference cache rows (main.c:1909-1950):
  *   q[n_heads * hd], k/v rows at k + t * kv_stride (+ kvh * hd), t in [0, nwin).
@@ -250,10 +259,31 @@ int g4_forward(g4_engine *e, int token, int pos, int lm_mode, float *logits);
 int g4_generate_greedy(g4_engine *e, const int *prompt, int n_prompt, int max_new, int eos,
                        int *out_tokens);
 
+/* generate (main.c:2335-2488) with the reference's sampler for one sequence:
+ * prefill prompt[0..n_prompt) one position at a time, then up to max_new
+ * tokens, each from sample_token(temp, topp, topk) after the repetition
+ * penalty over the last penalty_last_n generated tokens (penalty_last_n <= 0:
+ * all of them; repeat_penalty <= 1: none).  rng starts at seed (0 -> 1) as in
+ * main.c:2341.  The penalty and the top-k candidates run on the GPU; the
+ * temperature / top-p tail on the host with the reference's expressions.
+ * temp <= 0 is greedy.  Stops before emitting `eos` (eos < 0: never).
+ * Returns the number of tokens written to out_tokens, or -1. */
+int g4_generate(g4_engine *e, const int *prompt, int n_prompt, int max_new, float temp, float topp, int topk,
+                float repeat_penalty, int penalty_last_n, uint64_t seed, int eos, int *out_tokens);
+
 /* Batched greedy decode of B independent sequences in lockstep (all at the
  * same position).  tokens[B] in, next[B] out (argmax of each sequence's
  * softcapped logits).  lm_mode 0 skips the LM head (next untouched). */
 int g4_decode_batch(g4_engine *e, int B, const int *tokens, int pos, int lm_mode, int *next);
+
+/* One batched step with the sampler: tokens[B] in; for each sequence b the
+ * repetition penalty over recent[b * recent_ld .. + n_recent[b]) (host
+ * arrays; ignored when repeat_penalty <= 1), then sample_token(temp, topp,
+ * topk) with its own rng[b] (advanced); next[B] out.  The logits stay on the
+ * GPU; only the top-k candidates reach the host. */
+int g4_decode_batch_sample(g4_engine *e, int B, const int *tokens, int pos, float temp, float topp, int topk,
+                           float repeat_penalty, const int *recent, int recent_ld, const int *n_recent, uint64_t *rng,
+                           int *next);
 
 /* Device-pointer form used by bench loops: tokens/next are DEVICE int32[B]
  * buffers; enqueued on the engine stream, no synchronisation. */

@@ -180,6 +180,9 @@ class Reference(_Lib):
         self._mvc = self.fn("model_vc", fp, vp, C.c_int, C.c_int)
         self._gen = self.fn("generate_greedy", C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, vp)
         self._fillkv = self.fn("model_fill_kv", None, vp, C.c_int, C.c_uint64)
+        self._gens = self.fn("generate_sample", C.c_int, vp, vp, C.c_int, C.c_int, C.c_float, C.c_float, C.c_float,
+                             C.c_int, C.c_uint64, C.c_int, vp)
+        self._pen = self.fn("apply_repetition_penalty", None, vp, vp, C.c_int, C.c_float, C.c_int)
         try:
             with open(os.path.join(os.path.dirname(path), "BLAS")) as f:
                 self.blas = f.read().strip()
@@ -230,6 +233,19 @@ class Reference(_Lib):
     def gelu(self, x):
         return self._gelu(x)
 
+    def sample(self, logits, temp, topp, topk, rng_state):
+        """sample_token on a copy of the logits; returns (token, new rng state)."""
+        v = np.array(logits, dtype=np.float32, copy=True)
+        rng = C.c_uint64(rng_state)
+        t = self._sample(_p(v), v.size, temp, topp, topk, C.byref(rng))
+        return t, rng.value
+
+    def repetition_penalty(self, logits, tokens, penalty, last_n):
+        v = np.array(logits, dtype=np.float32, copy=True)
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        self._pen(_p(v), _p(t), t.size, penalty, last_n)
+        return v
+
     def sample_greedy(self, logits):
         v = np.ascontiguousarray(logits, np.float32)
         rng = C.c_uint64(1)
@@ -264,6 +280,12 @@ class _Model:
 
     def fill_kv(self, npos, seed=1):
         self.lib._fillkv(self.h, npos, seed)
+
+    def generate_sample(self, prompt, max_new, temp, topp=0.9, repeat_penalty=1.0, penalty_last_n=64, seed=1, eos=-1):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = self.lib._gens(self.h, _p(p), p.size, max_new, temp, topp, repeat_penalty, penalty_last_n, seed, eos, _p(out))
+        return out[:n]
 
     def generate_greedy(self, prompt, max_new, eos=-1):
         p = np.ascontiguousarray(prompt, dtype=np.int32)

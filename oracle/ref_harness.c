@@ -177,6 +177,42 @@ int ref_generate_greedy(void *mp, const int *prompt, int n_prompt, int max_new, 
     return gen;
 }
 
+/* apply_repetition_penalty (main.c:2114-2126). */
+void ref_apply_repetition_penalty(float *logits, const int *tokens, int n_tokens, float penalty, int last_n) {
+    apply_repetition_penalty(logits, tokens, n_tokens, penalty, last_n);
+}
+
+/* generate (main.c:2335-2488) with sampling, without the tokenizer output,
+ * thinking control or forced tokens: the same lm_mode choice (2372-2379), the
+ * repetition penalty over the generated tokens (2403-2405), sample_token with
+ * DEFAULT_TOP_K (2427-2429), the eos stop (2435). */
+int ref_generate_sample(void *mp, const int *prompt, int n_prompt, int max_new, float temp, float topp,
+                        float repeat_penalty, int penalty_last_n, uint64_t seed, int eos, int *out) {
+    Model *m = (Model *)mp;
+    uint64_t rng = seed ? seed : 1;
+    int token = prompt[0], gen = 0;
+    int greedy = temp <= 0.0f;
+    int fast_argmax = greedy && repeat_penalty <= 1.0f && m->cfg.logit_softcapping <= 0.0f;
+    for (int pos = 0; pos < n_prompt + max_new - 1; pos++) {
+        if (pos >= m->cfg.max_seq) break;
+        int lm_mode = pos < n_prompt - 1 ? 0 : (fast_argmax ? 2 : 1);
+        forward(m, token, pos, lm_mode);
+        int next;
+        if (pos < n_prompt - 1) {
+            next = prompt[pos + 1];
+        } else {
+            if (repeat_penalty > 1.0f) apply_repetition_penalty(m->s.logits, out, gen, repeat_penalty, penalty_last_n);
+            if (fast_argmax) next = m->s.argmax_tok;
+            else if (greedy) next = sample_token(m->s.logits, m->cfg.vocab_size, 0.0f, topp, DEFAULT_TOP_K, &rng);
+            else next = sample_token(m->s.logits, m->cfg.vocab_size, temp, topp, DEFAULT_TOP_K, &rng);
+            if (next == eos) break;
+            out[gen++] = next;
+        }
+        token = next;
+    }
+    return gen;
+}
+
 /* Fill the KV cache rows [0, npos) of every KV layer with seeded values in
  * [-1, 1) (xorshift64*).  Used only to time forward() at a long context
  * without running the prefill first: the work of a decode step does not
