@@ -72,6 +72,8 @@ SIGNATURES = [
     ("g4d_attn_decode_noalloc", ip, [vp, vp, vp, vp, ip, ip, ip, ip, vp]),
     ("g4_model_desc_bytes", C.c_size_t, []),
     ("g4_engine_create", vp, [vp, ip, ip, ip]),
+    ("g4_engine_create_ex", vp, [vp, ip, ip, ip, ip]),
+    ("g4_prefill", ip, [vp, ip, vp, vp, vp]),
     ("g4_engine_destroy", ip, [vp]),
     ("g4_engine_device_bytes", C.c_size_t, [vp]),
     ("g4_forward", ip, [vp, ip, ip, ip, vp]),
@@ -248,13 +250,15 @@ def kernel_launch_count() -> int:
 class Engine:
     """Device-resident decode engine for one model on one GPU."""
 
-    def __init__(self, model: "synth.SynthModel", device: int = 0, max_seq: int = 1024, max_batch: int = 1):
+    def __init__(self, model: "synth.SynthModel", device: int = 0, max_seq: int = 1024, max_batch: int = 1,
+                 prefill_rows: int = 0):
         self.model = model          # keeps the host tensors alive while uploading
         self.desc = model.desc()
         self.vocab = self.desc.vocab_size
         self.dim = self.desc.dim
         self.max_batch = max_batch
-        h = lib().g4_engine_create(C.byref(self.desc), device, max_seq, max_batch)
+        self.prefill_rows = prefill_rows
+        h = lib().g4_engine_create_ex(C.byref(self.desc), device, max_seq, max_batch, prefill_rows)
         if not h:
             _check(lib().g4_last_error() or G4_ERR_CUDA)
         self.h = h
@@ -296,6 +300,26 @@ class Engine:
         _check(lib().g4_decode_batch_sample(self.h, t.size, _p(t), pos, temp, topp, topk, repeat_penalty, _p(rec),
                                             0 if rec is None else rec.shape[1], _p(nr), _p(rng), _p(nxt)))
         return nxt
+
+    def prefill(self, seq, pos, tokens):
+        """Batched prefill rows (sequence, position, token); see g4_prefill."""
+        sq = np.ascontiguousarray(seq, dtype=np.int32)
+        ps = np.ascontiguousarray(pos, dtype=np.int32)
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        assert sq.size == ps.size == tk.size
+        _check(lib().g4_prefill(self.h, sq.size, _p(sq), _p(ps), _p(tk)))
+
+    def prefill_prompts(self, prompts, upto: int):
+        """Prefill positions [0, upto) of every sequence's prompt (prompts: [B][>= upto]) in calls of at
+        most prefill_rows rows, interleaving the sequences position-major."""
+        prompts = np.asarray(prompts, dtype=np.int32)
+        B = prompts.shape[0]
+        per = max(1, self.prefill_rows // B)  # positions per call
+        for p0 in range(0, upto, per):
+            p1 = min(upto, p0 + per)
+            ps = np.repeat(np.arange(p0, p1, dtype=np.int32), B)
+            sq = np.tile(np.arange(B, dtype=np.int32), p1 - p0)
+            self.prefill(sq, ps, prompts[sq, ps])
 
     def decode_batch(self, tokens, pos: int, lm_mode: int = 1) -> np.ndarray:
         t = np.ascontiguousarray(tokens, dtype=np.int32)

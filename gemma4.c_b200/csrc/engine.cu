@@ -72,6 +72,9 @@ struct g4_engine {
     int *d_tokens = nullptr, *d_next = nullptr, *d_pos = nullptr, *d_hist = nullptr, *attn_ctr = nullptr;
     int *h_pos = nullptr, *h_tok = nullptr, *h_err = nullptr;
     int *d_err = nullptr;  // bounded-wait status word written by the kernels
+    // prefill: rows per g4_prefill call, the (sequence, position) of each row (device, pinned host)
+    int prefill_cap = 0;
+    int *d_rowpos = nullptr, *d_rowseq = nullptr, *h_rows = nullptr;
     // sampler: top-k candidates per sequence (device and pinned host), recent tokens for the penalty
     float *cand_v = nullptr, *h_cand_v = nullptr;
     int *cand_i = nullptr, *h_cand_i = nullptr, *d_recent = nullptr, *d_nrec = nullptr;
@@ -158,6 +161,7 @@ void destroy(g4_engine *e) {
     if (e->h_tok) cudaFreeHost(e->h_tok);
     if (e->h_err) cudaFreeHost(e->h_err);
     if (e->h_cand_v) cudaFreeHost(e->h_cand_v);
+    if (e->h_rows) cudaFreeHost(e->h_rows);
     if (e->h_cand_i) cudaFreeHost(e->h_cand_i);
     if (e->st) cudaStreamDestroy(e->st);
     delete e;
@@ -321,7 +325,11 @@ bool attach_operand(g4_engine *e, ResNorm &r, int B, int type, int n) {
     return true;
 }
 
-int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits) {
+// One step for B rows.  Decode: row b is sequence b at the engine position.  Prefill (prefill =
+// true, lm_mode 0): row b is sequence d_rowseq[b] at position d_rowpos[b]; every layer that owns a
+// cache stores the K/V rows of all rows first, then each row attends with exactly the decode
+// step's arithmetic, so a prefilled sequence is bit-identical to one decoded position by position.
+int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool want_logits, bool prefill = false) {
     const int dim = e->dim, L = e->L, pd = e->pd;
     TRY(launch_embed_v(e->embd, e->embd_t, dim, (size_t)e->vocab, e->emb_scale, e->ple_tok, e->ple_tok_t, pd * L,
                        e->ple_scale, from_keys ? nullptr : e->d_tokens, e->keys, e->x, e->ple_tokb, B, e->st));
@@ -394,7 +402,15 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                 TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
 
         // attention (main.c:1886-1950)
-        TRY(launch_attention(attn_args(e, l), B, e->d_pos, e->max_seq, e->st));
+        if (prefill) {
+            AttnLayer A = attn_args(e, l);
+            A.row_pos = e->d_rowpos; A.row_seq = e->d_rowseq; A.early = 0;
+            if (A.append) TRY(launch_kv_append(A, B, e->st));
+            A.append = 0;
+            TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
+        } else {
+            TRY(launch_attention(attn_args(e, l), B, e->d_pos, e->max_seq, e->st));
+        }
 
         // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
         if (use_tc(e, B, ly.wo_t, EPI_STORE))
@@ -731,8 +747,9 @@ int sample_after_step(g4_engine *e, int B, float temp, float topp, int topk, flo
     return G4_OK;
 }
 
-int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
-    if (!m || max_seq <= 0 || max_batch <= 0) { set_error(G4_ERR_ARG, "engine: bad arguments"); return G4_ERR_ARG; }
+int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch, int prefill_rows) {
+    if (!m || max_seq <= 0 || max_batch <= 0 || prefill_rows < 0) { set_error(G4_ERR_ARG, "engine: bad arguments"); return G4_ERR_ARG; }
+    e->prefill_cap = prefill_rows;
     if (m->dim <= 0 || m->dim % G4_QK || m->hidden_dim <= 0 || m->n_layers <= 0 || m->n_heads <= 0 ||
         m->n_kv_heads <= 0 || m->n_heads % m->n_kv_heads || m->vocab_size <= 0 || m->ple_dim <= 0 || m->ple_dim > 1024 ||
         m->dim > 12288) {
@@ -814,7 +831,9 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         LayerDev &ly = e->layers[l];
         if (l < G4_N_LAYER_KV) {
             ly.src = l;
-            ly.ring = (ly.swa && e->window > 0 && e->window < max_seq) ? e->window : max_seq;
+            // a sliding-window ring holds the window plus one prefill call's rows, so the rows a call
+            // stores never overwrite window rows that its earlier rows still read
+            ly.ring = (ly.swa && e->window > 0 && e->window + prefill_rows < max_seq) ? e->window + prefill_rows : max_seq;
             const size_t n = (size_t)max_batch * e->nkv * ly.ring * ly.hd;
             TRY(dalloc_t(e, &ly.kc, n));
             TRY(dalloc_t(e, &ly.vc, n));
@@ -842,8 +861,8 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
         G4_CUDA(cudaMemcpyAsync(e->rope_full, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice, e->st));
         G4_CUDA(cudaStreamSynchronize(e->st));
     }
-    // activations
-    const size_t B = max_batch;
+    // activations: decode rows (max_batch sequences) or prefill rows, whichever is more
+    const size_t B = std::max(max_batch, prefill_rows), BS = max_batch;
     TRY(dalloc_t(e, &e->x, B * dim)); TRY(dalloc_t(e, &e->x2, B * dim)); TRY(dalloc_t(e, &e->xn, B * dim)); TRY(dalloc_t(e, &e->xf, B * dim));
     TRY(dalloc_t(e, &e->q, B * e->qd_max)); TRY(dalloc_t(e, &e->qn, B * e->qd_max)); TRY(dalloc_t(e, &e->qo, B * e->qd_max));
     TRY(dalloc_t(e, &e->k, B * e->kvd_max)); TRY(dalloc_t(e, &e->v, B * e->kvd_max));
@@ -851,7 +870,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     TRY(dalloc_t(e, &e->hb, B * e->hidden)); TRY(dalloc_t(e, &e->hb2, B * e->hidden));
     TRY(dalloc_t(e, &e->g, B * pd));
     TRY(dalloc_t(e, &e->ple_tokb, B * pd * L)); TRY(dalloc_t(e, &e->ple_ctx, B * pd * L)); TRY(dalloc_t(e, &e->ple, B * pd * L));
-    TRY(dalloc_t(e, &e->logits, B * e->vocab));
+    TRY(dalloc_t(e, &e->logits, BS * e->vocab));
     int nmax = dim > e->qd_max ? dim : e->qd_max;
     nmax = nmax > e->hidden ? nmax : e->hidden;
     nmax = nmax > pd ? nmax : pd;
@@ -861,7 +880,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     TRY(dalloc_t(e, &e->attn_part, B * e->nh * e->max_chunks * (size_t)(e->hd_max + 2)));
     TRY(dalloc_t(e, &e->keys, B));
     G4_CUDA(cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device));
-    if (max_batch > 1) {  // tensor-core path of the batched step
+    if (B > 1) {  // tensor-core path of the batched step (and of prefill rows)
         int nmax = std::max(std::max(dim, e->hidden), std::max(e->qd_max, pd));
         size_t part = 0;
         const int shapes[][2] = {{e->qd_max, dim}, {e->kvd_max, dim}, {dim, e->qd_max}, {e->hidden, dim},
@@ -885,14 +904,16 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
     G4_CUDA(cudaMallocHost((void **)&e->h_err, sizeof(int)));
     *e->h_err = 0;
     TRY(dalloc_t(e, &e->d_tokens, B)); TRY(dalloc_t(e, &e->d_next, B)); TRY(dalloc_t(e, &e->d_pos, 1));
-    TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * B));
-    TRY(dalloc_t(e, &e->cand_v, B * 64)); TRY(dalloc_t(e, &e->cand_i, B * 64));
-    TRY(dalloc_t(e, &e->d_recent, B * (size_t)max_seq)); TRY(dalloc_t(e, &e->d_nrec, B));
-    G4_CUDA(cudaMallocHost((void **)&e->h_cand_v, sizeof(float) * B * 64));
-    G4_CUDA(cudaMallocHost((void **)&e->h_cand_i, sizeof(int) * B * 64));
+    TRY(dalloc_t(e, &e->d_hist, (size_t)max_seq * BS));
+    TRY(dalloc_t(e, &e->d_rowpos, B)); TRY(dalloc_t(e, &e->d_rowseq, B));
+    G4_CUDA(cudaMallocHost((void **)&e->h_rows, sizeof(int) * 3 * B));
+    TRY(dalloc_t(e, &e->cand_v, BS * 64)); TRY(dalloc_t(e, &e->cand_i, BS * 64));
+    TRY(dalloc_t(e, &e->d_recent, BS * (size_t)max_seq)); TRY(dalloc_t(e, &e->d_nrec, BS));
+    G4_CUDA(cudaMallocHost((void **)&e->h_cand_v, sizeof(float) * BS * 64));
+    G4_CUDA(cudaMallocHost((void **)&e->h_cand_i, sizeof(int) * BS * 64));
     G4_CUDA(cudaMallocHost((void **)&e->h_pos, sizeof(int) * (size_t)max_seq));
     for (int i = 0; i < max_seq; i++) e->h_pos[i] = i;
-    G4_CUDA(cudaMallocHost((void **)&e->h_tok, sizeof(int) * (size_t)max_seq * B));
+    G4_CUDA(cudaMallocHost((void **)&e->h_tok, sizeof(int) * (size_t)max_seq * BS));
     G4_CUDA(cudaStreamSynchronize(e->st));
     return G4_OK;
 }
@@ -902,9 +923,13 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch) {
 extern "C" {
 
 g4_engine *g4_engine_create(const g4_model_desc *m, int device, int max_seq, int max_batch) {
+    return g4_engine_create_ex(m, device, max_seq, max_batch, 0);
+}
+
+g4_engine *g4_engine_create_ex(const g4_model_desc *m, int device, int max_seq, int max_batch, int prefill_rows) {
     g4_engine *e = new g4_engine();
     e->device = device;
-    if (create(e, m, max_seq, max_batch) != G4_OK) {
+    if (create(e, m, max_seq, max_batch, prefill_rows) != G4_OK) {
         const int code = g4_last_error();
         char msg[512];
         snprintf(msg, sizeof msg, "%s", g4_last_error_string());
@@ -1188,6 +1213,40 @@ int g4_decode_batch_sample(g4_engine *e, int B, const int *tokens, int pos, floa
     TRY(stage_tokens(e, tokens, B, pos));
     TRY(run_step(e, B, 1, false, true));
     return sample_after_step(e, B, temp, topp, topk, repeat_penalty, recent, recent_ld, n_recent, rng, next);
+}
+
+int g4_prefill(g4_engine *e, int n_rows, const int *seq, const int *pos, const int *tokens) {
+    if (!e || n_rows <= 0 || !seq || !pos || !tokens) { set_error(G4_ERR_ARG, "prefill: bad arguments"); return G4_ERR_ARG; }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (n_rows > e->prefill_cap) {
+        set_error(G4_ERR_STATE, "prefill: %d rows > the engine's %d prefill rows (g4_engine_create_ex)", n_rows, e->prefill_cap);
+        return G4_ERR_STATE;
+    }
+    for (int i = 0; i < n_rows; i++) {
+        if (seq[i] < 0 || seq[i] >= e->max_batch || pos[i] < 0 || pos[i] >= e->max_seq || tokens[i] < 0 || tokens[i] >= e->vocab) {
+            set_error(G4_ERR_ARG, "prefill: row %d (sequence %d, position %d, token %d) out of range", i, seq[i], pos[i], tokens[i]);
+            return G4_ERR_ARG;
+        }
+        for (int j = 0; j < i; j++)  // one row per (sequence, position); a call spans < prefill_cap positions
+            if (seq[j] == seq[i] && (pos[j] == pos[i] || abs(pos[j] - pos[i]) >= e->prefill_cap)) {
+                set_error(G4_ERR_ARG, "prefill: rows %d and %d of sequence %d at positions %d and %d", j, i, seq[i], pos[j], pos[i]);
+                return G4_ERR_ARG;
+            }
+    }
+    G4_CUDA(cudaSetDevice(e->device));
+    G4_CUDA(cudaStreamSynchronize(e->st));  // the pinned staging rows are reused
+    int *h = e->h_rows;
+    memcpy(h, seq, sizeof(int) * n_rows);
+    memcpy(h + n_rows, pos, sizeof(int) * n_rows);
+    memcpy(h + 2 * n_rows, tokens, sizeof(int) * n_rows);
+    G4_CUDA(cudaMemcpyAsync(e->d_rowseq, h, sizeof(int) * n_rows, cudaMemcpyHostToDevice, e->st));
+    G4_CUDA(cudaMemcpyAsync(e->d_rowpos, h + n_rows, sizeof(int) * n_rows, cudaMemcpyHostToDevice, e->st));
+    G4_CUDA(cudaMemcpyAsync(e->d_tokens, h + 2 * n_rows, sizeof(int) * n_rows, cudaMemcpyHostToDevice, e->st));
+    TRY(enqueue_step_unfused(e, n_rows, 0, false, false, true));
+    e->hidden_src = e->x;
+    TRY(enqueue_err_check(e));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    return err_after_sync(e);
 }
 
 }  // extern "C"

@@ -101,7 +101,14 @@ struct AttnLayer {
     int early;                      // 1: every cache row but `pos` was written before the launch's
                                     //    stream predecessor started (earlier graph launches), so it
                                     //    may be copied before the grid dependency wait
+    // Prefill: row b of the launch is the query of cache sequence row_seq[b] at position row_pos[b]
+    // (device arrays; null: row b is sequence b at *pos_dev).  The K/V rows of the launch's positions
+    // are stored beforehand by launch_kv_append (append = 0 here).
+    const int *row_pos, *row_seq;
 };
+// Store the K/V rows of `rows` prefill rows (k-norm + RoPE of K, norm of V, as the attention kernels
+// do for a decode step's new row) into the layer's cache.
+int launch_kv_append(const AttnLayer &L, int rows, cudaStream_t st);
 int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq, cudaStream_t st);
 int attn_chunk_size();
 // Host: reference-exact RoPE table for positions [0, npos).

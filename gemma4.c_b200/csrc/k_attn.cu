@@ -145,7 +145,8 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = *pos_dev;
+    const int pos = L.row_pos ? L.row_pos[b] : *pos_dev;
+    const int cb = L.row_seq ? L.row_seq[b] : b;  // cache sequence of this query row
     int t0 = 0;
     if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
     const int nwin = pos + 1 - t0;
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
     const bool last_chunk = c == nch - 1;
     const bool new_row = L.append && last_chunk;  // this CTA owns row `pos`
     const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
-    const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
+    const size_t head_base = ((size_t)cb * L.n_kv + h) * L.src_ring;
     if constexpr (attn_tma<EPL>()) {
         // 0. the chunk's rows in ring order: slots s_a.. (and 0.. after a wrap) -> kbuf/vbuf rows 0..cnt-1.
         // Row `pos` of a layer that appends is (re)written below; its stale slot is read here and ignored.
@@ -187,11 +188,11 @@ __global__ void __launch_bounds__(256) attn_fused_kernel(AttnLayer L, const int 
         }
     } else if (new_row && warp == G) {
         const int slot = pos % L.ring;
-        float *kdst = L.kc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        float *kdst = L.kc + (((size_t)cb * L.n_kv + h) * L.ring + slot) * HD;
         warp_norm_rope<EPL>(L.k + (size_t)b * kvd + (size_t)h * HD, L.k_norm, cs, L.n_rot, L.eps, knew, kdst);
     } else if (new_row && warp == G + 1) {
         const int slot = pos % L.ring;
-        float *vdst = L.vc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        float *vdst = L.vc + (((size_t)cb * L.n_kv + h) * L.ring + slot) * HD;
         warp_norm_rope<EPL>(L.v + (size_t)b * kvd + (size_t)h * HD, nullptr, nullptr, 0, L.eps, vnew, vdst);
     }
     __syncthreads();
@@ -390,7 +391,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     if (!L.early) pdl_wait();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pos = *pos_dev;
+    const int pos = L.row_pos ? L.row_pos[b] : *pos_dev;
+    const int cb = L.row_seq ? L.row_seq[b] : b;  // cache sequence of this query row
     int t0 = 0;
     if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
     const int nwin = pos + 1 - t0;
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     const int beg = c * span, ctot = min(span, nwin - beg), nsub = (ctot + kSub - 1) / kSub;
     const bool new_row = L.append && c == nsplit - 1;  // this CTA owns row `pos`
     const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
-    const size_t head_base = ((size_t)b * L.n_kv + h) * L.src_ring;
+    const size_t head_base = ((size_t)cb * L.n_kv + h) * L.src_ring;
     const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
 
     // rows [beg + kSub*j, +cnt) of the split (ring slots, split at a wrap) -> stage j % kStages.  Row `pos`
@@ -443,11 +445,11 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
         }
     } else if (new_row && warp == G) {
         const int slot = pos % L.ring;
-        float *kdst = L.kc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        float *kdst = L.kc + (((size_t)cb * L.n_kv + h) * L.ring + slot) * HD;
         warp_norm_rope<EPL>(L.k + (size_t)b * kvd + (size_t)h * HD, L.k_norm, cs, L.n_rot, L.eps, knew, kdst);
     } else if (new_row && warp == G + 1) {
         const int slot = pos % L.ring;
-        float *vdst = L.vc + (((size_t)b * L.n_kv + h) * L.ring + slot) * HD;
+        float *vdst = L.vc + (((size_t)cb * L.n_kv + h) * L.ring + slot) * HD;
         warp_norm_rope<EPL>(L.v + (size_t)b * kvd + (size_t)h * HD, nullptr, nullptr, 0, L.eps, vnew, vdst);
     }
     __syncthreads();
@@ -625,6 +627,38 @@ static int launch_fused_g(const AttnLayer &L, int G, dim3 grid, const int *pos_d
     case 4: return launch_fused_eg<EPL, 4>(grid, L, pos_dev, st);
     default: set_error(G4_ERR_ARG, "attention: GQA group %d unsupported", G); return G4_ERR_ARG;
     }
+}
+
+// K/V rows of prefill row blockIdx.x, kv head blockIdx.y: warp 0 normalises and rotates K, warp 1
+// normalises V, with the same device function and expressions as the attention kernels' new row.
+template <int EPL>
+__global__ void kv_append_kernel(AttnLayer L) {
+    constexpr int HD = EPL * 32;
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, h = blockIdx.y, warp = threadIdx.x >> 5;
+    const int pos = L.row_pos[r], cb = L.row_seq[r];
+    const int kvd = L.n_kv * HD, slot = pos % L.ring;
+    const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
+    const size_t dst = (((size_t)cb * L.n_kv + h) * L.ring + slot) * HD;
+    if (warp == 0)
+        warp_norm_rope<EPL>(L.k + (size_t)r * kvd + (size_t)h * HD, L.k_norm, cs, L.n_rot, L.eps, L.kc + dst, nullptr);
+    else
+        warp_norm_rope<EPL>(L.v + (size_t)r * kvd + (size_t)h * HD, nullptr, nullptr, 0, L.eps, L.vc + dst, nullptr);
+}
+
+int launch_kv_append(const AttnLayer &L, int rows, cudaStream_t st) {
+    if (!L.row_pos || !L.row_seq || rows <= 0) { set_error(G4_ERR_ARG, "kv_append: rows missing"); return G4_ERR_ARG; }
+    const dim3 grid(rows, L.n_kv);
+    switch (L.hd) {
+    case 64: G4_CUDA(launch_pdl(kv_append_kernel<2>, grid, dim3(64), 0, st, L)); break;
+    case 128: G4_CUDA(launch_pdl(kv_append_kernel<4>, grid, dim3(64), 0, st, L)); break;
+    case 256: G4_CUDA(launch_pdl(kv_append_kernel<8>, grid, dim3(64), 0, st, L)); break;
+    case 512: G4_CUDA(launch_pdl(kv_append_kernel<16>, grid, dim3(64), 0, st, L)); break;
+    default: set_error(G4_ERR_ARG, "kv_append: head_dim %d unsupported", L.hd); return G4_ERR_ARG;
+    }
+    G4_LAUNCHED();
+    return G4_OK;
 }
 
 int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq, cudaStream_t st) {

@@ -242,6 +242,10 @@ size_t g4_model_desc_bytes(void);
 /* Upload the model to `device` and allocate state for `max_batch` sequences
  * of up to `max_seq` positions.  Returns NULL on error (see g4_last_error). */
 g4_engine *g4_engine_create(const g4_model_desc *m, int device, int max_seq, int max_batch);
+/* As g4_engine_create, plus room for batched prefill: g4_prefill calls of up
+ * to prefill_rows rows (sliding-window caches then hold window + prefill_rows
+ * slots).  Not part of the reference interface. */
+g4_engine *g4_engine_create_ex(const g4_model_desc *m, int device, int max_seq, int max_batch, int prefill_rows);
 int g4_engine_destroy(g4_engine *e);
 /* Device bytes held by the engine (weights, KV cache, state). */
 size_t g4_engine_device_bytes(const g4_engine *e);
@@ -270,6 +274,19 @@ int g4_generate_greedy(g4_engine *e, const int *prompt, int n_prompt, int max_ne
  * Returns the number of tokens written to out_tokens, or -1. */
 int g4_generate(g4_engine *e, const int *prompt, int n_prompt, int max_new, float temp, float topp, int topk,
                 float repeat_penalty, int penalty_last_n, uint64_t seed, int eos, int *out_tokens);
+
+/* Batched prefill (the lm_mode 0 forwards of generate's prompt loop,
+ * main.c:2366-2402, for many positions and sequences at once): row i is token
+ * tokens[i] of sequence seq[i] at position pos[i].  All rows run through every
+ * layer together (tensor-core GEMMs over the rows); each layer stores the K/V
+ * rows of all rows, then each row attends over its own causal window with
+ * the decode step's arithmetic, so the cache and hidden states equal those of
+ * decoding the rows one position at a time, bit for bit.  The rows of one
+ * sequence must be distinct positions spanning fewer than prefill_rows, and
+ * every earlier position of the sequence must already be in the cache (an
+ * earlier call).  No LM head: run the last prompt token through
+ * g4_forward / g4_decode_batch.  n_rows <= the engine's prefill_rows. */
+int g4_prefill(g4_engine *e, int n_rows, const int *seq, const int *pos, const int *tokens);
 
 /* Batched greedy decode of B independent sequences in lockstep (all at the
  * same position).  tokens[B] in, next[B] out (argmax of each sequence's
