@@ -371,20 +371,21 @@ def config0_gemv(g4, reps: int = 20, rows: int = 10240):
 
 # ---------------------------------------------------------------- batch-1 decode
 def batch1_decode(g4, model, prompt: int, new: int, dev: int):
-    """Batch-1 greedy decode: `prompt` positions run one by one (lm_mode 0,
-    the reference's prefill loop, main.c:2366-2402), then `new` greedy tokens
+    """Batch-1 greedy decode: the first `prompt`-1 positions prefilled in
+    batches (g4_prefill, the lm_mode 0 forwards of main.c:2366-2402), the last
+    prompt token through the model with the LM head, then `new` greedy tokens
     timed with CUDA events on the engine stream (argmax fed back on the
     device).  e2e: the same tokens through g4_forward with a host token in
     and the host argmax out every position (the drop-in for forward())."""
     import torch
     S = g4.synth
-    eng = g4.Engine(model, dev, max_seq=prompt + 2 * new + 8, max_batch=1)
+    eng = g4.Engine(model, dev, max_seq=prompt + 2 * new + 8, max_batch=1, prefill_rows=256)
     try:
         toks = np.random.default_rng(4321).integers(0, S.E4B.vocab_size, size=prompt).astype(np.int32)
         td = torch.from_numpy(toks).cuda()
         t0 = time.perf_counter()
-        for pos in range(prompt):
-            eng.decode_batch_device(1, td.data_ptr() + 4 * pos, pos, 1 if pos == prompt - 1 else 0, None)
+        eng.prefill_prompts(toks[None, :], prompt - 1)
+        eng.decode_batch_device(1, td.data_ptr() + 4 * (prompt - 1), prompt - 1, 1, None)
         eng.sync()
         prefill_s = time.perf_counter() - t0
         s = torch.cuda.ExternalStream(eng.stream())
@@ -420,7 +421,7 @@ def batch1_decode(g4, model, prompt: int, new: int, dev: int):
     gbs = byts / (ms / new * 1e-3) / 1e9
     return {"workload": "batch-1 greedy decode, %d-token prompt run position by position, %d tokens timed" % (prompt, new),
             "value": new / (ms * 1e-3), "unit": "tok/s", "ms_per_token": ms / new, "prefill_s": prefill_s,
-            "prefill_tok_s": prompt / prefill_s,
+            "prefill_tok_s": prompt / prefill_s, "prefill": "batched (g4_prefill, 256 rows per call)",
             "step_roofline": {"bound": "hbm", "algorithmic_bytes_per_token": byts, "achieved": gbs,
                               "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": kind},
             "e2e": {"value": new / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
@@ -562,12 +563,17 @@ def main():
     ap.add_argument("--seqs", type=int, default=None, help="total sequences (default 64 / 1)")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 4096 / 512)")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--prefill", default=None, choices=["run", "fill"],
-                    help="run: decode the prompt position by position; fill: seeded KV rows for the prompt "
-                         "(default: fill for batch64, run for batch1)")
+    ap.add_argument("--prefill", default=None, choices=["run", "fill", "batched"],
+                    help="run: decode the prompt position by position; fill: seeded KV rows for the prompt; "
+                         "batched: g4_prefill over all sequences (default: fill for batch64, batched for batch1)")
+    ap.add_argument("--prefill-sample", type=int, default=512,
+                    help="batch64 extras: prompt positions per sequence of the timed batched-prefill sample")
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--gemv-rows", type=int, default=10240, help="gemv0 workload: matrix rows")
     ap.add_argument("--tc-min", type=int, default=None, help="engine tensor-core batch threshold")
+    ap.add_argument("--lm-split", action="store_true",
+                    help="N > 1: row-split the tied LM head over the ranks (NCCL all-gathers of the hidden "
+                         "states and of one argmax key per sequence)")
     a = ap.parse_args()
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -637,9 +643,15 @@ def main():
     model = S.make_model(S.E4B, seed=3)
     wbytes = model.weight_bytes()
     max_seq = prompt + a.warmup + a.steps * 2 + 8
-    eng = g4.Engine(model, dist.local, max_seq=max_seq, max_batch=B)
+    eng = g4.Engine(model, dist.local, max_seq=max_seq, max_batch=B, prefill_rows=256)
     if a.tc_min:
         eng.set_tc_min_batch(a.tc_min)
+    if a.lm_split and dist.world > 1:
+        import torch.distributed as tdist
+        box = [g4.nccl_unique_id() if dist.rank == 0 else None]
+        tdist.broadcast_object_list(box, src=0)
+        eng.lm_split(box[0], dist.rank, dist.world)
+        cfg["lm_head"] = "row-split over %d ranks (NCCL all-gather of hidden states and argmax keys)" % dist.world
     model_keep = model  # host tensors stay alive until the end
     stream = eng.stream()
     # prompts: seeded per global sequence id
@@ -647,11 +659,27 @@ def main():
     allp = rng.integers(0, S.E4B.vocab_size, size=(seqs, prompt), dtype=np.int32)
     mine = allp[mine_ids.start:mine_ids.stop]
     prompts_dev = torch.from_numpy(np.ascontiguousarray(mine.T)).cuda()  # [prompt][B]
-    prefill = a.prefill or ("fill" if a.workload == "batch64" else "run")
+    prefill = a.prefill or ("fill" if a.workload == "batch64" else "batched")
     cfg["prefill"] = prefill
+    prefill_sample = None
     t0 = time.perf_counter()
     if prefill == "fill":  # KV rows of the prompt from a seed; the last prompt token runs for real
         eng.fill_kv(prompt - 1, seed=1234 + dist.rank)
+        if not a.no_extras and dist.world == 1:
+            # a timed batched-prefill sample: the first positions of every sequence's prompt through
+            # g4_prefill (tensor-core GEMMs over 256 rows per call), over the seeded rows
+            n = min(a.prefill_sample, prompt - 1)
+            eng.sync()
+            t1 = time.perf_counter()
+            eng.prefill_prompts(mine, n)
+            eng.sync()
+            dt = time.perf_counter() - t1
+            prefill_sample = {"tokens": n * B, "s": dt, "tok_s": n * B / dt,
+                              "sample": "positions 0..%d of %d sequences through g4_prefill, 256 rows per call"
+                                        % (n - 1, B)}
+        eng.decode_batch_device(B, prompts_dev.data_ptr() + (prompt - 1) * B * 4, prompt - 1, 1, None)
+    elif prefill == "batched":
+        eng.prefill_prompts(mine, prompt - 1)
         eng.decode_batch_device(B, prompts_dev.data_ptr() + (prompt - 1) * B * 4, prompt - 1, 1, None)
     else:
         for pos in range(prompt):
@@ -705,7 +733,7 @@ def main():
            "vs_baseline": None, "dtype": dtype,
            "data": "synthetic (seeded random-init model and prompts)", "config": cfg,
            "e2e": e2e, "gpu_launches": int(kernels_per_step * a.steps),
-           "kernels_per_step": kernels_per_step, "prefill_s": prefill_s,
+           "kernels_per_step": kernels_per_step, "prefill_s": prefill_s, "prefill_sample": prefill_sample,
            "weights_gb": wbytes / 1e9, "clocks": clk.summary()}
     if dist.rank == 0 and not a.no_extras:
         rl = gemv_roofline(g4, B)

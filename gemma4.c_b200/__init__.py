@@ -91,6 +91,11 @@ SIGNATURES = [
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
     ("g4_engine_time_attention", ip, [vp, vp, ip, ip, ip, vp]),
     ("g4_set_tc_min_batch", ip, [ip]),
+    ("g4_nccl_unique_id", ip, [vp]),
+    ("g4_engine_lm_split", ip, [vp, vp, ip, ip]),
+    ("g4_lm_split_rows", ip, [ip, ip, ip, vp, vp]),
+    ("g4_lm_split_merge", ip, [vp, ip, ip, ip, ip, vp]),
+    ("g4_argmax_keys", ip, [vp, ip, ip, vp]),
     ("g4_engine_set_tc_min_batch", ip, [vp, ip]),
 ]
 
@@ -212,6 +217,34 @@ def sample_token(logits, temp: float, topp: float, topk: int, rng_state: int):
     if r < 0:
         _check(lib().g4_last_error() or G4_ERR_ARG)
     return r, st.value
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    _check(lib().g4_nccl_unique_id(buf))
+    return buf.raw
+
+
+def lm_split_rows(vocab: int, world: int, rank: int):
+    r0, r1 = C.c_int(), C.c_int()
+    chunk = lib().g4_lm_split_rows(vocab, world, rank, C.byref(r0), C.byref(r1))
+    if chunk < 0:
+        _check(G4_ERR_ARG)
+    return chunk, r0.value, r1.value
+
+
+def lm_split_merge(keys_all: np.ndarray, world: int, rank: int, B: int, chunk: int) -> np.ndarray:
+    ka = np.ascontiguousarray(keys_all, dtype=np.uint64)
+    out = np.zeros(B, np.uint64)
+    _check(lib().g4_lm_split_merge(_p(ka), world, rank, B, chunk, _p(out)))
+    return out
+
+
+def argmax_key(logits, row0: int = 0) -> int:
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    k = C.c_uint64()
+    _check(lib().g4_argmax_keys(_p(lg), lg.size, row0, C.byref(k)))
+    return k.value
 
 
 def weight_upload(host: np.ndarray, t: int, n: int, rows: int) -> int:
@@ -363,6 +396,11 @@ class Engine:
         ms = np.zeros(1, np.float32)
         _check(lib().g4_engine_time_attention(self.h, _p(ls), len(ls), batch, reps, _p(ms)))
         return float(ms[0])
+
+    def lm_split(self, nccl_id: bytes, rank: int, world: int):
+        """Row-split the LM head over `world` ranks (one engine per GPU); nccl_id from nccl_unique_id()."""
+        buf = C.create_string_buffer(bytes(nccl_id), 128)
+        _check(lib().g4_engine_lm_split(self.h, buf, rank, world))
 
     def set_tc_min_batch(self, b: int) -> int:
         r = lib().g4_engine_set_tc_min_batch(self.h, b)

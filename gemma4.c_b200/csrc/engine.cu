@@ -21,7 +21,9 @@
 //   gemv      g = gelu(Winp_gate.x) * ple[l]           (fused epilogue)
 //   gemv      p_raw = Wproj.g
 // then the final residual, output norm, tied LM head + softcap + argmax.
+#include <dlfcn.h>
 #include <math.h>
+#include <nccl.h>
 #include <string.h>
 
 #include <algorithm>
@@ -74,6 +76,11 @@ struct g4_engine {
     int *d_err = nullptr;  // bounded-wait status word written by the kernels
     // prefill: rows per g4_prefill call, the (sequence, position) of each row (device, pinned host)
     int prefill_cap = 0;
+    // row-split LM head over `split_world` ranks (g4_engine_lm_split): this rank's rows [lm_r0, lm_r1)
+    ncclComm_t comm = nullptr;
+    int split_rank = 0, split_world = 1, lm_r0 = 0, lm_r1 = 0, lm_chunk = 0;
+    float *xf_all = nullptr;
+    unsigned long long *keys_loc = nullptr, *keys_all = nullptr;
     int *d_rowpos = nullptr, *d_rowseq = nullptr, *h_rows = nullptr;
     // sampler: top-k candidates per sequence (device and pinned host), recent tokens for the penalty
     float *cand_v = nullptr, *h_cand_v = nullptr;
@@ -95,6 +102,54 @@ struct g4_engine {
 };
 
 namespace {
+
+// NCCL is loaded at run time (the copy a host process already loaded, e.g. torch's, when there
+// is one), so the library has no link-time dependency on it.
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+int nccl_load() {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.ok) return G4_OK;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) { set_error(G4_ERR_STATE, "NCCL (libnccl.so.2) not found: %s", dlerror()); return G4_ERR_STATE; }
+    g_nccl.get_unique_id = (ncclResult_t(*)(ncclUniqueId *))dlsym(h, "ncclGetUniqueId");
+    g_nccl.comm_init_rank = (ncclResult_t(*)(ncclComm_t *, int, ncclUniqueId, int))dlsym(h, "ncclCommInitRank");
+    g_nccl.all_gather = (ncclResult_t(*)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t))dlsym(h, "ncclAllGather");
+    g_nccl.comm_destroy = (ncclResult_t(*)(ncclComm_t))dlsym(h, "ncclCommDestroy");
+    g_nccl.error_string = (const char *(*)(ncclResult_t))dlsym(h, "ncclGetErrorString");
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.all_gather || !g_nccl.comm_destroy || !g_nccl.error_string) {
+        set_error(G4_ERR_STATE, "NCCL symbols missing");
+        return G4_ERR_STATE;
+    }
+    g_nccl.ok = true;
+    return G4_OK;
+}
+#define G4_NCCL(call)                                                                          \
+    do {                                                                                       \
+        const ncclResult_t r_ = (call);                                                        \
+        if (r_ != ncclSuccess) {                                                               \
+            set_error(G4_ERR_CUDA, "%s failed: %s", #call, g_nccl.error_string(r_));           \
+            return G4_ERR_CUDA;                                                                \
+        }                                                                                      \
+    } while (0)
+
+__global__ void lm_split_merge_kernel(const unsigned long long *keys_all, int world, int rank, int B, int chunk,
+                                      unsigned long long *keys) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) keys[b] = lm_split_merge_one(keys_all, world, rank, B, chunk, b);
+}
 
 int dalloc(g4_engine *e, void **p, size_t bytes) {
     *p = nullptr;
@@ -156,6 +211,7 @@ void destroy(g4_engine *e) {
     cudaSetDevice(e->device);
     if (e->st) cudaStreamSynchronize(e->st);
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    if (e->comm) g_nccl.comm_destroy(e->comm);  // after the graphs that hold its collectives
     for (void *p : e->allocs) cudaFree(p);
     if (e->h_pos) cudaFreeHost(e->h_pos);
     if (e->h_tok) cudaFreeHost(e->h_tok);
@@ -325,6 +381,30 @@ bool attach_operand(g4_engine *e, ResNorm &r, int B, int type, int n) {
     return true;
 }
 
+// Row-split tied LM head (after the output norm wrote xf[B][dim]): gather every rank's final hidden
+// states, compute this rank's vocabulary rows for all of them (softcap + first-max key per
+// sequence), gather the slice keys and merge them into this rank's sequences' keys: the argmax
+// over the whole vocabulary with the reference's first-max rule (main.c:2045-2050).
+int enqueue_lm_split(g4_engine *e, int B) {
+    const int W = e->split_world, BT = W * B, rows = e->lm_r1 - e->lm_r0;
+    G4_NCCL(g_nccl.all_gather(e->xf, e->xf_all, (size_t)B * e->dim, ncclFloat32, e->comm, e->st));
+    G4_CUDA(cudaMemsetAsync(e->keys_loc, 0, sizeof(unsigned long long) * BT, e->st));
+    const uint8_t *w = (const uint8_t *)e->embd + (size_t)e->lm_r0 * device_row_bytes(e->embd_t, e->dim);
+    if (rows > 0) {
+        if (use_tc(e, BT, e->embd_t, EPI_SOFTCAP_ARGMAX))
+            TRY(tc_gemm(e, w, e->embd_t, e->dim, rows, e->xf_all, e->dim, false, nullptr, rows, BT, EPI_SOFTCAP_ARGMAX,
+                        e->keys_loc, e->softcap));
+        else
+            TRY(gemv(e, w, e->embd_t, e->dim, rows, e->xf_all, e->dim, false, nullptr, rows, BT, EPI_SOFTCAP_ARGMAX,
+                     nullptr, 0, e->keys_loc, e->softcap));
+    }
+    G4_NCCL(g_nccl.all_gather(e->keys_loc, e->keys_all, (size_t)BT, ncclUint64, e->comm, e->st));
+    G4_CUDA(launch_pdl(lm_split_merge_kernel, dim3((B + 127) / 128), dim3(128), 0, e->st,
+                       (const unsigned long long *)e->keys_all, W, e->split_rank, B, e->lm_chunk, e->keys));
+    G4_LAUNCHED();
+    return launch_keys_to_tokens(e->keys, e->d_next, B, e->st);
+}
+
 // One step for B rows.  Decode: row b is sequence b at the engine position.  Prefill (prefill =
 // true, lm_mode 0): row b is sequence d_rowseq[b] at position d_rowpos[b]; every layer that owns a
 // cache stores the K/V rows of all rows first, then each row attends with exactly the decode
@@ -477,10 +557,11 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     ResNorm rf{};
     rf.x_in = e->x; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = e->x;
     rf.pre_w = lm_mode ? e->norm_out : nullptr; rf.xn_out = e->xf; rf.dim = dim; rf.eps = e->eps;
-    const bool tc_head = lm_mode && use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX);
+    const bool tc_head = lm_mode && !e->comm && use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX);
     const bool head_ready = tc_head && attach_operand(e, rf, B, e->embd_t, dim);
     TRY(launch_resnorm(rf, B, e->st));
     if (!lm_mode) return G4_OK;
+    if (e->comm) return enqueue_lm_split(e, B);
     // tied LM head + softcap + first-max argmax (1780-1796, 2045-2050)
     const bool dense = e->embd_t == G4_F32 || e->embd_t == G4_F16 || e->embd_t == G4_BF16;
     if (tc_head)
@@ -627,6 +708,13 @@ int enqueue_step_fused(g4_engine *e, int B, int lm_mode, bool from_keys, bool wa
         return G4_OK;
     }
     e->hidden_src = e->xf;
+    if (e->comm) {  // the output norm on its own, then the row-split head
+        ResNorm rf{};
+        rf.x_in = cur; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = nxt;
+        rf.pre_w = e->norm_out; rf.xn_out = e->xf; rf.dim = dim; rf.eps = e->eps;
+        TRY(launch_resnorm(rf, B, e->st));
+        return enqueue_lm_split(e, B);
+    }
     const bool dense = is_dense(e->embd_t);
     TRY(gemv_p(e, e->embd, e->embd_t, dim, e->vocab, &pl, 1, nullptr, dim, (want_logits || dense) ? e->logits : nullptr,
                e->vocab, B, EPI_SOFTCAP_ARGMAX, nullptr, 0, e->keys, e->softcap));
@@ -1247,6 +1335,76 @@ int g4_prefill(g4_engine *e, int n_rows, const int *seq, const int *pos, const i
     TRY(enqueue_err_check(e));
     G4_CUDA(cudaStreamSynchronize(e->st));
     return err_after_sync(e);
+}
+
+int g4_nccl_unique_id(void *id) {
+    if (!id) { set_error(G4_ERR_ARG, "nccl_unique_id: null"); return G4_ERR_ARG; }
+    TRY(nccl_load());
+    ncclUniqueId u;
+    G4_NCCL(g_nccl.get_unique_id(&u));
+    memcpy(id, &u, sizeof u);
+    return G4_OK;
+}
+
+int g4_lm_split_rows(int vocab, int world, int rank, int *row0, int *row1) {
+    if (vocab <= 0 || world <= 0 || rank < 0 || rank >= world || !row0 || !row1) {
+        set_error(G4_ERR_ARG, "lm_split_rows: bad arguments");
+        return G4_ERR_ARG;
+    }
+    const int chunk = ((vocab + world - 1) / world + 127) / 128 * 128;  // whole 128-row tiles per rank
+    *row0 = std::min(vocab, rank * chunk);
+    *row1 = std::min(vocab, *row0 + chunk);
+    return chunk;
+}
+
+int g4_lm_split_merge(const uint64_t *keys_all, int world, int rank, int B, int chunk, uint64_t *out) {
+    if (!keys_all || !out || world <= 0 || rank < 0 || rank >= world || B <= 0 || chunk <= 0) {
+        set_error(G4_ERR_ARG, "lm_split_merge: bad arguments");
+        return G4_ERR_ARG;
+    }
+    for (int b = 0; b < B; b++)
+        out[b] = lm_split_merge_one((const unsigned long long *)keys_all, world, rank, B, chunk, b);
+    return G4_OK;
+}
+
+int g4_argmax_keys(const float *logits, int n, int row0, uint64_t *key) {
+    if (!logits || n <= 0 || !key) { set_error(G4_ERR_ARG, "argmax_keys: bad arguments"); return G4_ERR_ARG; }
+    unsigned long long best = 0ull;
+    for (int i = 0; i < n; i++) {  // the device's packed key (argmax_key) computed on the host
+        uint32_t b;
+        memcpy(&b, logits + i, 4);
+        if ((b & 0x7fffffffu) == 0u) b = 0u;
+        b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+        const unsigned long long k = ((unsigned long long)b << 32) | (uint32_t)(0xffffffffu - (uint32_t)(i + row0));
+        best = k > best ? k : best;
+    }
+    *key = best;
+    return G4_OK;
+}
+
+int g4_engine_lm_split(g4_engine *e, const void *nccl_id, int rank, int world) {
+    if (!e || !nccl_id || world < 2 || rank < 0 || rank >= world) {
+        set_error(G4_ERR_ARG, "lm_split: bad arguments");
+        return G4_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (e->comm) { set_error(G4_ERR_STATE, "lm_split: already split"); return G4_ERR_STATE; }
+    TRY(nccl_load());
+    G4_CUDA(cudaSetDevice(e->device));
+    G4_CUDA(cudaStreamSynchronize(e->st));
+    int r0 = 0, r1 = 0;
+    const int chunk = g4_lm_split_rows(e->vocab, world, rank, &r0, &r1);
+    if (chunk < 0) return G4_ERR_ARG;
+    TRY(dalloc_t(e, &e->xf_all, (size_t)world * e->max_batch * e->dim));
+    TRY(dalloc_t(e, &e->keys_loc, (size_t)world * e->max_batch));
+    TRY(dalloc_t(e, &e->keys_all, (size_t)world * world * e->max_batch));
+    ncclUniqueId u;
+    memcpy(&u, nccl_id, sizeof u);
+    G4_NCCL(g_nccl.comm_init_rank(&e->comm, world, u, rank));
+    e->split_rank = rank; e->split_world = world; e->lm_r0 = r0; e->lm_r1 = r1; e->lm_chunk = chunk;
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);  // captured without the split
+    e->graphs.clear(); e->graph_kernels.clear(); e->graph_hidden.clear();
+    return G4_OK;
 }
 
 }  // extern "C"

@@ -155,5 +155,24 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 __host__ __device__ inline int argmax_key_index(unsigned long long k) {
     return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
 }
+// The key of a row-split LM head slice that starts at row row0, as a key over the whole vocabulary
+// (0 = no row stays 0): the value part is unchanged, the index becomes row0 + local index, so the
+// largest key over all slices is the first index of the largest logit.
+__host__ __device__ inline unsigned long long lm_key_global(unsigned long long k, int row0) {
+    if (!k) return 0ull;
+    const uint32_t idx = 0xffffffffu - (uint32_t)(k & 0xffffffffu);
+    return (k & 0xffffffff00000000ull) | (unsigned long long)(0xffffffffu - (idx + (uint32_t)row0));
+}
+// Merge of a row-split LM head for the B sequences of rank `rank`: keys_all[rr][world*B] are the
+// slice keys of rank rr (slice rr starts at row rr*chunk) for every rank's sequences.
+__host__ __device__ inline unsigned long long lm_split_merge_one(const unsigned long long *keys_all, int world,
+                                                                int rank, int B, int chunk, int b) {
+    unsigned long long best = 0ull;
+    for (int rr = 0; rr < world; rr++) {
+        const unsigned long long k = lm_key_global(keys_all[(size_t)rr * world * B + (size_t)rank * B + b], rr * chunk);
+        best = k > best ? k : best;
+    }
+    return best;
+}
 
 }  // namespace g4

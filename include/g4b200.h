@@ -334,6 +334,29 @@ int g4_engine_set_tc_min_batch(g4_engine *e, int min_batch);
 /* Number of kernels in the most recent step (the nodes of its CUDA graph). */
 int g4_engine_last_step_kernels(const g4_engine *e);
 
+/* Optional row-split LM head over `world` GPUs, one engine per GPU (one
+ * process per GPU), each decoding its own sequences in lockstep with the
+ * others (the same B, positions and lm_mode on every rank).  Rank r owns the
+ * vocabulary rows [r*chunk, (r+1)*chunk) (g4_lm_split_rows).  Each step
+ * gathers every rank's output-normed hidden states (one NCCL all-gather of
+ * B*dim floats), computes its rows for all of them with the softcap and a
+ * packed (value, first index) key per sequence, gathers the keys (one
+ * all-gather of 8 bytes per sequence and rank) and keeps the largest key of
+ * each of its sequences: the first index of the largest logit over the whole
+ * vocabulary, as the reference's greedy scan (main.c:2045-2050).  Logits are
+ * not returned in this mode.  nccl_id: 128 bytes from g4_nccl_unique_id on
+ * one rank, passed to every rank.  NCCL is loaded at run time
+ * (libnccl.so.2).  Not part of the reference interface. */
+int g4_nccl_unique_id(void *nccl_id);
+int g4_engine_lm_split(g4_engine *e, const void *nccl_id, int rank, int world);
+/* Host helpers of the split (used by tests): the rows of rank `rank`
+ * (returns the rows per rank, -1 on error), the merge of the gathered keys
+ * keys_all[world][world*B] into out[B] for rank `rank`, and the packed key of
+ * the first largest value of logits[n] with row indices offset by row0. */
+int g4_lm_split_rows(int vocab, int world, int rank, int *row0, int *row1);
+int g4_lm_split_merge(const uint64_t *keys_all, int world, int rank, int B, int chunk, uint64_t *out);
+int g4_argmax_keys(const float *logits, int n, int row0, uint64_t *key);
+
 /* Test taps: hidden state x[dim] of sequence b after the last step, and the
  * K/V rows (n_kv_heads * head_dim floats each) stored for (layer, pos). */
 int g4_engine_get_hidden(g4_engine *e, int b, float *x);
