@@ -723,7 +723,7 @@ def main():
            "d2h_bytes_per_step": 4 * B, "api": "g4_decode_batch (host token ids in, host next ids out)"}
 
     hbm_peak, tc_peak, peak_kind = measured_peaks()
-    if B >= 9:  # the engine's tensor-core threshold (engine.cu tc_min_batch)
+    if B >= 2:  # the engine's tensor-core threshold (engine.cu tc_min_batch)
         dtype = ("tensor cores: Q4_K as exact fp16 integer products, Q5_K int8 x int8 -> int32, Q6_K and BF16 "
                  "on split-fp32 activations (fp16 x2 / bf16 x3) -> fp32; fp32 attention, KV cache and norms")
     else:

@@ -97,7 +97,7 @@ struct g4_engine {
     uint8_t *tcq = nullptr, *tc6 = nullptr, *tcb = nullptr;  // B operands (Q4_K/Q5_K, Q6_K, BF16)
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
-    int nsm = 0, tc_min_batch = 9;
+    int nsm = 0, tc_min_batch = 2;  // measured: the tensor-core step wins from 2 sequences (5.2 vs 9.2 ms)
     std::mutex mu;
 };
 

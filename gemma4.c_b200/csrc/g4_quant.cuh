@@ -115,10 +115,11 @@ __device__ __forceinline__ void q6x_block(const float (&v)[8], uint32_t (&p)[6],
 }
 
 // The exact block dot from its three piece dots D_j = sum_i v_i * a_j,i:
-// the float of D0*2^16 + D1*2^8 + D2 (|D_j| < 2^27), rounded once.
+// the float of D0*2^16 + D1*2^8 + D2 (|D_j| < 2^27), rounded once.  The sum
+// is formed exactly in double (every partial is an integer below 2^44).
 __device__ __forceinline__ float q6x_dot(int D0, int D1, int D2) {
-    const long long D = (long long)D0 * 65536ll + (long long)D1 * 256ll + (long long)D2;
-    return __ll2float_rn(D);
+    const double D = __fma_rn((double)D0, 65536.0, __fma_rn((double)D1, 256.0, (double)D2));
+    return __double2float_rn(D);
 }
 
 }  // namespace g4

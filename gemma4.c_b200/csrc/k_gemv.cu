@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restri
         const uint16_t *r = (const uint16_t *)w + (size_t)row * n;
         const bool bf = type == G4_BF16;
         if (vec) {
+#pragma unroll 4
             for (int j = lane * 8; j < n; j += 256) {
                 const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + j));
                 const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
@@ -229,7 +230,10 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
         // two CTAs per SM (<= 100 KB of staged activations each), about one wave in total
         const int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : 0;
         if (NS) {
-            const int gy = (B + NS - 1) / NS, gx = std::max(1, std::min((rows + 7) / 8, 296 / gy));
+            // short rows: one row per warp (staging the activations is cheap); long rows: about two
+            // waves of CTAs that each stage once and loop over rows
+            const int gy = (B + NS - 1) / NS;
+            const int gx = n <= 1024 ? (rows + 7) / 8 : std::max(1, std::min((rows + 7) / 8, 296 / gy));
             const dim3 grid(gx, gy);
             if (NS == 16) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<16>, grid, dim3(256), per * 16, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
             else if (NS == 8) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<8>, grid, dim3(256), per * 8, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));

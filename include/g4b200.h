@@ -325,7 +325,7 @@ int g4_engine_fill_kv(g4_engine *e, int npos, uint64_t seed);
 int g4_engine_time_attention(g4_engine *e, const int *layers, int n, int batch, int reps, float *ms);
 
 /* Batch size from which the engine's step runs the K-quant projections and
- * the LM head on the tensor cores (default 9; below it, streaming GEMVs with
+ * the LM head on the tensor cores (default 2; below it, streaming GEMVs with
  * the residual/norm work fused in).  Results do not depend on it: both paths
  * compute every row bit-identically.  Not part of the reference interface;
  * returns the previous value, or -1 on a bad argument. */
