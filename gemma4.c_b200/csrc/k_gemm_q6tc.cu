@@ -77,7 +77,7 @@ struct Q6State {
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
-    float ys[8][2][16];  // per epilogue warp: activation block scales of its sequences, by item parity
+    float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
 };
 
 __device__ __forceinline__ bool q6_wait(Q6State &S, uint64_t *bar, uint32_t parity) {
@@ -334,21 +334,28 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
             return row < a.rows ? __ldg(reinterpret_cast<const uint16_t *>(a.w + (size_t)row * a.row_bytes + (size_t)a.nb * 208) + bb)
                                 : (uint16_t)0;
         };
+        // activation block scales of this warp's sequences for block bb, both passes (lane < SP: pass 0,
+        // lane - SP: pass 1), loaded one block ahead
+        auto fetch_ys = [&](int bb) -> float {
+            const int ps = lane / SP, l = lane % SP;
+            return ps < NPASS ? __ldg(a.yd + (size_t)bb * NP + ps * NPP + p * SP + l) : 0.0f;
+        };
         uint16_t nhd = u < a.units ? fetch_d(u, b) : (uint16_t)0;
+        float nys = u < a.units ? fetch_ys(b) : 0.0f;
         while (u < a.units && ok) {
             const int b1 = min(a.nb, (u % a.ksplit) * a.kslice + a.kslice);
             const float dw = f16_to_f32(nhd);
+            if (lane < NPASS * SP) S.ys[pw][i & 1][lane] = nys;
+            __syncwarp();
             int nu = u, nbk = b + 1;
             if (nbk >= b1) { nu = u + gridDim.x; nbk = nu < a.units ? (nu % a.ksplit) * a.kslice : 0; }
-            if (nu < a.units) nhd = fetch_d(nu, nbk);
+            if (nu < a.units) { nhd = fetch_d(nu, nbk); nys = fetch_ys(nbk); }
 #pragma unroll
             for (int ps = 0; ps < NPASS; ps++) {
                 const int it = i * NPASS + ps, buf = it & 1;
-                if (lane < SP) S.ys[pw][it & 1][lane] = __ldg(a.yd + (size_t)b * NP + ps * NPP + p * SP + lane);
-                __syncwarp();
                 if (!q6_wait(S, &S.acc_full[buf], (it >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
-                const float *yv = S.ys[pw][it & 1];
+                const float *yv = S.ys[pw][i & 1] + ps * SP;
                 const uint32_t col = tl + buf * CF::acc + p * SP;
 #pragma unroll
                 for (int c = 0; c < SP / 8; c++) {

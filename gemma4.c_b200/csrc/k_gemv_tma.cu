@@ -60,13 +60,8 @@ __device__ __forceinline__ void tm_scales(const uint4 &m, int j, int c, int &sc_
     mn_c = (int)__byte_perm(mn03, mn47, 0x4440 | c) & 0xff;
 }
 
-// Sum over the 8 lanes of this lane's group (lanes 8q..8q+7); exact for ints.
-__device__ __forceinline__ int grp_sum(int v, unsigned mask) {
-    v += __shfl_xor_sync(mask, v, 1);
-    v += __shfl_xor_sync(mask, v, 2);
-    v += __shfl_xor_sync(mask, v, 4);
-    return v;
-}
+// Sum over the 8 lanes of this lane's group (lanes 8q..8q+7, `mask`); exact for ints.
+__device__ __forceinline__ int grp_sum(int v, unsigned mask) { return __reduce_add_sync(mask, v); }
 
 // One super-block k of one row (in shared memory) against NB activations:
 // the 8 lanes of the group each cover 32 weights, their integer partial sums
@@ -166,13 +161,18 @@ __device__ __forceinline__ void tm_block(const uint8_t *row, int nb, int n, int 
 
 // The canonical fold of one row's block terms (RowOrder): terms of block b of
 // sequence s at t[b * NB + s].
+// Segment starts are tracked with counters (the row's unit index modulo the stream-K share, and
+// the block index modulo the K slice) instead of a division per block.
 template <int NB>
 __device__ __forceinline__ float tm_fold(const float2 *t, int nb, int s, const RowOrder &o, int row) {
     float v = 0.0f, P = 0.0f;
+    int us = o.share > 0 ? (int)(((long long)(o.tile0 + row / 128) * nb) % o.share) : 0, ks = 0;
     for (int b = 0; b < nb; b++) {
-        if (seg_start(o, row, nb, b)) { v = __fadd_rn(v, P); P = 0.0f; }
+        if (b > 0 && ((o.share > 0 && us == 0) || (o.kslice > 0 && ks == 0))) { v = __fadd_rn(v, P); P = 0.0f; }
         const float2 ab = t[b * NB + s];
         P = __fmaf_rn(ab.x, ab.y, P);
+        if (o.share > 0 && ++us == o.share) us = 0;
+        if (o.kslice > 0 && ++ks == o.kslice) ks = 0;
     }
     return __fadd_rn(v, P);
 }
