@@ -615,7 +615,7 @@ static int mm_tc(float *o, const void *w, int n, int d, int type, const g4_block
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
         G4_TRY(launch_tc_from_q8(type, (const uint8_t *)q8 + (size_t)g0 * nb * G4_Q8_BYTES, gb, n, np, S->bq, yd, st));
         G4_TRY(launch_gemm_tc(&tm, w, type, n, d, S->bq, yd, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
-                              nullptr, S->nsm, st));
+                              nullptr, S->nsm, st, nullptr));
     }
     return G4_OK;
 }
@@ -632,7 +632,7 @@ static int mm_tc6(float *o, const float *x, const void *w, int n, int d, int bat
         const int gb = batch - g0 < 64 ? batch - g0 : 64, np = tc_np(gb);
         G4_TRY(launch_tc6_split(x + (size_t)g0 * n, n, gb, n, np, S->bq, ys, st));
         G4_TRY(launch_gemm_q6tc(maps, w, n, d, S->bq, ys, gb, np, o + (size_t)g0 * d, d, S->part, S->part_bytes,
-                                nullptr, S->nsm, EPI_STORE, 0.0f, nullptr, st));
+                                nullptr, S->nsm, EPI_STORE, 0.0f, nullptr, st, nullptr));
     }
     return G4_OK;
 }

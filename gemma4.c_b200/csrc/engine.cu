@@ -97,6 +97,7 @@ struct g4_engine {
     uint8_t *tcq = nullptr, *tc6 = nullptr, *tcb = nullptr;  // B operands (Q4_K/Q5_K, Q6_K, BF16)
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
+    int *tc_tickets = nullptr;  // per row tile, zero between launches (in-kernel merge of split tiles)
     int nsm = 0, tc_min_batch = 2;  // measured: the tensor-core step wins from 2 sequences (5.2 vs 9.2 ms)
     std::mutex mu;
 };
@@ -309,12 +310,12 @@ int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float 
             float *ys = (float *)(e->tc6 + tc6_ys_offset(n));
             if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, e->st));
             TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, e->tc_part, e->tc_part_bytes,
-                                 e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st));
+                                 e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st, e->tc_tickets));
         } else {
             float *yd = (float *)(e->tcq + tc_yd_offset(n));
             if (!act_ready) TRY(launch_tc_quant(type, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
             TRY(launch_gemm_tc((const CUtensorMap *)maps, w, type, n, rows, e->tcq, yd, gb, np, o, ldo, e->tc_part,
-                               e->tc_part_bytes, e->d_err, e->nsm, e->st));
+                               e->tc_part_bytes, e->d_err, e->nsm, e->st, e->tc_tickets));
         }
     }
     return G4_OK;
@@ -356,7 +357,7 @@ int tc_gemm_q4_pair(g4_engine *e, const void *w, int rows, float *out, int ldo, 
         if (!act_ready) TRY(launch_tc_quant(G4_Q4_K, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
         TRY(launch_gemm_q4tc2((const CUtensorMap *)m1, w, rows, out + (size_t)g0 * ldo, ldo, (const CUtensorMap *)m2, w2,
                               rows2, out2 ? out2 + (size_t)g0 * ldo2 : nullptr, ldo2, n, e->tcq, yd, gb, np, e->tc_part,
-                              e->tc_part_bytes, e->d_err, e->nsm, e->st, epi));
+                              e->tc_part_bytes, e->d_err, e->nsm, e->st, epi, e->tc_tickets));
     }
     return G4_OK;
 }
@@ -986,6 +987,7 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch, int
         TRY(dalloc_t(e, &e->tcb, bf16tc_operand_bytes((nmax + 63) / 64 * 64)));
         e->tc_part_bytes = std::max(part, (size_t)16);
         TRY(dalloc_t(e, &e->tc_part, e->tc_part_bytes / sizeof(float)));
+        TRY(dalloc_t(e, &e->tc_tickets, (size_t)e->vocab / 128 + 4096));  // zeroed; every launch leaves them zero
     }
     TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
     TRY(dalloc_t(e, &e->d_err, 1));

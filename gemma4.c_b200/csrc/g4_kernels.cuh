@@ -175,7 +175,7 @@ int prime_tc_attrs();
 int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq, float *ys, cudaStream_t st);
 int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
                      int np, float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
-                     int epi, float cap, unsigned long long *keys, cudaStream_t st);
+                     int epi, float cap, unsigned long long *keys, cudaStream_t st, int *tickets);
 
 // ---- batched K-quant GEMM on tcgen05 (k_gemm_tc.cu), 16..64 sequences
 struct TcPlan {
@@ -197,7 +197,7 @@ RowOrder q6_row_order(int rows, int n, int nsm, bool argmax);
 int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
                       const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
                       int np, float *part, size_t part_bytes, int *err, int nsm, cudaStream_t st,
-                      int epi);
+                      int epi, int *tickets);
 int tc_np(int B);                    // padded sequence count: 16, 32 or 64
 size_t tc_operand_bytes(int n);      // B operand + block scales of one activation (NP = 64)
 size_t tc_yd_offset(int n);          // where the block scales start inside that buffer
@@ -210,6 +210,6 @@ int launch_tc_quant(int type, const float *x, int ldx, int B, int n, int np, uin
 int launch_tc_from_q8(int type, const void *q8, int B, int n, int np, uint8_t *bq, float *yd, cudaStream_t st);
 int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
                    float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
-                   cudaStream_t st);
+                   cudaStream_t st, int *tickets);
 
 }  // namespace g4

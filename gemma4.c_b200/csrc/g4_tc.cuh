@@ -34,6 +34,8 @@ struct TcArgs {
     int total;                  // all tiles * nb
     int prow;                   // rows of a partial slice: all tiles * 128
     int all_part;               // 1: every tile goes through the partial slots (merge epilogue)
+    int *tickets;               // per row tile, zero between launches: the last CTA to finish a split
+                                // tile merges its partial slots (null: a separate merge launch)
 };
 
 __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {

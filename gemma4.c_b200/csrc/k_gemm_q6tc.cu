@@ -77,6 +77,7 @@ struct Q6State {
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
+    volatile int ticket;
     float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
 };
 
@@ -103,6 +104,20 @@ __device__ __forceinline__ void q6_planes(uint32_t qb, int sc, uint32_t &h, uint
     const uint32_t u1 = ((qb >> 8) & 0x00FF00FFu) * (uint32_t)sc + C;  // quants 1, 3
     h = __vsub4(((u0 >> 6) & 0x00FF00FFu) | (((u1 >> 6) & 0x00FF00FFu) << 8), 0x40404040u);
     l = (u0 & 0x003F003Fu) | ((u1 & 0x003F003Fu) << 8);
+}
+
+// The K slices of row `row` for this thread's sequences, summed in slice order (0 + P0 + P1 ...).
+// Kept out of line: it runs once per split tile, by the CTA that finishes it last.
+__device__ __noinline__ void q6_merge_rows(const TcArgs &a, int NP, int NPASS, int NPP, int SP, int p, int row) {
+    if (row >= a.rows) return;
+    for (int ps = 0; ps < NPASS; ps++)
+        for (int s = 0; s < SP; s++) {
+            const int seq = ps * NPP + p * SP + s;
+            if (seq >= a.B) continue;
+            float v = 0.0f;
+            for (int k = 0; k < a.ksplit; k++) v = __fadd_rn(v, __ldcg(a.part + ((size_t)k * NP + seq) * a.rows + row));
+            a.out[(size_t)seq * a.ldo + row] = v;
+        }
 }
 
 template <int NP>
@@ -326,6 +341,19 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                     }
                     P[ps][s] = 0.0f;
                 }
+            if (a.ksplit > 1 && a.tickets) {
+                // the last CTA to finish a K slice of this row tile sums the slices in order (0 + P0 + P1 ...)
+                const int rt = u / a.ksplit;
+                __threadfence();
+                asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
+                if (warp == 10 && lane == 0) S.ticket = atomicAdd(a.tickets + rt, 1);
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (S.ticket == a.ksplit - 1) {
+                    __threadfence();
+                    q6_merge_rows(a, NP, NPASS, NPP, SP, p, row);
+                    if (warp == 10 && lane == 0) a.tickets[rt] = 0;  // ready for the next launch
+                }
+            }
         };
         int u = blockIdx.x, b = u < a.units ? (u % a.ksplit) * a.kslice : 0;
         // d of row r for the block (fp16 after the quant planes of the row), loaded one block ahead
@@ -466,7 +494,7 @@ int launch_tc6_split(const float *x, int ldx, int B, int n, int np, uint8_t *bq,
 
 int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uint8_t *bq, const float *ys, int B,
                      int np, float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
-                     int epi, float cap, unsigned long long *keys, cudaStream_t st) {
+                     int epi, float cap, unsigned long long *keys, cudaStream_t st, int *tickets) {
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "q6 tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     if (epi != EPI_STORE && epi != EPI_SOFTCAP_ARGMAX) { set_error(G4_ERR_ARG, "q6 tc gemm: epilogue %d", epi); return G4_ERR_ARG; }
     if (epi == EPI_SOFTCAP_ARGMAX && !keys) { set_error(G4_ERR_ARG, "q6 tc gemm: argmax keys missing"); return G4_ERR_ARG; }
@@ -482,6 +510,7 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
     }
     TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q6_K, n), bq, ys, out, part, err, nb, rows, B, ldo,
              p.ksplit, p.kslice, p.units, epi, cap, keys};
+    a.tickets = tickets;
 #define G4_Q6TC_CASE(N)                                                                             \
     if (np == N) {                                                                                   \
         const size_t smem = Q6Cfg<N>::total;                                                         \
@@ -490,7 +519,7 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
     G4_Q6TC_CASE(16) else G4_Q6TC_CASE(32) else G4_Q6TC_CASE(64)
 #undef G4_Q6TC_CASE
     G4_LAUNCHED();
-    if (p.ksplit > 1) return launch_tc_merge(part, p.ksplit, np, rows, B, out, ldo, EPI_STORE, nullptr, 0, st);
+    if (p.ksplit > 1 && !tickets) return launch_tc_merge(part, p.ksplit, np, rows, B, out, ldo, EPI_STORE, nullptr, 0, st);
     return G4_OK;
 }
 

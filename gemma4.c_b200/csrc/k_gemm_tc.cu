@@ -480,6 +480,7 @@ struct Q4State {
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
+    volatile int ticket;
     float yd[8][2][32];  // per epilogue warp: block scales of its sequences, by block parity
 };
 
@@ -498,6 +499,38 @@ __device__ __forceinline__ void q4_fail(Q4State &S, int *err) {
     S.abort = 1;
     if (err) atomicExch(err, G4_ERR_TIMEOUT);
 }
+// Merge of a split row tile t (this thread: row r of the tile, sequences p*SP ..) from its partial
+// slots, summed in slot order (0 + P0 + P1 ...), then stored; for a gate/up pair (a.all_part) the
+// gate tile tg and its up tile give GELU(gate) * up (main.c:1973-1978).  Kept out of line: it runs
+// once per split tile, by the CTA that finishes it last.
+__device__ __noinline__ void q4_merge_tile(const TcArgs &a, int NP, int SP, int p, int r, int t, int tg) {
+    const size_t prow = (size_t)a.prow;
+    auto sum = [&](int tt, int seq) {
+        const int ns = ((tt + 1) * a.nb - 1) / a.share - (tt * a.nb) / a.share + 1;
+        float v = 0.0f;
+        for (int k = 0; k < ns; k++) v = __fadd_rn(v, __ldcg(a.part + ((size_t)k * NP + seq) * prow + (size_t)tt * 128 + r));
+        return v;
+    };
+    if (a.all_part) {
+        const int rw = tg * 128 + r;
+        if (rw < a.rows)
+            for (int s = 0; s < SP; s++) {
+                const int seq = p * SP + s;
+                if (seq < a.B) a.out[(size_t)seq * a.ldo + rw] = gelu_f32(sum(tg, seq)) * sum(a.tiles0 + tg, seq);
+            }
+        return;
+    }
+    const bool m2 = t >= a.tiles0;
+    const int row = (m2 ? t - a.tiles0 : t) * 128 + r;
+    if (row >= (m2 ? a.rows2 : a.rows)) return;
+    float *dst = (m2 ? a.out2 : a.out) + row;
+    const size_t ld = m2 ? (size_t)a.ldo2 : (size_t)a.ldo;
+    for (int s = 0; s < SP; s++) {
+        const int seq = p * SP + s;
+        if (seq < a.B) dst[(size_t)seq * ld] = sum(t, seq);
+    }
+}
+
 // Warp roles.  Warps 2..17 work on TMEM lane quadrant (warp & 3), i.e. 32
 // weight rows each (a warp may only touch its own quadrant):
 //   warps 2..9   expand: warp-group e = (warp-2)/4 expands the quarters 2e
@@ -752,6 +785,23 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                     mine[(size_t)(2 * s) * prow] = f.x;
                     mine[(size_t)(2 * s + 1) * prow] = f.y;
                 }
+                if (a.tickets) {
+                    // The last CTA to finish this tile (for a gate/up pair: both tiles of the pair) sums
+                    // the partial slots in slot order, 0 + P0 + P1 + ... (the canonical row order).
+                    const int tg = m2 ? t - a.tiles0 : t;  // gate (first-matrix) tile of a pair
+                    auto nseg_of = [&](int tt) { return ((tt + 1) * a.nb - 1) / a.share - (tt * a.nb) / a.share + 1; };
+                    const int tk = a.all_part ? tg : t;
+                    const int expect = a.all_part ? nseg_of(tg) + nseg_of(a.tiles0 + tg) : nseg;
+                    __threadfence();
+                    asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
+                    if (warp == 10 && lane == 0) S.ticket = atomicAdd(a.tickets + tk, 1);
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
+                    if (S.ticket == expect - 1) {
+                        __threadfence();
+                        q4_merge_tile(a, NP, SP, p, r, t, tg);
+                        if (warp == 10 && lane == 0) a.tickets[tk] = 0;  // ready for the next launch
+                    }
+                }
             }
 #pragma unroll
             for (int s = 0; s < SP / 2; s++) acc[s] = 0ull;
@@ -997,7 +1047,7 @@ __global__ void sk_merge_kernel(const float *__restrict__ part, int prow, int NP
 int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out, int ldo, const CUtensorMap *tm2,
                       const void *w2, int rows2, float *out2, int ldo2, int n, const uint8_t *bq, const float *yd, int B,
                       int np, float *part, size_t part_bytes, int *err, int nsm, cudaStream_t st,
-                      int epi) {
+                      int epi, int *tickets) {
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     if (epi != EPI_STORE && !(epi == EPI_GELU_MUL && w2 && rows2 == rows)) {
         set_error(G4_ERR_ARG, "tc gemm: epilogue %d needs a gate/up pair of equal shape", epi);
@@ -1014,6 +1064,7 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
              1, nb, tiles, EPI_STORE, 0.0f, nullptr};
     a.w2 = (const uint8_t *)w2; a.out2 = out2; a.rows2 = rows2; a.ldo2 = ldo2; a.tiles0 = w2 ? tiles0 : tiles;
     a.share = p.share; a.total = tiles * nb; a.prow = tiles * 128; a.all_part = all_part ? 1 : 0;
+    a.tickets = tickets;
     const CUtensorMap *m2 = w2 ? tm2 : tm;
 #define G4_Q4TC_CASE(N)                                                                                  \
     if (np == N)                                                                                           \
@@ -1022,7 +1073,7 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
     G4_Q4TC_CASE(16) else G4_Q4TC_CASE(32) else G4_Q4TC_CASE(64)
 #undef G4_Q4TC_CASE
     G4_LAUNCHED();
-    if (!merge) return G4_OK;
+    if (!merge || tickets) return G4_OK;  // with tickets the kernel merges split tiles itself
     const int mrows = all_part ? tiles0 * 128 : tiles * 128;
     G4_CUDA(launch_pdl(sk_merge_kernel, dim3((unsigned)(mrows / 128), (unsigned)B), dim3(128), 0, st, (const float *)part,
                        tiles * 128, np, nb, p.share, a.tiles0, rows, out, ldo, rows2, out2, ldo2, B, epi, a.all_part));
@@ -1032,11 +1083,11 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
 
 int launch_gemm_tc(const CUtensorMap *tm, const void *w, int type, int n, int rows, const uint8_t *bq, const float *yd, int B, int np,
                    float *out, int ldo, float *part, size_t part_bytes, int *err, int nsm,
-                   cudaStream_t st) {
+                   cudaStream_t st, int *tickets) {
     if (type != G4_Q4_K && type != G4_Q5_K) { set_error(G4_ERR_TYPE, "tc gemm: type %d", type); return G4_ERR_TYPE; }
     if (type == G4_Q4_K)
         return launch_gemm_q4tc2(tm, w, rows, out, ldo, nullptr, nullptr, 0, nullptr, 0, n, bq, yd, B, np, part, part_bytes,
-                                 err, nsm, st, EPI_STORE);
+                                 err, nsm, st, EPI_STORE, tickets);
     if (B < 1 || B > np || (np != 16 && np != 32 && np != 64)) { set_error(G4_ERR_ARG, "tc gemm: batch %d / %d", B, np); return G4_ERR_ARG; }
     const int nb = n / G4_QK;
     const TcPlan p = tc_plan(rows, nb, nsm);

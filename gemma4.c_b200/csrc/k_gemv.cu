@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restri
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
                       int B, int epi, const float *evec, int ld_evec, cudaStream_t st, const Prologue *pro,
                       int pro_writer) {
-    if (!pro && B > 8 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
+    if (!pro && B > 1 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
         const size_t per = (size_t)n * 4;
         // two CTAs per SM (<= 100 KB of staged activations each), about one wave in total
         const int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : 0;

@@ -61,7 +61,12 @@ __device__ __forceinline__ void tm_scales(const uint4 &m, int j, int c, int &sc_
 }
 
 // Sum over the 8 lanes of this lane's group (lanes 8q..8q+7, `mask`); exact for ints.
-__device__ __forceinline__ int grp_sum(int v, unsigned mask) { return __reduce_add_sync(mask, v); }
+__device__ __forceinline__ int grp_sum(int v, unsigned mask) {
+    v += __shfl_xor_sync(mask, v, 1);
+    v += __shfl_xor_sync(mask, v, 2);
+    v += __shfl_xor_sync(mask, v, 4);
+    return v;
+}
 
 // One super-block k of one row (in shared memory) against NB activations:
 // the 8 lanes of the group each cover 32 weights, their integer partial sums
