@@ -78,7 +78,7 @@ struct Q6State {
     uint32_t tmem_base;
     volatile int abort;
     volatile int ticket;
-    float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
+    alignas(16) float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
 };
 
 __device__ __forceinline__ bool q6_wait(Q6State &S, uint64_t *bar, uint32_t parity) {

@@ -481,7 +481,7 @@ struct Q4State {
     uint32_t tmem_base;
     volatile int abort;
     volatile int ticket;
-    float yd[8][2][32];  // per epilogue warp: block scales of its sequences, by block parity
+    alignas(16) float yd[8][2][32];  // per epilogue warp (read as float2): block scales of its sequences, by block parity
 };
 
 // Waiting warps sleep in the barrier (1 ms suspend hint) instead of
