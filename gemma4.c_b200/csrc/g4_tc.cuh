@@ -11,6 +11,9 @@
 
 namespace g4 {
 
+// Split row tiles one CTA of a tensor-core GEMM may have to merge after its units.
+constexpr int kTcMergeCap = 16;
+
 struct TcArgs {
     const uint8_t *w;   // weight rows (device layout), row_bytes apart
     size_t row_bytes;
@@ -149,6 +152,32 @@ __device__ __forceinline__ void bf3_store_group(uint8_t *bq, int g, int NP, int 
     for (int q = 0; q < 3; q++)
         *reinterpret_cast<uint32_t *>(blk + (k >> 3) * (3 * NP * 16) + (q * NP + s) * 16 + (k & 7) * 2) =
             (uint32_t)p0[q] | ((uint32_t)p1[q] << 16);
+}
+
+// Merge of split partials for G consecutive sequences of one output element:
+// v[s] = ((0 + P_0) + P_1) + ... + P_{ns-1}, slot k of sequence s at
+// p0[k * slot_stride + s * seq_stride].  The loads of a batch of slots are all
+// issued before the adds (the partials sit in L2), so a merge costs about one
+// L2 round trip per batch instead of one per slot and sequence; the additions
+// keep the slot order.
+template <int G>
+__device__ __forceinline__ void slot_sums(const float *p0, size_t slot_stride, size_t seq_stride, int ns, float (&v)[G]) {
+    constexpr int KU = G >= 16 ? 1 : 16 / G;  // slots per batch: 16 loads in flight
+#pragma unroll
+    for (int s = 0; s < G; s++) v[s] = 0.0f;
+    for (int k0 = 0; k0 < ns; k0 += KU) {
+        float t[KU][G];
+#pragma unroll
+        for (int u = 0; u < KU; u++)
+            if (k0 + u < ns)
+#pragma unroll
+                for (int s = 0; s < G; s++) t[u][s] = __ldcg(p0 + (size_t)(k0 + u) * slot_stride + (size_t)s * seq_stride);
+#pragma unroll
+        for (int u = 0; u < KU; u++)
+            if (k0 + u < ns)
+#pragma unroll
+                for (int s = 0; s < G; s++) v[s] = __fadd_rn(v[s], t[u][s]);
+    }
 }
 
 }  // namespace g4

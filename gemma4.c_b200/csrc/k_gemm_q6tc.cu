@@ -77,7 +77,8 @@ struct Q6State {
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
-    volatile int ticket;
+    int mcount;               // row tiles this CTA finished last (merged after its units)
+    int mlist[kTcMergeCap];
     alignas(16) float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
 };
 
@@ -107,17 +108,19 @@ __device__ __forceinline__ void q6_planes(uint32_t qb, int sc, uint32_t &h, uint
 }
 
 // The K slices of row `row` for this thread's sequences, summed in slice order (0 + P0 + P1 ...).
-// Kept out of line: it runs once per split tile, by the CTA that finishes it last.
-__device__ __noinline__ void q6_merge_rows(const TcArgs &a, int NP, int NPASS, int NPP, int SP, int p, int row) {
+template <int SP>
+__device__ __forceinline__ void q6_merge_rows(const TcArgs &a, int NP, int NPASS, int NPP, int p, int row) {
     if (row >= a.rows) return;
-    for (int ps = 0; ps < NPASS; ps++)
-        for (int s = 0; s < SP; s++) {
-            const int seq = ps * NPP + p * SP + s;
-            if (seq >= a.B) continue;
-            float v = 0.0f;
-            for (int k = 0; k < a.ksplit; k++) v = __fadd_rn(v, __ldcg(a.part + ((size_t)k * NP + seq) * a.rows + row));
-            a.out[(size_t)seq * a.ldo + row] = v;
-        }
+    const size_t rows = (size_t)a.rows;
+    for (int ps = 0; ps < NPASS; ps++) {
+        const int s0 = ps * NPP + p * SP;
+        if (s0 >= a.B) break;
+        float v[SP];
+        slot_sums<SP>(a.part + (size_t)s0 * rows + row, (size_t)NP * rows, rows, a.ksplit, v);
+#pragma unroll
+        for (int s = 0; s < SP; s++)
+            if (s0 + s < a.B) a.out[(size_t)(s0 + s) * a.ldo + row] = v[s];
+    }
 }
 
 template <int NP>
@@ -151,6 +154,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
         mbar_init(&S.mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort = 0;
+        S.mcount = 0;
     }
     if (warp == 1) tc_alloc(&S.tmem_base, 512);
     tc_fence_before();
@@ -342,16 +346,15 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                     P[ps][s] = 0.0f;
                 }
             if (a.ksplit > 1 && a.tickets) {
-                // the last CTA to finish a K slice of this row tile sums the slices in order (0 + P0 + P1 ...)
-                const int rt = u / a.ksplit;
+                // Count this slice in; the CTA that completes the row tile merges it after its units.
                 __threadfence();
                 asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
-                if (warp == 10 && lane == 0) S.ticket = atomicAdd(a.tickets + rt, 1);
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                if (S.ticket == a.ksplit - 1) {
-                    __threadfence();
-                    q6_merge_rows(a, NP, NPASS, NPP, SP, p, row);
-                    if (warp == 10 && lane == 0) a.tickets[rt] = 0;  // ready for the next launch
+                if (warp == 10 && lane == 0) {
+                    const int rt = u / a.ksplit;
+                    if (atomicAdd(a.tickets + rt, 1) == a.ksplit - 1) {
+                        if (S.mcount < kTcMergeCap) S.mlist[S.mcount++] = rt;
+                        else if (a.err) atomicExch(a.err, G4_ERR_STATE);
+                    }
                 }
             }
         };
@@ -412,7 +415,15 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
             if (nu != u) finish(u);
             u = nu; b = nbk; i++;
         }
-        if (!ok) q6_fail(S, a.err);
+        if (!ok) {
+            q6_fail(S, a.err);
+        } else if (a.ksplit > 1 && a.tickets) {
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // S.mlist complete
+            const int nm = S.mcount;
+            if (nm) __threadfence();
+            for (int m = 0; m < nm; m++) q6_merge_rows<SP>(a, NP, NPASS, NPP, p, S.mlist[m] * 128 + r);
+            if (warp == 10 && lane < nm) a.tickets[S.mlist[lane]] = 0;  // ready for the next launch
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -508,6 +519,8 @@ int launch_gemm_q6tc(const void *maps, const void *w, int n, int rows, const uin
         set_error(G4_ERR_ARG, "q6 tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
+    // in-kernel merges: a CTA keeps at most kTcMergeCap row tiles to merge (one per unit it runs)
+    if (tickets && (p.units + p.grid - 1) / p.grid > kTcMergeCap) tickets = nullptr;
     TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q6_K, n), bq, ys, out, part, err, nb, rows, B, ldo,
              p.ksplit, p.kslice, p.units, epi, cap, keys};
     a.tickets = tickets;

@@ -480,7 +480,8 @@ struct Q4State {
     uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
     volatile int abort;
-    volatile int ticket;
+    int mcount;               // split row tiles this CTA finished last (merged after its units)
+    int mlist[kTcMergeCap];
     alignas(16) float yd[8][2][32];  // per epilogue warp (read as float2): block scales of its sequences, by block parity
 };
 
@@ -503,21 +504,24 @@ __device__ __forceinline__ void q4_fail(Q4State &S, int *err) {
 // slots, summed in slot order (0 + P0 + P1 ...), then stored; for a gate/up pair (a.all_part) the
 // gate tile tg and its up tile give GELU(gate) * up (main.c:1973-1978).  Kept out of line: it runs
 // once per split tile, by the CTA that finishes it last.
-__device__ __noinline__ void q4_merge_tile(const TcArgs &a, int NP, int SP, int p, int r, int t, int tg) {
+template <int G>
+__device__ __forceinline__ void q4_merge_tile(const TcArgs &a, int NP, int SP, int p, int r, int t, int tg) {
     const size_t prow = (size_t)a.prow;
-    auto sum = [&](int tt, int seq) {
+    auto sums = [&](int tt, int s0, float (&v)[G]) {
         const int ns = ((tt + 1) * a.nb - 1) / a.share - (tt * a.nb) / a.share + 1;
-        float v = 0.0f;
-        for (int k = 0; k < ns; k++) v = __fadd_rn(v, __ldcg(a.part + ((size_t)k * NP + seq) * prow + (size_t)tt * 128 + r));
-        return v;
+        slot_sums<G>(a.part + (size_t)s0 * prow + (size_t)tt * 128 + r, (size_t)NP * prow, prow, ns, v);
     };
     if (a.all_part) {
         const int rw = tg * 128 + r;
-        if (rw < a.rows)
-            for (int s = 0; s < SP; s++) {
-                const int seq = p * SP + s;
-                if (seq < a.B) a.out[(size_t)seq * a.ldo + rw] = gelu_f32(sum(tg, seq)) * sum(a.tiles0 + tg, seq);
-            }
+        if (rw >= a.rows) return;
+        for (int s0 = p * SP; s0 < p * SP + SP && s0 < a.B; s0 += G) {
+            float g[G], u[G];
+            sums(tg, s0, g);
+            sums(a.tiles0 + tg, s0, u);
+#pragma unroll
+            for (int s = 0; s < G; s++)
+                if (s0 + s < a.B) a.out[(size_t)(s0 + s) * a.ldo + rw] = gelu_f32(g[s]) * u[s];
+        }
         return;
     }
     const bool m2 = t >= a.tiles0;
@@ -525,9 +529,12 @@ __device__ __noinline__ void q4_merge_tile(const TcArgs &a, int NP, int SP, int 
     if (row >= (m2 ? a.rows2 : a.rows)) return;
     float *dst = (m2 ? a.out2 : a.out) + row;
     const size_t ld = m2 ? (size_t)a.ldo2 : (size_t)a.ldo;
-    for (int s = 0; s < SP; s++) {
-        const int seq = p * SP + s;
-        if (seq < a.B) dst[(size_t)seq * ld] = sum(t, seq);
+    for (int s0 = p * SP; s0 < p * SP + SP && s0 < a.B; s0 += G) {
+        float v[G];
+        sums(t, s0, v);
+#pragma unroll
+        for (int s = 0; s < G; s++)
+            if (s0 + s < a.B) dst[(size_t)(s0 + s) * ld] = v[s];
     }
 }
 
@@ -571,6 +578,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         mbar_init(&S.mma_done, 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort = 0;
+        S.mcount = 0;
     }
     if (warp == 1) tc_alloc(&S.tmem_base, 512);
     tc_fence_before();
@@ -786,20 +794,19 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
                     mine[(size_t)(2 * s + 1) * prow] = f.y;
                 }
                 if (a.tickets) {
-                    // The last CTA to finish this tile (for a gate/up pair: both tiles of the pair) sums
-                    // the partial slots in slot order, 0 + P0 + P1 + ... (the canonical row order).
-                    const int tg = m2 ? t - a.tiles0 : t;  // gate (first-matrix) tile of a pair
-                    auto nseg_of = [&](int tt) { return ((tt + 1) * a.nb - 1) / a.share - (tt * a.nb) / a.share + 1; };
-                    const int tk = a.all_part ? tg : t;
-                    const int expect = a.all_part ? nseg_of(tg) + nseg_of(a.tiles0 + tg) : nseg;
+                    // Count this CTA's part in; the CTA that completes the tile (for a gate/up pair: both
+                    // tiles of the pair) merges it after its units, in slot order 0 + P0 + P1 + ...
                     __threadfence();
                     asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
-                    if (warp == 10 && lane == 0) S.ticket = atomicAdd(a.tickets + tk, 1);
-                    asm volatile("bar.sync 1, 256;" ::: "memory");
-                    if (S.ticket == expect - 1) {
-                        __threadfence();
-                        q4_merge_tile(a, NP, SP, p, r, t, tg);
-                        if (warp == 10 && lane == 0) a.tickets[tk] = 0;  // ready for the next launch
+                    if (warp == 10 && lane == 0) {
+                        auto nseg_of = [&](int tt) { return ((tt + 1) * a.nb - 1) / a.share - (tt * a.nb) / a.share + 1; };
+                        const int tg = m2 ? t - a.tiles0 : t;
+                        const int tk = a.all_part ? tg : t;
+                        const int expect = a.all_part ? nseg_of(tg) + nseg_of(a.tiles0 + tg) : nseg;
+                        if (atomicAdd(a.tickets + tk, 1) == expect - 1) {
+                            if (S.mcount < kTcMergeCap) S.mlist[S.mcount++] = t;
+                            else if (a.err) atomicExch(a.err, G4_ERR_STATE);
+                        }
                     }
                 }
             }
@@ -844,7 +851,21 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
             }
             if (g + 1 == g1 || (g + 1) % a.nb == 0) finish(g / a.nb);
         }
-        if (!ok) q4_fail(S, a.err);
+        if (!ok) {
+            q4_fail(S, a.err);
+        } else if (a.tickets) {
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // S.mlist complete
+            const int nm = S.mcount;
+            if (nm) __threadfence();
+            for (int m = 0; m < nm; m++) {
+                const int t = S.mlist[m];
+                q4_merge_tile<(SP < 16 ? SP : 16)>(a, NP, SP, p, r, t, t >= a.tiles0 ? t - a.tiles0 : t);
+            }
+            if (warp == 10 && lane < nm) {  // ready for the next launch
+                const int t = S.mlist[lane];
+                a.tickets[a.all_part ? (t >= a.tiles0 ? t - a.tiles0 : t) : t] = 0;
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -1060,6 +1081,9 @@ int launch_gemm_q4tc2(const CUtensorMap *tm, const void *w, int rows, float *out
         set_error(G4_ERR_ARG, "tc gemm: partial buffer too small");
         return G4_ERR_ARG;
     }
+    // in-kernel merges: a CTA keeps at most kTcMergeCap tiles to merge (its first and last tile, or
+    // for a gate/up pair every tile it touches)
+    if (tickets && all_part && (p.share + nb - 1) / nb + 1 > kTcMergeCap) tickets = nullptr;
     TcArgs a{(const uint8_t *)w, device_row_bytes(G4_Q4_K, n), bq, yd, out, part, err, nb, rows, B, ldo,
              1, nb, tiles, EPI_STORE, 0.0f, nullptr};
     a.w2 = (const uint8_t *)w2; a.out2 = out2; a.rows2 = rows2; a.ldo2 = ldo2; a.tiles0 = w2 ? tiles0 : tiles;

@@ -228,16 +228,22 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
     if (!pro && B > 1 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
         const size_t per = (size_t)n * 4;
         // two CTAs per SM (<= 100 KB of staged activations each), about one wave in total
-        const int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : 0;
+        int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : per * 2 <= 100 * 1024 ? 2 : 0;
         if (NS) {
             // short rows: one row per warp (staging the activations is cheap); long rows: about two
-            // waves of CTAs that each stage once and loop over rows
-            const int gy = (B + NS - 1) / NS;
-            const int gx = n <= 1024 ? (rows + 7) / 8 : std::max(1, std::min((rows + 7) / 8, 296 / gy));
-            const dim3 grid(gx, gy);
-            if (NS == 16) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<16>, grid, dim3(256), per * 16, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
-            else if (NS == 8) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<8>, grid, dim3(256), per * 8, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
-            else G4_CUDA(launch_pdl(gemv_dense_ms_kernel<4>, grid, dim3(256), per * 4, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            // waves of CTAs that each stage once and loop over rows.  A matrix of few rows gets
+            // fewer sequences per CTA, so that about 128 CTAs share the weight stream.
+            auto grid_of = [&](int ns) {
+                const int gy = (B + ns - 1) / ns;
+                const int gx = n <= 1024 ? (rows + 7) / 8 : std::max(1, std::min((rows + 7) / 8, 296 / gy));
+                return dim3(gx, gy);
+            };
+            while (NS > 2 && NS / 2 >= B) NS /= 2;
+            while (NS > 2 && grid_of(NS).x * grid_of(NS).y < 128 && grid_of(NS / 2).y > grid_of(NS).y) NS /= 2;
+            const dim3 grid = grid_of(NS);
+            if (NS == 8) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<8>, grid, dim3(256), per * 8, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            else if (NS == 4) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<4>, grid, dim3(256), per * 4, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            else G4_CUDA(launch_pdl(gemv_dense_ms_kernel<2>, grid, dim3(256), per * 2, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
             G4_LAUNCHED();
             return G4_OK;
         }
@@ -323,9 +329,9 @@ namespace g4 {
 int prime_gemv_ks_attrs();
 int prime_gemv_attrs() {
     G4_CUDA(cudaFuncSetAttribute(gemv_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return prime_gemv_ks_attrs();
 }
 }  // namespace g4

@@ -31,7 +31,121 @@ __device__ __forceinline__ float cta_sum(float v, float *red) {
     return t;
 }
 
-// rmsnorm (main.c:1451-1456): o = (x * (1/sqrt(mean(x^2) + eps))) * w
+// The tensor-core B operands (and Q8_K blocks) of the finished vector src[dim] of sequence b.
+__device__ __forceinline__ void resnorm_operands(const ResNorm &r, const float *src, int b, bool q8) {
+    const int nb = r.dim / G4_QK, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (q8) {
+        uint8_t *q8o = (uint8_t *)r.q8_out + (size_t)b * nb * G4_Q8_BYTES;
+        for (int k = warp; k < nb; k += nw) {
+            uint32_t q[2];
+            float d;
+            int ls;
+            warp_quant_block(src + k * G4_QK, lane, q, d, ls);
+            store_q8_block(q8o + (size_t)k * G4_Q8_BYTES, lane, q, d, ls);
+        }
+    }
+    if (r.tc4_bq)
+        for (int k = warp; k < nb; k += nw) {
+            uint32_t q[2];
+            float d;
+            int ls;
+            warp_quant_block(src + k * G4_QK, lane, q, d, ls);
+            tc4_store_q8(r.tc4_bq + (size_t)k * 544 * r.tc_np, r.tc4_yd + (size_t)k * r.tc_np, r.tc_np, b, lane, q, d, ls);
+        }
+    if (r.tc6_bq)
+        for (int k = warp; k < nb; k += nw) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = src[k * G4_QK + 8 * lane + j];
+            tc6_store_block(r.tc6_bq, r.tc6_ys, k, r.tc_np, b, lane, v, true);
+        }
+    if (r.bf3_bq)
+        for (int g = warp; g < r.dim / kBfK; g += nw)
+            bf3_store_group(r.bf3_bq, g, r.tc_np, b, lane, src[g * kBfK + 2 * lane], src[g * kBfK + 2 * lane + 1]);
+}
+
+// rmsnorm (main.c:1451-1456): o = (x * (1/sqrt(mean(x^2) + eps))) * w.
+// 256 threads, one CTA per sequence; thread t owns elements t + 256k in
+// registers, which is the element order of canon_sumsq, so the sums are those
+// of the fused GEMV prologue.  The norm weights are loaded before the wait on
+// the previous kernel and the residual inputs right after it, so the kernel
+// makes one dependent trip to memory before its stores.
+template <int NBM>
+__global__ void __launch_bounds__(256) resnorm_reg_kernel(ResNorm r) {
+    extern __shared__ __align__(16) float xs[];  // [dim] the finished vector (xn, or x without pre_w)
+    __shared__ float red[8];
+    pdl_trigger();
+    const int b = blockIdx.x, dim = r.dim, t = threadIdx.x, nb = dim / G4_QK;
+    float pw[NBM], qw[NBM], x[NBM], d[NBM];
+#pragma unroll
+    for (int k = 0; k < NBM; k++)
+        if (k < nb) {
+            pw[k] = r.delta ? __ldg(r.post_w + t + G4_QK * k) : 0.0f;
+            qw[k] = r.pre_w ? __ldg(r.pre_w + t + G4_QK * k) : 0.0f;
+        }
+    pdl_wait();
+    const float *xi = r.x_in + (size_t)b * dim;
+    const float *dl = r.delta ? r.delta + (size_t)b * dim : nullptr;
+#pragma unroll
+    for (int k = 0; k < NBM; k++)
+        if (k < nb) {
+            x[k] = xi[t + G4_QK * k];
+            d[k] = dl ? dl[t + G4_QK * k] : 0.0f;
+        }
+    auto tree = [&](float p) {  // canon_sumsq's reduction of the 256 per-thread chains
+        p = warp_sum(p);
+        __syncthreads();
+        if ((t & 31) == 0) red[t >> 5] = p;
+        __syncthreads();
+        return ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
+    };
+    if (dl) {
+        float p = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) p = fmaf(d[k], d[k], p);
+        const float ss = tree(p);
+        const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) x[k] = __fadd_rn(x[k], __fmul_rn(__fmul_rn(d[k], inv), pw[k]));
+    }
+    if (r.scale) {
+        const float sc = *r.scale;
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) x[k] = __fmul_rn(x[k], sc);
+    }
+    if (r.x_out) {
+        float *xo = r.x_out + (size_t)b * dim;
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) xo[t + G4_QK * k] = x[k];
+    }
+    if (r.pre_w) {
+        float p = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) p = fmaf(x[k], x[k], p);
+        const float ss = tree(p);
+        const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (k < nb) {
+                x[k] = __fmul_rn(__fmul_rn(x[k], inv), qw[k]);
+                if (r.xn_out) r.xn_out[(size_t)b * dim + t + G4_QK * k] = x[k];
+            }
+    }
+    const bool q8 = r.pre_w && r.q8_out;
+    if (!q8 && !r.tc4_bq && !r.tc6_bq && !r.bf3_bq) return;
+#pragma unroll
+    for (int k = 0; k < NBM; k++)
+        if (k < nb) xs[t + G4_QK * k] = x[k];
+    __syncthreads();
+    resnorm_operands(r, xs, b, q8);
+}
+
+// The same for any dim (the vector staged in shared memory), 512 threads.
 __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
     extern __shared__ __align__(16) float xs[];  // [dim] x, then [dim] xn
     __shared__ float red[32];
@@ -50,14 +164,13 @@ __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
     }
     if (r.scale) {
         const float sc = *r.scale;
-        for (int i = tid; i < dim; i += blockDim.x) xs[i] = xs[i] * sc;
+        for (int i = tid; i < dim; i += blockDim.x) xs[i] = __fmul_rn(xs[i], sc);
     }
     __syncthreads();
     if (r.x_out) {
         float *xo = r.x_out + (size_t)b * dim;
         for (int i = tid; i < dim; i += blockDim.x) xo[i] = xs[i];
     }
-    const int nb = dim / G4_QK, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     if (r.pre_w) {
         const float ss = canon_sumsq(xs, dim, red);
         const float inv = 1.0f / sqrtf(ss / (float)dim + r.eps);
@@ -66,40 +179,11 @@ __global__ void __launch_bounds__(512) resnorm_kernel(ResNorm r) {
             xn[i] = v;
             if (r.xn_out) r.xn_out[(size_t)b * dim + i] = v;
         }
-        if (r.q8_out) {
-            __syncthreads();
-            uint8_t *q8 = (uint8_t *)r.q8_out + (size_t)b * nb * G4_Q8_BYTES;
-            for (int k = warp; k < nb; k += nw) {
-                uint32_t q[2];
-                float d;
-                int ls;
-                warp_quant_block(xn + k * G4_QK, lane, q, d, ls);
-                store_q8_block(q8 + (size_t)k * G4_Q8_BYTES, lane, q, d, ls);
-            }
-        }
     }
-    if (!r.tc4_bq && !r.tc6_bq && !r.bf3_bq) return;
-    // tensor-core operands of sequence b (the same per-warp writers as the standalone kernels)
+    const bool q8 = r.pre_w && r.q8_out;
+    if (!q8 && !r.tc4_bq && !r.tc6_bq && !r.bf3_bq) return;
     __syncthreads();
-    const float *src = r.pre_w ? xn : xs;
-    if (r.tc4_bq)
-        for (int k = warp; k < nb; k += nw) {
-            uint32_t q[2];
-            float d;
-            int ls;
-            warp_quant_block(src + k * G4_QK, lane, q, d, ls);
-            tc4_store_q8(r.tc4_bq + (size_t)k * 544 * r.tc_np, r.tc4_yd + (size_t)k * r.tc_np, r.tc_np, b, lane, q, d, ls);
-        }
-    if (r.tc6_bq)
-        for (int k = warp; k < nb; k += nw) {
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = src[k * G4_QK + 8 * lane + j];
-            tc6_store_block(r.tc6_bq, r.tc6_ys, k, r.tc_np, b, lane, v, true);
-        }
-    if (r.bf3_bq)
-        for (int g = warp; g < dim / kBfK; g += nw)
-            bf3_store_group(r.bf3_bq, g, r.tc_np, b, lane, src[g * kBfK + 2 * lane], src[g * kBfK + 2 * lane + 1]);
+    resnorm_operands(r, r.pre_w ? xn : xs, b, q8);
 }
 
 int launch_resnorm(const ResNorm &r, int B, cudaStream_t st) {
@@ -108,6 +192,11 @@ int launch_resnorm(const ResNorm &r, int B, cudaStream_t st) {
     if ((r.tc4_bq || r.tc6_bq || r.bf3_bq) && (B > r.tc_np || (r.tc_np != 16 && r.tc_np != 32 && r.tc_np != 64))) {
         set_error(G4_ERR_ARG, "resnorm: %d sequences in a tensor-core group of %d", B, r.tc_np);
         return G4_ERR_ARG;
+    }
+    if (r.dim % G4_QK == 0 && r.dim <= 16 * G4_QK) {
+        G4_CUDA(launch_pdl(resnorm_reg_kernel<16>, dim3(B), dim3(256), (size_t)r.dim * 4, st, r));
+        G4_LAUNCHED();
+        return G4_OK;
     }
     const size_t smem = (size_t)r.dim * 8;
     if (smem > 100 * 1024) { set_error(G4_ERR_ARG, "resnorm: dim %d too large", r.dim); return G4_ERR_ARG; }
