@@ -42,6 +42,79 @@ __device__ __forceinline__ float canon_sumsq(const float *v, int n, float *red) 
     return ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
 }
 
+// prologue_run for dim = 256 * nb, nb <= NBM: thread t < 256 holds elements
+// t + 256k in registers (the element order of canon_sumsq), so all of a
+// sequence's inputs are loaded in one trip to memory; same operations and
+// rounding as the general loop below.
+template <int NBM>
+__device__ __forceinline__ void prologue_run_reg(const Prologue &P, int B, float *xs_all, bool writer, float *red) {
+    const int dim = P.dim, t = threadIdx.x, nb = dim / 256;
+    const bool own = t < 256;
+    auto tree = [&](float p) {  // canon_sumsq's reduction of the 256 per-thread chains
+        p = warp_sum(p);
+        __syncthreads();
+        if (own && (t & 31) == 0) red[t >> 5] = p;
+        __syncthreads();
+        return ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
+    };
+    for (int s = 0; s < B; s++) {
+        float x[NBM], d[NBM], pw[NBM], qw[NBM];
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (own && k < nb) {
+                const int i = t + 256 * k;
+                x[k] = P.x_in[(size_t)s * dim + i];
+                d[k] = P.delta ? P.delta[(size_t)s * dim + i] : 0.0f;
+                pw[k] = P.delta ? P.post_w[i] : 0.0f;
+                qw[k] = P.pre_w ? P.pre_w[i] : 0.0f;
+            }
+        if (P.delta) {
+            float p = 0.0f;
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) p = fmaf(d[k], d[k], p);
+            const float ss = tree(p);
+            const float inv = 1.0f / sqrtf(ss / (float)dim + P.eps);
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) x[k] = __fadd_rn(x[k], __fmul_rn(__fmul_rn(d[k], inv), pw[k]));
+        }
+        if (P.scale) {
+            const float sc = *P.scale;
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) x[k] = __fmul_rn(x[k], sc);
+        }
+        if (writer && P.x_out)
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) P.x_out[(size_t)s * dim + t + 256 * k] = x[k];
+        if (P.pre_w) {
+            float p = 0.0f;
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) p = fmaf(x[k], x[k], p);
+            const float ss = tree(p);
+            const float inv = 1.0f / sqrtf(ss / (float)dim + P.eps);
+#pragma unroll
+            for (int k = 0; k < NBM; k++)
+                if (own && k < nb) {
+                    x[k] = __fmul_rn(__fmul_rn(x[k], inv), qw[k]);
+                    if (writer && P.xn_out) P.xn_out[(size_t)s * dim + t + 256 * k] = x[k];
+                }
+        }
+#pragma unroll
+        for (int k = 0; k < NBM; k++)
+            if (own && k < nb) xs_all[(size_t)s * dim + t + 256 * k] = x[k];
+    }
+    __syncthreads();
+}
+
+// Whether prologue_run_reg<10> applies (dim <= 2560, whole super-blocks, >= 256 threads).
+__device__ __forceinline__ bool prologue_reg_ok(const Prologue &P) {
+    return P.dim % 256 == 0 && P.dim <= 10 * 256 && blockDim.x >= 256;
+}
+
 // Fills xs[B][dim] (fp32 activation) and, when q8 != null, q8[B][dim/256]
 // BlockQ8_K in shared memory.  Ends with a CTA barrier.
 __device__ __forceinline__ void prologue_run(const Prologue &P, int B, float *xs_all, uint8_t *q8_all, bool writer,
@@ -60,7 +133,7 @@ __device__ __forceinline__ void prologue_run(const Prologue &P, int B, float *xs
         }
         if (P.scale) {
             const float sc = *P.scale;
-            for (int i = tid; i < dim; i += nt) xs[i] = xs[i] * sc;
+            for (int i = tid; i < dim; i += nt) xs[i] = __fmul_rn(xs[i], sc);
         }
         if (P.pre_w) {
             __syncthreads();  // xs complete before the cross-thread sum

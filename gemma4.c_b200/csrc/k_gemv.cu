@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
         if (P.delta) P.delta += (size_t)s * P.dim;
         if (P.x_out) P.x_out += (size_t)s * P.dim;
         if (P.xn_out) P.xn_out += (size_t)s * P.dim;
-        prologue_run(P, 1, xs, nullptr, pro_writer && blockIdx.x == 0, pred);
+        if (prologue_reg_ok(P)) prologue_run_reg<10>(P, 1, xs, pro_writer && blockIdx.x == 0, pred);
+        else prologue_run(P, 1, xs, nullptr, pro_writer && blockIdx.x == 0, pred);
     } else {
         for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[(size_t)s * ldx + i];
         __syncthreads();
@@ -114,12 +115,42 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
     }
 }
 
-// Dense GEMV for many sequences: each weight row is read once per NS
-// sequences (staged in shared memory) instead of once per sequence.  Every
-// accumulator sees exactly the operation order of gemv_dense_kernel, so the
-// result of a sequence does not depend on the batch.
-template <int NS>
-__global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
+static int g_tm_sms_dense = 0;  // SM count, set when the kernels' attributes are primed
+
+// Sum over the 32 lanes of each of the NV = 2^H values v[] with 31 shuffles
+// in all (instead of 5 per value).  Every value goes through the butterfly of
+// warp_sum (lane bit 4 first, then 3, 2, 1, 0), so each total is bitwise that
+// of warp_sum.  Returns the total of value index (lane >> (5 - H)).
+template <int NV>
+__device__ __forceinline__ float warp_sum_many(float (&v)[NV], int lane) {
+    constexpr int H = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
+    static_assert((1 << H) == NV, "NV must be a power of two <= 32");
+#pragma unroll
+    for (int step = 0; step < H; step++) {
+        const int o = 16 >> step, half = NV >> (step + 1);
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int k = 0; k < half; k++) {
+            const float send = up ? v[k] : v[k + half];
+            const float keep = up ? v[k + half] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int o = 16 >> H; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+// Dense GEMV for many sequences: NS sequences' activations are staged in
+// shared memory once per CTA, and each warp works on RW rows at a time, so an
+// activation value read from shared memory serves RW rows and a weight value
+// read from memory serves NS sequences.  The CTAs loop over the rows.  Every
+// accumulator (row, sequence) sees exactly the operation order of
+// gemv_dense_kernel (lane-strided fmaf chain, then the warp_sum butterfly), so
+// the result of a sequence does not depend on the batch.
+template <int NS, int RW>
+__global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                             const float *__restrict__ x, int ldx, int B,
                                                             float *__restrict__ out, int ldo, int epi,
                                                             const float *__restrict__ evec, int ld_evec) {
@@ -149,76 +180,107 @@ __global__ void __launch_bounds__(256) gemv_dense_ms_kernel(const void *__restri
             xs[(size_t)s * n + j] = x[(size_t)(s0 + s) * ldx + j];
         }
     }
+    for (int i = ns * n + threadIdx.x; i < NS * n; i += blockDim.x) xs[i] = 0.0f;  // padding sequences
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // the staged activations serve rows blockIdx.x*8 + warp, stepping over the grid
-    for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < rows; row += gridDim.x * (blockDim.x >> 5)) {
-    float acc[NS];
+    const bool vec = (n % 8) == 0, f32 = type == G4_F32, bf = type == G4_BF16;
+    for (int row0 = (blockIdx.x * (blockDim.x >> 5) + warp) * RW; row0 < rows; row0 += gridDim.x * (blockDim.x >> 5) * RW) {
+        float acc[RW][NS];
 #pragma unroll
-    for (int s = 0; s < NS; s++) acc[s] = 0.0f;
-    const bool vec = (n % 8) == 0;
-    if (type == G4_F32) {
-        const float *r = (const float *)w + (size_t)row * n;
-        if (vec) {
+        for (int r = 0; r < RW; r++)
+#pragma unroll
+            for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
+        int rr[RW];  // rows past the end repeat the last row (computed, not stored)
+#pragma unroll
+        for (int r = 0; r < RW; r++) rr[r] = min(row0 + r, rows - 1);
+        if (f32 && vec) {
             for (int j = lane * 4; j < n; j += 128) {
-                const float4 a = __ldg(reinterpret_cast<const float4 *>(r + j));
+                float4 a[RW];
+#pragma unroll
+                for (int r = 0; r < RW; r++) a[r] = __ldg(reinterpret_cast<const float4 *>((const float *)w + (size_t)rr[r] * n + j));
 #pragma unroll
                 for (int s = 0; s < NS; s++) {
-                    const float *xv = xs + (size_t)s * n + j;
-                    float t = acc[s];
-                    t = fmaf(a.x, xv[0], t); t = fmaf(a.y, xv[1], t); t = fmaf(a.z, xv[2], t); t = fmaf(a.w, xv[3], t);
-                    acc[s] = t;
+                    const float4 xv = *reinterpret_cast<const float4 *>(xs + (size_t)s * n + j);
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        float t = acc[r][s];
+                        t = fmaf(a[r].x, xv.x, t); t = fmaf(a[r].y, xv.y, t); t = fmaf(a[r].z, xv.z, t); t = fmaf(a[r].w, xv.w, t);
+                        acc[r][s] = t;
+                    }
                 }
             }
-        } else {
+        } else if (f32) {
             for (int j = lane; j < n; j += 32) {
-                const float a = __ldg(r + j);
+                float a[RW];
 #pragma unroll
-                for (int s = 0; s < NS; s++) acc[s] = fmaf(a, xs[(size_t)s * n + j], acc[s]);
+                for (int r = 0; r < RW; r++) a[r] = __ldg((const float *)w + (size_t)rr[r] * n + j);
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const float xv = xs[(size_t)s * n + j];
+#pragma unroll
+                    for (int r = 0; r < RW; r++) acc[r][s] = fmaf(a[r], xv, acc[r][s]);
+                }
             }
-        }
-    } else {
-        const uint16_t *r = (const uint16_t *)w + (size_t)row * n;
-        const bool bf = type == G4_BF16;
-        if (vec) {
-#pragma unroll 4
+        } else if (vec) {
+#pragma unroll 2
             for (int j = lane * 8; j < n; j += 256) {
-                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + j));
-                const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
-                float wf[8];
+                float wf[RW][8];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint16_t l = (uint16_t)(ww[i] & 0xffffu), h = (uint16_t)(ww[i] >> 16);
-                    wf[2 * i] = bf ? bf16_to_f32(l) : f16_to_f32(l);
-                    wf[2 * i + 1] = bf ? bf16_to_f32(h) : f16_to_f32(h);
+                for (int r = 0; r < RW; r++) {
+                    const uint4 a = __ldg(reinterpret_cast<const uint4 *>((const uint16_t *)w + (size_t)rr[r] * n + j));
+                    const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const uint16_t l = (uint16_t)(ww[i] & 0xffffu), h = (uint16_t)(ww[i] >> 16);
+                        wf[r][2 * i] = bf ? bf16_to_f32(l) : f16_to_f32(l);
+                        wf[r][2 * i + 1] = bf ? bf16_to_f32(h) : f16_to_f32(h);
+                    }
                 }
 #pragma unroll
                 for (int s = 0; s < NS; s++) {
                     const float4 x0 = *reinterpret_cast<const float4 *>(xs + (size_t)s * n + j);
                     const float4 x1 = *reinterpret_cast<const float4 *>(xs + (size_t)s * n + j + 4);
-                    float t = acc[s];
-                    t = fmaf(x0.x, wf[0], t); t = fmaf(x0.y, wf[1], t); t = fmaf(x0.z, wf[2], t); t = fmaf(x0.w, wf[3], t);
-                    t = fmaf(x1.x, wf[4], t); t = fmaf(x1.y, wf[5], t); t = fmaf(x1.z, wf[6], t); t = fmaf(x1.w, wf[7], t);
-                    acc[s] = t;
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        float t = acc[r][s];
+                        t = fmaf(x0.x, wf[r][0], t); t = fmaf(x0.y, wf[r][1], t); t = fmaf(x0.z, wf[r][2], t); t = fmaf(x0.w, wf[r][3], t);
+                        t = fmaf(x1.x, wf[r][4], t); t = fmaf(x1.y, wf[r][5], t); t = fmaf(x1.z, wf[r][6], t); t = fmaf(x1.w, wf[r][7], t);
+                        acc[r][s] = t;
+                    }
                 }
             }
         } else {
             for (int j = lane; j < n; j += 32) {
-                const uint16_t v = __ldg(r + j);
-                const float wv = bf ? bf16_to_f32(v) : f16_to_f32(v);
+                float wv[RW];
 #pragma unroll
-                for (int s = 0; s < NS; s++) acc[s] = fmaf(xs[(size_t)s * n + j], wv, acc[s]);
+                for (int r = 0; r < RW; r++) {
+                    const uint16_t v = __ldg((const uint16_t *)w + (size_t)rr[r] * n + j);
+                    wv[r] = bf ? bf16_to_f32(v) : f16_to_f32(v);
+                }
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const float xv = xs[(size_t)s * n + j];
+#pragma unroll
+                    for (int r = 0; r < RW; r++) acc[r][s] = fmaf(xv, wv[r], acc[r][s]);
+                }
             }
         }
-    }
+        // totals: value index r * NS + s, one per lane group of 32 / (RW * NS) lanes
+        float flat[RW * NS];
 #pragma unroll
-    for (int s = 0; s < NS; s++) {
-        float a = warp_sum(acc[s]);
-        if (lane == 0 && s < ns) {
-            if (epi == EPI_GELU_SCALE) a = gelu_f32(a) * evec[(size_t)(s0 + s) * ld_evec + row];
-            out[(size_t)(s0 + s) * ldo + row] = a;
+        for (int r = 0; r < RW; r++)
+#pragma unroll
+            for (int s = 0; s < NS; s++) flat[r * NS + s] = acc[r][s];
+        constexpr int NV = RW * NS, LPV = 32 / NV;
+        const float tot = warp_sum_many<NV>(flat, lane);
+        if ((lane & (LPV - 1)) == 0) {
+            const int idx = lane / LPV, r = idx / NS, s = idx % NS, row = row0 + r;
+            if (row < rows && s < ns) {
+                float a = tot;
+                if (epi == EPI_GELU_SCALE) a = gelu_f32(a) * evec[(size_t)(s0 + s) * ld_evec + row];
+                out[(size_t)(s0 + s) * ldo + row] = a;
+            }
         }
-    }
     }
 }
 
@@ -227,23 +289,33 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
                       int pro_writer) {
     if (!pro && B > 1 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
         const size_t per = (size_t)n * 4;
-        // two CTAs per SM (<= 100 KB of staged activations each), about one wave in total
+        // NS sequences per CTA (<= 100 KB of staged activations: two CTAs per SM), RW rows per warp
         int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : per * 2 <= 100 * 1024 ? 2 : 0;
+        while (NS > 2 && NS / 2 >= B) NS /= 2;
         if (NS) {
-            // short rows: one row per warp (staging the activations is cheap); long rows: about two
-            // waves of CTAs that each stage once and loop over rows.  A matrix of few rows gets
-            // fewer sequences per CTA, so that about 128 CTAs share the weight stream.
-            auto grid_of = [&](int ns) {
+            // about two waves of CTAs (two per SM), each staging its sequences once and looping over
+            // rows; a matrix of few rows gets fewer sequences per CTA so that more CTAs share it
+            const int nsm = g_tm_sms_dense > 0 ? g_tm_sms_dense : 148;
+            auto grid_of = [&](int ns, int rw) {
                 const int gy = (B + ns - 1) / ns;
-                const int gx = n <= 1024 ? (rows + 7) / 8 : std::max(1, std::min((rows + 7) / 8, 296 / gy));
-                return dim3(gx, gy);
+                const int need = (rows + 8 * rw - 1) / (8 * rw);
+                return dim3(std::max(1, std::min(need, 2 * nsm / gy)), gy);
             };
-            while (NS > 2 && NS / 2 >= B) NS /= 2;
-            while (NS > 2 && grid_of(NS).x * grid_of(NS).y < 128 && grid_of(NS / 2).y > grid_of(NS).y) NS /= 2;
-            const dim3 grid = grid_of(NS);
-            if (NS == 8) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<8>, grid, dim3(256), per * 8, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
-            else if (NS == 4) G4_CUDA(launch_pdl(gemv_dense_ms_kernel<4>, grid, dim3(256), per * 4, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
-            else G4_CUDA(launch_pdl(gemv_dense_ms_kernel<2>, grid, dim3(256), per * 2, st, w, type, n, rows, x, ldx, B, out, ldo, epi, evec, ld_evec));
+            int RW = NS == 8 ? 4 : 8;
+            while (NS > 2 && grid_of(NS, RW).x * grid_of(NS, RW).y < nsm && grid_of(NS / 2, RW).y > grid_of(NS, RW).y) {
+                NS /= 2;
+                RW = NS == 8 ? 4 : 8;
+            }
+            while (RW > 1 && grid_of(NS, RW).x * grid_of(NS, RW).y < nsm && grid_of(NS, RW / 2).x > grid_of(NS, RW).x) RW /= 2;
+            const dim3 grid = grid_of(NS, RW);
+#define G4_DMS(NSV, RWV)                                                                                          \
+    if (NS == NSV && RW == RWV)                                                                                    \
+        G4_CUDA(launch_pdl(gemv_dense_ms_kernel<NSV, RWV>, grid, dim3(256), per * NSV, st, w, type, n, rows, x, ldx, \
+                           B, out, ldo, epi, evec, ld_evec));
+            G4_DMS(8, 4) else G4_DMS(8, 2) else G4_DMS(8, 1)
+            else G4_DMS(4, 8) else G4_DMS(4, 4) else G4_DMS(4, 2) else G4_DMS(4, 1)
+            else G4_DMS(2, 8) else G4_DMS(2, 4) else G4_DMS(2, 2) else G4_DMS(2, 1)
+#undef G4_DMS
             G4_LAUNCHED();
             return G4_OK;
         }
@@ -328,10 +400,19 @@ int launch_qk_block_sums(const void *w, int type, int n, int rows, const void *q
 namespace g4 {
 int prime_gemv_ks_attrs();
 int prime_gemv_attrs() {
+    {
+        int dev = 0, nsm = 0;
+        G4_CUDA(cudaGetDevice(&dev));
+        G4_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        g_tm_sms_dense = nsm;
+    }
     G4_CUDA(cudaFuncSetAttribute(gemv_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+#define G4_DMS_ATTR(NSV, RWV) \
+    G4_CUDA(cudaFuncSetAttribute(gemv_dense_ms_kernel<NSV, RWV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+    G4_DMS_ATTR(8, 4) G4_DMS_ATTR(8, 2) G4_DMS_ATTR(8, 1)
+    G4_DMS_ATTR(4, 8) G4_DMS_ATTR(4, 4) G4_DMS_ATTR(4, 2) G4_DMS_ATTR(4, 1)
+    G4_DMS_ATTR(2, 8) G4_DMS_ATTR(2, 4) G4_DMS_ATTR(2, 2) G4_DMS_ATTR(2, 1)
+#undef G4_DMS_ATTR
     return prime_gemv_ks_attrs();
 }
 }  // namespace g4

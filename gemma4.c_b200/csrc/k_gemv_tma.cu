@@ -184,7 +184,7 @@ __device__ __forceinline__ float tm_fold(const float2 *t, int nb, int s, const R
 
 // Stage (or compute, with the fused prologue) the activation of sequences
 // [s0, s0+nbc) into shared memory.  Ends with a CTA barrier.
-template <int TYPE>
+template <int TYPE, int NB>
 __device__ __forceinline__ void tm_stage(const GemvJobs &jobs, const GemvJob &J, TmAct &A, float *pro_x, int s0,
                                          int nbc, bool writer, float *pred) {
     const int n = J.n, nb = n / G4_QK, tid = threadIdx.x, lane = tid & 31, nt = blockDim.x;
@@ -195,7 +195,8 @@ __device__ __forceinline__ void tm_stage(const GemvJobs &jobs, const GemvJob &J,
         if (P.delta) P.delta += (size_t)s0 * P.dim;
         if (P.x_out) P.x_out += (size_t)s0 * P.dim;
         if (P.xn_out) P.xn_out += (size_t)s0 * P.dim;
-        prologue_run(P, nbc, pro_x, nullptr, writer, pred);
+        if (NB == 1 && prologue_reg_ok(P)) prologue_run_reg<10>(P, nbc, pro_x, writer, pred);
+        else prologue_run(P, nbc, pro_x, nullptr, writer, pred);
     }
     if (TYPE == G4_Q6_K) {  // fp32 (prologue output or the global activation) -> fixed-point pieces
         for (int t = warp; t < nbc * nb; t += nw) {
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
         if (producer && lane == 0)
             for (; issued < my_tiles && issued < S; issued++) issue(issued);
         pdl_wait();  // activation / residual from the previous kernel; weights above do not depend on it
-        tm_stage<TYPE>(jobs, J, A, pro_x, s0, nbc, jobs.pro_writer && bx == 0, pred);
+        tm_stage<TYPE, NB>(jobs, J, A, pro_x, s0, nbc, jobs.pro_writer && bx == 0, pred);
 
         if (producer) {
             if (lane == 0) {
