@@ -724,10 +724,11 @@ def main():
 
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     if B >= 2:  # the engine's tensor-core threshold (engine.cu tc_min_batch)
-        dtype = ("tensor cores: Q4_K as exact fp16 integer products, Q5_K int8 x int8 -> int32, Q6_K and BF16 "
-                 "on split-fp32 activations (fp16 x2 / bf16 x3) -> fp32; fp32 attention, KV cache and norms")
+        dtype = ("tensor cores: Q4_K as exact fp16 integer products, Q5_K int8 x int8 -> int32, Q6_K int8 x int8 "
+                 "-> int32 on 3-piece fixed-point activations; fp32 dense GEMV, attention, KV cache and norms")
     else:
-        dtype = "int8 x int4/int5 dp4a -> int32 (Q4_K/Q5_K x Q8_K), fp32 (Q6_K, dense, attention, norms)"
+        dtype = ("int8 x int4/int5 dp4a -> int32 (Q4_K/Q5_K x Q8_K), int8 dp4a on 3-piece fixed-point activations "
+                 "(Q6_K), fp32 (dense, attention, norms)")
     out = {"metric": metric, "value": value, "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": dtype,
