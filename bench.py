@@ -571,6 +571,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--gemv-rows", type=int, default=10240, help="gemv0 workload: matrix rows")
     ap.add_argument("--tc-min", type=int, default=None, help="engine tensor-core batch threshold")
+    ap.add_argument("--attn-split", default=None,
+                    help="attention rows per CTA 'sliding,global' (multiples of 32; default 128,256)")
     ap.add_argument("--lm-split", action="store_true",
                     help="N > 1: row-split the tied LM head over the ranks (NCCL all-gathers of the hidden "
                          "states and of one argmax key per sequence)")
@@ -646,6 +648,10 @@ def main():
     eng = g4.Engine(model, dist.local, max_seq=max_seq, max_batch=B, prefill_rows=256)
     if a.tc_min:
         eng.set_tc_min_batch(a.tc_min)
+    if a.attn_split:
+        sw, gl = (int(v) for v in a.attn_split.split(","))
+        eng.set_attn_split(sw, gl)
+        cfg["attn_split"] = [sw, gl]
     if a.lm_split and dist.world > 1:
         import torch.distributed as tdist
         box = [g4.nccl_unique_id() if dist.rank == 0 else None]

@@ -97,6 +97,7 @@ SIGNATURES = [
     ("g4_lm_split_merge", ip, [vp, ip, ip, ip, ip, vp]),
     ("g4_argmax_keys", ip, [vp, ip, ip, vp]),
     ("g4_engine_set_tc_min_batch", ip, [vp, ip]),
+    ("g4_engine_set_attn_split", ip, [vp, ip, ip]),
 ]
 
 _lib = None
@@ -407,6 +408,10 @@ class Engine:
         if r < 0:
             _check(G4_ERR_ARG)
         return r
+
+    def set_attn_split(self, sliding: int, global_: int):
+        """Attention rows per CTA for sliding / global layers (multiples of 32; 0: default)."""
+        _check(lib().g4_engine_set_attn_split(self.h, sliding, global_))
 
     def last_step_kernels(self) -> int:
         return int(lib().g4_engine_last_step_kernels(self.h))

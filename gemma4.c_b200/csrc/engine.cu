@@ -98,6 +98,7 @@ struct g4_engine {
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
     int *tc_tickets = nullptr;  // per row tile, zero between launches (in-kernel merge of split tiles)
+    int attn_split_swa = 0, attn_split_full = 0;  // attention rows per CTA (0: the kernel's default)
     int nsm = 0, tc_min_batch = 2;  // measured: the tensor-core step wins from 2 sequences (5.2 vs 9.2 ms)
     std::mutex mu;
 };
@@ -336,6 +337,7 @@ static AttnLayer attn_args(const g4_engine *e, int l) {
     A.window = ly.swa ? e->window : 0;
     A.eps = e->eps; A.err = e->d_err;
     A.qo = e->qo; A.part = e->attn_part; A.counters = e->attn_ctr; A.max_chunks = e->max_chunks;
+    A.split = ly.swa ? e->attn_split_swa : e->attn_split_full;
     // Steps run as whole CUDA graphs in stream order, so every cache row but `pos` was written by an
     // earlier graph launch (or fill_kv) that has completed; row `pos` of a shared-KV source is
     // written by an earlier kernel of this step and is only read after the dependency wait.
@@ -1055,6 +1057,25 @@ int g4_engine_set_tc_min_batch(g4_engine *e, int min_batch) {
     }
     e->tc_min_batch = min_batch;
     return prev;
+}
+
+int g4_engine_set_attn_split(g4_engine *e, int sliding, int global) {
+    if (!e || sliding < 0 || global < 0 || sliding % 32 || global % 32) {
+        set_error(G4_ERR_ARG, "set_attn_split: rows must be multiples of 32 (0: default)");
+        return G4_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (sliding != e->attn_split_swa || global != e->attn_split_full) {  // captured steps used the old split
+        G4_CUDA(cudaSetDevice(e->device));
+        G4_CUDA(cudaStreamSynchronize(e->st));
+        for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+        e->graphs.clear();
+        e->graph_kernels.clear();
+        e->graph_hidden.clear();
+    }
+    e->attn_split_swa = sliding;
+    e->attn_split_full = global;
+    return G4_OK;
 }
 
 void *g4_engine_stream(g4_engine *e) { return e ? (void *)e->st : nullptr; }

@@ -671,12 +671,13 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     dim3 grid(nch, L.n_kv, B);
     int rc;
     if (L.hd <= 256) {
-        // Split length: a fixed number of rows per CTA for each layer kind (128 for a sliding
-        // window, 256 for the global context), never derived from the batch or the cache length.
+        // Split length: a fixed number of rows per CTA for each layer kind (by default 128 for a
+        // sliding window, 256 for the global context), never derived from the batch or the cache length.
         // The float sums of a sequence then follow the same split boundaries whether it is decoded
         // alone or in a batch, so batched and single-sequence decoding give identical results.
         // (Both are multiples of kChunk, which keeps the partials within max_chunks.)
-        const int sp = L.window > 0 ? 128 : 256;
+        const int sp = L.split > 0 ? L.split : (L.window > 0 ? 128 : 256);
+        if (sp % kChunk) { set_error(G4_ERR_ARG, "attention: split %d not a multiple of %d", sp, kChunk); return G4_ERR_ARG; }
         const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
         switch (L.hd) {
         case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;
