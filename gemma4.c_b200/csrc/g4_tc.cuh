@@ -13,6 +13,9 @@ namespace g4 {
 
 // Split row tiles one CTA of a tensor-core GEMM may have to merge after its units.
 constexpr int kTcMergeCap = 16;
+// Sequences per MMA pass of gemm_q6tc for a group of NP sequences (the B operand rows of one pass
+// are 3 pieces x tc6_npp(NP)).
+__host__ __device__ constexpr int tc6_npp(int NP) { return NP < 32 ? NP : 32; }
 
 struct TcArgs {
     const uint8_t *w;   // weight rows (device layout), row_bytes apart
@@ -113,7 +116,7 @@ __device__ __forceinline__ void tc4_store_q8(uint8_t *blk, float *ydk, int NP, i
 // B operand of gemm_q6tc for super-block k (768*NP bytes): the three fixed-point pieces of every
 // sequence's block (q6x_block) as int8 K-major core matrices,
 //   byte (kk/16)*(3*NP*16) + row*16 + kk%16,   row = (s/NPP)*3*NPP + j*NPP + s%NPP
-// (MMA pass s/NPP, then piece j, then sequence; NPP = min(NP, 32)), from this lane's elements
+// (MMA pass s/NPP, then piece j, then sequence; NPP = tc6_npp(NP)), from this lane's elements
 // 8*lane .. 8*lane+7 (one warp per block and sequence).  ys[k][s] = 2^(E-22) (0 when !valid).
 __device__ __forceinline__ void tc6_store_block(uint8_t *bq, float *ys, int k, int NP, int s, int lane, const float (&v)[8],
                                                 bool valid) {
@@ -123,7 +126,7 @@ __device__ __forceinline__ void tc6_store_block(uint8_t *bq, float *ys, int k, i
     uint32_t p[6];
     float y;
     q6x_block(w, p, y);
-    const int npp = NP < 32 ? NP : 32, pass = s / npp, sl = s % npp;
+    const int npp = tc6_npp(NP), pass = s / npp, sl = s % npp;
     uint8_t *blk = bq + (size_t)k * 768 * NP + (size_t)(lane >> 1) * (3 * NP * 16) + 8 * (lane & 1);
 #pragma unroll
     for (int j = 0; j < 3; j++)

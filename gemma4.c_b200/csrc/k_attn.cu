@@ -72,6 +72,32 @@ __device__ __forceinline__ void load_row(float (&dst)[EPL], const float *src) {
 // Per-head RMSNorm (+ weight) and Neox RoPE of one head vector by one warp
 // (main.c:1458-1476, 1725-1745).  Lane l holds elements l + 32 i, so the RoPE
 // partner j + hd/2 of element j sits in the same lane.  Writes dst[hd].
+// Element e of a lane's share of a row in the streaming kernel: vectors of V
+// floats, lane-interleaved (lane l holds [V*l, V*l+V), [32V + V*l, ...), ...),
+// so every vector load of a warp reads one contiguous span of shared memory
+// (no bank conflicts).
+template <int EPL>
+__device__ __forceinline__ int row_elem(int lane, int e) {
+    constexpr int V = EPL % 4 == 0 ? 4 : 2;
+    return V * lane + 32 * V * (e / V) + e % V;
+}
+template <int EPL>
+__device__ __forceinline__ void load_row_il(float (&dst)[EPL], const float *row, int lane) {
+    if constexpr (EPL % 4 == 0) {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 4) {
+            const float4 a = *reinterpret_cast<const float4 *>(row + row_elem<EPL>(lane, e));
+            dst[e] = a.x; dst[e + 1] = a.y; dst[e + 2] = a.z; dst[e + 3] = a.w;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) {
+            const float2 a = *reinterpret_cast<const float2 *>(row + row_elem<EPL>(lane, e));
+            dst[e] = a.x; dst[e + 1] = a.y;
+        }
+    }
+}
+
 template <int EPL>
 __device__ __forceinline__ void warp_norm_rope(const float *src, const float *w, const float2 *cs, int n_rot, float eps,
                                                float *dst, float *dst2) {
@@ -455,7 +481,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     __syncthreads();
     float qv[G][EPL];
 #pragma unroll
-    for (int g = 0; g < G; g++) load_row<EPL>(qv[g], qs[g] + lane * EPL);
+    for (int g = 0; g < G; g++) load_row_il<EPL>(qv[g], qs[g], lane);
     float m[G], l[G], acc[G][EPL];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -477,7 +503,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
             const int tl = warp + NW * r;
             const int t = t0 + beg + j * kSub + tl;
             float kr[EPL];
-            load_row<EPL>(kr, ((new_row && t == pos) ? knew : kb + min(tl, cnt - 1) * HD) + lane * EPL);
+            load_row_il<EPL>(kr, (new_row && t == pos) ? knew : kb + min(tl, cnt - 1) * HD, lane);
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 float d = 0.0f;
@@ -515,7 +541,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
             if (tl >= cnt) break;
             const int t = t0 + beg + j * kSub + tl;
             float vr[EPL];
-            load_row<EPL>(vr, ((new_row && t == pos) ? vnew : vb + tl * HD) + lane * EPL);
+            load_row_il<EPL>(vr, (new_row && t == pos) ? vnew : vb + tl * HD, lane);
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 const float pr = __shfl_sync(0xffffffffu, p, (r * G + g) << (5 - H));
@@ -534,7 +560,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < EPL; e++) red[((size_t)warp * G + g) * HD + lane * EPL + e] = acc[g][e];
+        for (int e = 0; e < EPL; e++) red[((size_t)warp * G + g) * HD + row_elem<EPL>(lane, e)] = acc[g][e];
     __syncthreads();
     if (tid < G) {
         float M = -INFINITY;

@@ -24,9 +24,9 @@
 // quants into the int8 planes of A in TMEM (tcgen05.st), warp group e = half
 // e of the block; warps 10..17 run the per-block epilogue for half of the
 // sequences of each MMA pass.  The MMA N is 3 pieces x NPP sequences
-// (NPP = 32, two passes at 64 sequences), and the accumulators of
-// consecutive passes alternate between two TMEM buffers.  Every wait is
-// bounded (2 s).
+// (NPP = 32, two passes at 64 sequences), and consecutive passes rotate
+// through the TMEM accumulator buffers that fit beside A (two at N = 96,
+// four at N = 48).  Every wait is bounded (2 s).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -43,7 +43,7 @@ namespace {
 
 constexpr int kQ6Threads = 576;
 constexpr int kQ6RawStages = 3;
-constexpr int kQ6BStages = 2;
+constexpr int kQ6BStagesMax = 4;
 
 // The device row of a Q6_K matrix is stored as planes: ql (128 B per
 // super-block), qh (64 B), scales (16 B), d (2 B).  A raw tile (128 rows x
@@ -57,29 +57,32 @@ constexpr int kQ6QhOff = 16384, kQ6ScOff = 24576;
 
 template <int NP>
 struct Q6Cfg {
-    static constexpr int NPP = NP < 32 ? NP : 32;  // sequences per MMA pass
+    static constexpr int NPP = tc6_npp(NP);        // sequences per MMA pass
     static constexpr int NPASS = NP / NPP;          // passes per super-block
     static constexpr int N = 3 * NPP;               // MMA N: three activation pieces
     static constexpr int SP = NPP / 2;              // sequences per epilogue warp and pass
     static constexpr int raw = 128 * 208;           // ql, qh, sc of one super-block for 128 rows
     static constexpr int bst = 768 * NP;            // B operand of one super-block
+    static constexpr int BS = NP == 64 ? 3 : 4;      // B operand stages (copies in flight)
     static constexpr int b_off = kQ6RawStages * raw;
-    static constexpr int total = b_off + kQ6BStages * bst + 1024;
-    // TMEM: two accumulator buffers [D_h | D_l] of N columns each, then A: plane h (64 columns of
+    static constexpr int total = b_off + BS * bst + 1024;
+    // TMEM: NBUF accumulator buffers [D_h | D_l] of N columns each, then A: plane h (64 columns of
     // 4 int8 weights), plane l (64)
     static constexpr uint32_t acc = 2 * N;
-    static constexpr uint32_t a = 2 * acc;
+    static constexpr int NBUF = (512 - 128) / acc > 4 ? 4 : (512 - 128) / acc;
+    static constexpr uint32_t a = NBUF * acc;
+    static_assert(NP % NPP == 0, "sequence group");
     static_assert(a + 128 <= 512, "TMEM columns");
 };
 
 struct Q6State {
-    uint64_t raw_full[kQ6RawStages], raw_empty[kQ6RawStages], b_full[kQ6BStages], b_empty[kQ6BStages];
-    uint64_t a_full[4], a_empty[4], acc_full[2], acc_empty[2], mma_done;
+    uint64_t raw_full[kQ6RawStages], raw_empty[kQ6RawStages], b_full[kQ6BStagesMax], b_empty[kQ6BStagesMax];
+    uint64_t a_full[4], a_empty[4], acc_full[4], acc_empty[4], mma_done;
     uint32_t tmem_base;
     volatile int abort;
     int mcount;               // row tiles this CTA finished last (merged after its units)
     int mlist[kTcMergeCap];
-    alignas(16) float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (both passes), by block parity
+    alignas(16) float ys[8][2][32];  // per epilogue warp: activation block scales of its sequences (all passes), by block parity
 };
 
 __device__ __forceinline__ bool q6_wait(Q6State &S, uint64_t *bar, uint32_t parity) {
@@ -126,7 +129,8 @@ __device__ __forceinline__ void q6_merge_rows(const TcArgs &a, int NP, int NPASS
 template <int NP>
 __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_constant__ Q6Maps maps, TcArgs a) {
     using CF = Q6Cfg<NP>;
-    constexpr int RAW = CF::raw, BST = CF::bst, BS = kQ6BStages, RS = kQ6RawStages;
+    constexpr int RAW = CF::raw, BST = CF::bst, BS = CF::BS, RS = kQ6RawStages;
+    static_assert(CF::total + sizeof(Q6State) <= 227 * 1024, "shared memory per CTA");
     constexpr int NPP = CF::NPP, NPASS = CF::NPASS, N = CF::N, SP = CF::SP;
     extern __shared__ uint8_t smem_dyn[];
     __shared__ Q6State S;
@@ -147,7 +151,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
             mbar_init(&S.a_full[i], 4);
             mbar_init(&S.a_empty[i], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < CF::NBUF; i++) {
             mbar_init(&S.acc_full[i], 1);
             mbar_init(&S.acc_empty[i], 8);
         }
@@ -210,8 +214,8 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
                     if (!q6_wait(S, &S.b_full[bs], (i / BS) & 1)) { ok = false; break; }
                     const uint32_t bsa = smem_u32(bst + bs * BST);
                     for (int ps = 0; ps < NPASS && ok; ps++) {
-                        const int it = i * NPASS + ps, buf = it & 1;
-                        if (!q6_wait(S, &S.acc_empty[buf], ((it >> 1) & 1) ^ 1)) { ok = false; break; }
+                        const int it = i * NPASS + ps, buf = it % CF::NBUF;
+                        if (!q6_wait(S, &S.acc_empty[buf], ((it / CF::NBUF) & 1) ^ 1)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t dh = tbase + buf * CF::acc, dl = dh + N;
                         for (int qi = 0; qi < 4; qi++) {
@@ -383,8 +387,8 @@ __global__ void __launch_bounds__(kQ6Threads, 1) gemm_q6tc_kernel(const __grid_c
             if (nu < a.units) { nhd = fetch_d(nu, nbk); nys = fetch_ys(nbk); }
 #pragma unroll
             for (int ps = 0; ps < NPASS; ps++) {
-                const int it = i * NPASS + ps, buf = it & 1;
-                if (!q6_wait(S, &S.acc_full[buf], (it >> 1) & 1)) { ok = false; break; }
+                const int it = i * NPASS + ps, buf = it % CF::NBUF;
+                if (!q6_wait(S, &S.acc_full[buf], (it / CF::NBUF) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const float *yv = S.ys[pw][i & 1] + ps * SP;
                 const uint32_t col = tl + buf * CF::acc + p * SP;
