@@ -91,6 +91,7 @@ SIGNATURES = [
     ("g4_engine_fill_kv", ip, [vp, ip, C.c_uint64]),
     ("g4_engine_time_attention", ip, [vp, vp, ip, ip, ip, vp]),
     ("g4_set_tc_min_batch", ip, [ip]),
+    ("g4_set_gemv_rows", ip, [ip]),
     ("g4_nccl_unique_id", ip, [vp]),
     ("g4_engine_lm_split", ip, [vp, vp, ip, ip]),
     ("g4_lm_split_rows", ip, [ip, ip, ip, vp, vp]),
@@ -270,6 +271,11 @@ def set_tc_min_batch(b: int) -> int:
     if r < 0:
         _check(G4_ERR_ARG)
     return r
+
+
+def set_gemv_rows(on: bool) -> int:
+    """Batch-1 Q4_K/Q5_K GEMVs on the row-owner kernel (True) or the tiled kernel; returns the previous."""
+    return int(lib().g4_set_gemv_rows(1 if on else 0))
 
 
 def registry_clear():

@@ -680,6 +680,8 @@ int g4_sample_token(const float *logits, int n, float temp, float topp, int topk
     return sample_tail_host(hv, hi, k, temp, topp, rng, p);
 }
 
+int g4_set_gemv_rows(int on) { return g4::set_gemv_rows(on ? 1 : 0); }
+
 int g4_set_tc_min_batch(int b) {
     if (b < 1) { set_error(G4_ERR_ARG, "tc min batch %d", b); return -1; }
     return g_tc_min_batch.exchange(b);

@@ -71,6 +71,7 @@ constexpr int kFusedMaxBatch = 8;
 
 int launch_quantize_q8k(const float *x, int ldx, void *y, int n, int B, cudaStream_t st);
 int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st);
+int set_gemv_rows(int on);  // 1: batch-1 Q4_K/Q5_K GEMVs on gemv_rows_kernel; returns the previous value
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
                       int B, int epi, const float *evec, int ld_evec, cudaStream_t st,
                       const Prologue *pro = nullptr, int pro_writer = 0);

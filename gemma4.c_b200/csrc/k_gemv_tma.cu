@@ -419,7 +419,220 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
     }
 }
 
+// ---------------------------------------------------------------- batch-1 row-owner GEMV (Q4_K / Q5_K)
+//
+// At batch 1 the GEMV is bounded by instruction issue and by the latency of
+// its first weight bytes more than by HBM bandwidth, so this variant keeps
+// the work per weight small: each warp owns tiles of 8 row units (a row of a
+// matrix; for a gate/up pair 4 rows of each) and streams them through two
+// shared-memory buffers of its own (8 bulk copies of KC super-blocks per row,
+// one mbarrier per buffer, no CTA-wide synchronisation after the activation
+// is staged).  4 lanes share a super-block (64 weights each: 16 dp4a, two
+// shuffle levels per integer sum), and lane group g folds its row's block
+// terms in registers in the canonical row order (RowOrder), so the result is
+// bit-identical to gemv_tma_kernel and to the tensor-core GEMMs.  The first
+// two chunks of every warp are requested before griddepcontrol.wait.
+constexpr int kRoWarps = 16;
+constexpr int kRoThreads = kRoWarps * 32;
+constexpr int kRoBufs = 2;
+
+struct RoPlan {
+    int row_bytes;
+    int kc;           // super-blocks per chunk
+    int chunk_bytes;  // kc * block bytes (one row unit)
+    int unit_stride;  // bytes between the row units of a buffer (chunk padded to 16 mod 32: no bank conflicts)
+    int stage_bytes;  // 8 row units
+    int act_bytes;    // activation staging (+ prologue scratch) before the warp buffers
+    int pro_off;
+    int tiles;        // tiles of all jobs
+    int tile_begin[kMaxJobs + 1];
+};
+
+// Scales and mins of sub-blocks 2j and 2j+1 of a Q4_K/Q5_K block (get_scale_min_k4, main.c:162-170).
+__device__ __forceinline__ void ro_scales(const uint4 &m, int j, int &sc0, int &sc1, int &mn0, int &mn1) {
+    const uint32_t s0 = m.y, s1 = m.z, s2 = m.w;
+    const uint32_t sc03 = s0 & 0x3f3f3f3fu;
+    const uint32_t sc47 = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
+    const uint32_t mn03 = s1 & 0x3f3f3f3fu;
+    const uint32_t mn47 = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
+    sc0 = (int)__byte_perm(sc03, sc47, 0x4440 | (2 * j)) & 0xff;
+    sc1 = (int)__byte_perm(sc03, sc47, 0x4440 | (2 * j + 1)) & 0xff;
+    mn0 = (int)__byte_perm(mn03, mn47, 0x4440 | (2 * j)) & 0xff;
+    mn1 = (int)__byte_perm(mn03, mn47, 0x4440 | (2 * j + 1)) & 0xff;
+}
+
+// Term (a, c) of super-block b of one row (blk in shared memory) for this lane's 64 weights
+// (32-byte chunk j = lane & 3 of the quants): the integer sums S and M of the whole block
+// (exact, over the 4 lanes of the group), then a = d_x, c = fma(d, S, -dmin*M) as in tm_block.
+template <int TYPE>
+__device__ __forceinline__ float2 ro_block(const uint8_t *blk, int b, int j, const TmAct &A) {
+    constexpr int QOFF = TYPE == G4_Q4_K ? 16 : 48;
+    const uint4 meta = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + QOFF + 32 * j);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + QOFF + 32 * j + 16);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        lo[i] = w[i] & 0x0F0F0F0Fu;
+        hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+    }
+    if (TYPE == G4_Q5_K) {  // 5th bit: bit 2j (low nibbles) / 2j+1 (high) of qh[l]
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            lo[i] |= ((hw[i] >> (2 * j)) & 0x01010101u) << 4;
+            hi[i] |= ((hw[i] >> (2 * j + 1)) & 0x01010101u) << 4;
+        }
+    }
+    const int8_t *q8 = A.qs + (size_t)b * G4_QK + 64 * j;
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(q8), a1 = *reinterpret_cast<const uint4 *>(q8 + 16);
+    const uint4 a2 = *reinterpret_cast<const uint4 *>(q8 + 32), a3 = *reinterpret_cast<const uint4 *>(q8 + 48);
+    int dl = __dp4a((int)lo[0], (int)a0.x, 0);
+    dl = __dp4a((int)lo[1], (int)a0.y, dl);
+    dl = __dp4a((int)lo[2], (int)a0.z, dl);
+    dl = __dp4a((int)lo[3], (int)a0.w, dl);
+    dl = __dp4a((int)lo[4], (int)a1.x, dl);
+    dl = __dp4a((int)lo[5], (int)a1.y, dl);
+    dl = __dp4a((int)lo[6], (int)a1.z, dl);
+    dl = __dp4a((int)lo[7], (int)a1.w, dl);
+    int dh = __dp4a((int)hi[0], (int)a2.x, 0);
+    dh = __dp4a((int)hi[1], (int)a2.y, dh);
+    dh = __dp4a((int)hi[2], (int)a2.z, dh);
+    dh = __dp4a((int)hi[3], (int)a2.w, dh);
+    dh = __dp4a((int)hi[4], (int)a3.x, dh);
+    dh = __dp4a((int)hi[5], (int)a3.y, dh);
+    dh = __dp4a((int)hi[6], (int)a3.z, dh);
+    dh = __dp4a((int)hi[7], (int)a3.w, dh);
+    int sc0, sc1, mn0, mn1;
+    ro_scales(meta, j, sc0, sc1, mn0, mn1);
+    const int *bs = A.bs2 + (size_t)b * 8 + 2 * j;  // 4-byte aligned only (nb may be odd)
+    int S = sc0 * dl + sc1 * dh, M = mn0 * bs[0] + mn1 * bs[1];
+    S += __shfl_xor_sync(0xffffffffu, S, 1);
+    M += __shfl_xor_sync(0xffffffffu, M, 1);
+    S += __shfl_xor_sync(0xffffffffu, S, 2);
+    M += __shfl_xor_sync(0xffffffffu, M, 2);
+    const float dw = f16_to_f32((uint16_t)(meta.x & 0xffffu));
+    const float dmw = f16_to_f32((uint16_t)(meta.x >> 16));
+    return make_float2(A.dx[b], __fmaf_rn(dw, __int2float_rn(S), __fmul_rn(-dmw, __int2float_rn(M))));
+}
+
+// The fields of job jb that a tile needs (selected without indexing the parameter array).
+struct RoJob {
+    const uint8_t *w, *w2;
+    float *out;
+    int rows;
+    RowOrder ord, ord2;
+};
+__device__ __forceinline__ RoJob ro_job(const GemvJobs &jobs, int jb) {
+    const GemvJob &J = jb == 0 ? jobs.j[0] : jb == 1 ? jobs.j[1] : jobs.j[2];
+    return RoJob{(const uint8_t *)J.w, (const uint8_t *)J.w2, J.out, J.rows, J.ord, J.ord2};
+}
+
+template <int TYPE, int R>
+__global__ void __launch_bounds__(kRoThreads, 1) gemv_rows_kernel(GemvJobs jobs, RoPlan plan) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kRoWarps][kRoBufs];
+    __shared__ float pred[8];
+    constexpr int BLK = TYPE == G4_Q4_K ? 144 : 176;
+    constexpr int UPR = 8 / R;  // rows per tile
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, j = lane & 3;
+    pdl_trigger();
+    const int n = jobs.j[0].n, nb = n / G4_QK, KC = plan.kc, nck = (nb + KC - 1) / KC;
+    TmAct A{};
+    A.qs = (int8_t *)smem;
+    A.dx = (float *)(smem + (size_t)n);
+    A.bs2 = (int *)(smem + (size_t)n + (size_t)nb * 4);
+    float *pro_x = (float *)(smem + plan.pro_off);
+    uint8_t *stage = smem + plan.act_bytes + (size_t)warp * kRoBufs * plan.stage_bytes;
+    const int nwarps = gridDim.x * kRoWarps, gw = warp * gridDim.x + (int)blockIdx.x;
+    const int my_tiles = gw < plan.tiles ? (plan.tiles - gw + nwarps - 1) / nwarps : 0;
+    const int nchunks = my_tiles * nck;
+    auto job_of = [&](int T, int &lt) {
+        int jb = 0;
+        if (jobs.njobs > 1 && T >= plan.tile_begin[1]) jb = 1;
+        if (jobs.njobs > 2 && T >= plan.tile_begin[2]) jb = 2;
+        lt = T - (jb == 0 ? 0 : jb == 1 ? plan.tile_begin[1] : plan.tile_begin[2]);
+        return jb;
+    };
+    auto issue = [&](int ci) {  // lane 0: the chunk's bulk copies, one per row unit
+        const int T = gw + (ci / nck) * nwarps, kc = ci % nck, kb0 = kc * KC, kcnt = min(KC, nb - kb0);
+        int lt;
+        const RoJob Jt = ro_job(jobs, job_of(T, lt));
+        const int r0 = lt * UPR, vr = min(UPR, Jt.rows - r0);  // valid rows of the tile
+        uint64_t *bar = &full[warp][ci % kRoBufs];
+        uint8_t *dst = stage + (ci % kRoBufs) * plan.stage_bytes;
+        const uint32_t cb = (uint32_t)(kcnt * BLK);
+        mbar_expect_tx(bar, cb * (uint32_t)(vr * R));
+        const size_t off = (size_t)r0 * plan.row_bytes + (size_t)kb0 * BLK;
+        for (int u = 0; u < vr; u++) {
+            bulk_g2s(dst + (size_t)u * plan.unit_stride, Jt.w + off + (size_t)u * plan.row_bytes, cb, bar);
+            if (R == 2) bulk_g2s(dst + (size_t)(u + 4) * plan.unit_stride, Jt.w2 + off + (size_t)u * plan.row_bytes, cb, bar);
+        }
+    };
+    if (lane == 0) {
+        for (int b = 0; b < kRoBufs; b++) mbar_init(&full[warp][b], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int ci = 0; ci < kRoBufs && ci < nchunks; ci++) issue(ci);
+    }
+    __syncwarp();
+    pdl_wait();  // activation / residual from the previous kernel; the weights above do not depend on it
+    tm_stage<TYPE, 1>(jobs, jobs.j[0], A, pro_x, 0, 1, jobs.pro_writer && blockIdx.x == 0, pred);
+
+    float v = 0.0f, P = 0.0f;
+    int us = 0, ks = 0, row = 0;
+    RowOrder o{};
+    RoJob Jt{};
+    int ci = 0;
+    for (; ci < nchunks; ci++) {
+        const int kc = ci % nck, kb0 = kc * KC, kcnt = min(KC, nb - kb0);
+        if (!mbar_wait(&full[warp][ci % kRoBufs], (ci / kRoBufs) & 1)) {
+            if (jobs.err && lane == 0) atomicExch(jobs.err, G4_ERR_TIMEOUT);
+            break;
+        }
+        if (kc == 0) {  // a new tile: this group's row and its canonical order
+            int lt;
+            Jt = ro_job(jobs, job_of(gw + (ci / nck) * nwarps, lt));
+            row = lt * UPR + (R == 2 ? (g & 3) : g);
+            o = (R == 2 && g >= 4) ? Jt.ord2 : Jt.ord;
+            v = 0.0f;
+            P = 0.0f;
+            us = o.share > 0 ? (int)(((long long)(o.tile0 + row / 128) * nb) % o.share) : 0;
+            ks = 0;
+        }
+        const uint8_t *rowp = stage + (ci % kRoBufs) * plan.stage_bytes + (size_t)g * plan.unit_stride;
+#pragma unroll 2
+        for (int kk = 0; kk < kcnt; kk++) {
+            const int b = kb0 + kk;
+            const float2 t = ro_block<TYPE>(rowp + (size_t)kk * BLK, b, j, A);
+            if (b > 0 && ((o.share > 0 && us == 0) || (o.kslice > 0 && ks == 0))) { v = __fadd_rn(v, P); P = 0.0f; }
+            P = __fmaf_rn(t.x, t.y, P);
+            if (o.share > 0 && ++us == o.share) us = 0;
+            if (o.kslice > 0 && ++ks == o.kslice) ks = 0;
+        }
+        if (kc == nck - 1) {
+            const float fin = __fadd_rn(v, P);
+            if (R == 2) {
+                const float up = __shfl_xor_sync(0xffffffffu, fin, 16);  // group g + 4: the up row
+                if (g < 4 && j == 0 && row < Jt.rows) Jt.out[row] = gelu_f32(fin) * up;
+            } else if (j == 0 && row < Jt.rows) {
+                Jt.out[row] = fin;
+            }
+        }
+        __syncwarp();  // every lane is done with this buffer before it is refilled
+        if (lane == 0 && ci + kRoBufs < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(ci + kRoBufs);
+        }
+    }
+    if (ci < nchunks && lane == 0)  // gave up: drain this warp's copies in flight (bounded) before the CTA exits
+        for (int k = ci; k < nchunks && k < ci + kRoBufs; k++) (void)mbar_wait(&full[warp][k % kRoBufs], (k / kRoBufs) & 1);
+}
+
 static int g_tm_sms = 0;
+static int g_ro_off = 0;  // 1: batch 1 takes gemv_tma_kernel as well (g4_set_gemv_rows)
 static constexpr int kTmSmemBudget = 220 * 1024;
 
 // Activation staging bytes of nbs sequences (Q4/Q5: Q8_K planes; Q6: fixed-point pieces), then the
@@ -492,6 +705,60 @@ static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st) {
     return G4_OK;
 }
 
+// The batch-1 row-owner GEMV, when it applies: one sequence, Q4_K/Q5_K, plain or gate/up epilogues,
+// one activation for all jobs.  Returns 1 if launched, 0 if not applicable, < 0 on error.
+template <int TYPE>
+static int ro_dispatch(GemvJobs &jobs, cudaStream_t st) {
+    const GemvJob &J0 = jobs.j[0];
+    const int n = J0.n, nb = n / G4_QK, R = J0.w2 ? 2 : 1;
+    constexpr int BLK = TYPE == G4_Q4_K ? 144 : 176;
+    for (int i = 0; i < jobs.njobs; i++) {
+        const GemvJob &J = jobs.j[i];
+        if (J.epi != EPI_STORE && J.epi != EPI_GELU_MUL) return 0;
+        if ((J.epi == EPI_GELU_MUL) != (J.w2 != nullptr) || !J.out) return 0;
+        if (!jobs.has_pro && J.act != J0.act) return 0;
+    }
+    RoPlan plan{};
+    plan.row_bytes = nb * BLK;
+    size_t act = ((tm_stage_bytes<TYPE>(1, n) + 15) & ~(size_t)15);
+    plan.pro_off = (int)act;
+    if (jobs.has_pro) act += (size_t)n * 4;
+    plan.act_bytes = (int)((act + 127) & ~(size_t)127);
+    const long room = (long)kTmSmemBudget - plan.act_bytes;
+    int kc = (int)(room / ((long)kRoWarps * kRoBufs * 8 * BLK));
+    if (kc > nb) kc = nb;
+    if (kc < 1) return 0;
+    plan.kc = kc;
+    plan.chunk_bytes = kc * BLK;
+    plan.unit_stride = plan.chunk_bytes % 32 ? plan.chunk_bytes : plan.chunk_bytes + 16;
+    plan.stage_bytes = 8 * plan.unit_stride;
+    if ((size_t)plan.act_bytes + (size_t)kRoWarps * kRoBufs * plan.stage_bytes > (size_t)kTmSmemBudget) {
+        kc = (int)(room / ((long)kRoWarps * kRoBufs * 8 * (BLK + 16)));
+        if (kc < 1) return 0;
+        plan.kc = kc;
+        plan.chunk_bytes = kc * BLK;
+        plan.unit_stride = plan.chunk_bytes % 32 ? plan.chunk_bytes : plan.chunk_bytes + 16;
+        plan.stage_bytes = 8 * plan.unit_stride;
+    }
+    const int upr = 8 / R;
+    int tiles = 0;
+    for (int i = 0; i < jobs.njobs; i++) {
+        plan.tile_begin[i] = tiles;
+        tiles += (jobs.j[i].rows + upr - 1) / upr;
+    }
+    plan.tile_begin[jobs.njobs] = tiles;
+    plan.tiles = tiles;
+    const int ctas = tiles < g_tm_sms ? tiles : g_tm_sms;
+    const size_t smem = (size_t)plan.act_bytes + (size_t)kRoWarps * kRoBufs * plan.stage_bytes;
+    cudaError_t e = R == 2 ? launch_pdl(gemv_rows_kernel<TYPE, 2>, dim3(ctas), dim3(kRoThreads), smem, st, jobs, plan)
+                           : launch_pdl(gemv_rows_kernel<TYPE, 1>, dim3(ctas), dim3(kRoThreads), smem, st, jobs, plan);
+    if (e != cudaSuccess) {
+        set_error(G4_ERR_CUDA, "gemv_rows launch: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 1;
+}
+
 int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
     if (g_tm_sms == 0) {
         int dev = 0;
@@ -551,6 +818,14 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
         J.cta_begin = ctas;
         ctas += J.ctas;
     }
+    if (B == 1 && !g_ro_off && (type == G4_Q4_K || type == G4_Q5_K)) {
+        const int r = type == G4_Q4_K ? ro_dispatch<G4_Q4_K>(jobs, st) : ro_dispatch<G4_Q5_K>(jobs, st);
+        if (r < 0) return G4_ERR_CUDA;
+        if (r > 0) {
+            G4_LAUNCHED();
+            return G4_OK;
+        }
+    }
     int rc;
     switch (type) {
     case G4_Q4_K: rc = tm_dispatch<G4_Q4_K>(jobs, ctas, B, st); break;
@@ -577,7 +852,17 @@ static int tm_prime() {
     return rc ? rc : tm_prime_r<TYPE, 2>();
 }
 
+int set_gemv_rows(int on) {
+    const int prev = g_ro_off ? 0 : 1;
+    g_ro_off = on ? 0 : 1;
+    return prev;
+}
+
 int prime_gemv_ks_attrs() {
+    G4_CUDA(cudaFuncSetAttribute(gemv_rows_kernel<G4_Q4_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmSmemBudget));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rows_kernel<G4_Q4_K, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmSmemBudget));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rows_kernel<G4_Q5_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmSmemBudget));
+    G4_CUDA(cudaFuncSetAttribute(gemv_rows_kernel<G4_Q5_K, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmSmemBudget));
     int rc = tm_prime<G4_Q4_K>();
     rc |= tm_prime<G4_Q5_K>();
     rc |= tm_prime<G4_Q6_K>();

@@ -177,6 +177,13 @@ int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_b
  * one, or -1 on a bad value. */
 int g4_set_tc_min_batch(int min_batch);
 
+/* Which kernel runs Q4_K/Q5_K GEMVs of one activation vector (g4_mm,
+ * g4d_mm with batch 1, the engine's batch-1 step): 1 (default) the row-owner
+ * kernel (a warp streams whole rows and folds them in registers), 0 the
+ * tiled streaming kernel used for 2..15 activations.  Both give bit-identical
+ * results.  Not part of the reference interface; returns the previous value. */
+int g4_set_gemv_rows(int on);
+
 /* Decode attention (the result of g4_attn_decode) on DEVICE pointers, for
  * callers that cannot let the library allocate device memory.  This entry
  * point has no counterpart in the reference.  It calls no cudaMalloc/cudaFree:

@@ -152,3 +152,22 @@ def test_e4b_batch_invariance_at_long_context(g4, gpu):
             assert n1 == nxt[b], (b, n1, nxt[b])
     finally:
         es.close()
+
+
+@pytest.mark.parametrize("which", ["tiny", "tinyq5"])
+def test_batch1_gemv_kernels_identical_in_engine(g4, gpu, request, which):
+    """Batch-1 decode (fused residual/norm prologues, Q+K and gate/up launches) on the row-owner GEMV
+    and on the tiled GEMV: identical hidden states and greedy tokens."""
+    model = request.getfixturevalue(which)
+    prompt = np.random.default_rng(5).integers(0, model.shape.vocab_size, 6).astype(np.int32)
+    out = []
+    prev = g4.set_gemv_rows(True)
+    try:
+        for on in (True, False):
+            g4.set_gemv_rows(on)
+            out.append(single(g4, model, prompt, 6))
+    finally:
+        g4.set_gemv_rows(prev)
+    (ga, ha), (gb, hb) = out
+    assert list(ga) == list(gb)
+    assert (ha.view(np.uint32) == hb.view(np.uint32)).all()

@@ -164,3 +164,21 @@ def test_logits_tied(gpu, orc, g4):
     assert am == orc.argmax_first(e)
     _, am2 = gpu.logits_tied(x, emb, Q6, 512, 4096, 30.0, want_logits=False)
     assert am2 == am
+
+
+@pytest.mark.parametrize("t,rows,n", [(Q4, 10240, 2560), (Q4, 2560, 2048), (Q4, 7, 768), (Q5, 2048, 2560),
+                                      (Q4, 2560, 10240), (Q5, 13, 1280)])
+def test_batch1_gemv_kernels_bitwise(gpu, g4, t, rows, n):
+    """The row-owner batch-1 GEMV and the tiled streaming GEMV fold every row's exact block terms in
+    the same canonical order: identical bits (ragged tiles, odd block counts, long rows)."""
+    rng = np.random.default_rng(rows * 5 + n + t)
+    w = g4.synth.rand_blocks(rng, t, rows, n, 1e-3, 2e-2)
+    x = rng.standard_normal(n).astype(np.float32)
+    prev = g4.set_gemv_rows(True)
+    try:
+        a = gpu.mm(x, w, n, rows, t)
+        g4.set_gemv_rows(False)
+        b = gpu.mm(x, w, n, rows, t)
+    finally:
+        g4.set_gemv_rows(prev)
+    assert (a.view(np.uint32) == b.view(np.uint32)).all()
