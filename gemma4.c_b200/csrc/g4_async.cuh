@@ -48,6 +48,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Wait for phase `parity` of `bar` with the thread suspended between tests (it
+// issues no instructions while the phase is incomplete, leaving the issue
+// slots to working warps); false after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
 // Wait for phase `parity` of `bar`; false after kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                 for (; issued < my_tiles; issued++) {
                     const int st = issued % S;
                     // slot st was last used by tile issued-S: wait until all consumer warps released it
-                    if (!mbar_wait(&empty[st], ((issued / S) - 1) & 1)) { ok = false; break; }
+                    if (!mbar_wait_sleep(&empty[st], ((issued / S) - 1) & 1)) { ok = false; break; }
                     if (abort_flag) break;
                     issue(issued);
                 }
@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) gemv_tma_kernel(GemvJobs jobs, 
                             (size_t)(q / GPR) * R * nb * NB;
             for (int i = 0; i < my_tiles; i++) {
                 const int tile = cta + i * nctas, st = i % S;
-                if (!mbar_wait(&full[st], (i / S) & 1)) {
+                if (!mbar_wait_sleep(&full[st], (i / S) & 1)) {
                     atomicExch(&abort_flag, 1);
                     if (jobs.err) atomicExch(jobs.err, G4_ERR_TIMEOUT);
                     break;
@@ -588,7 +588,7 @@ __global__ void __launch_bounds__(kRoThreads, 1) gemv_rows_kernel(GemvJobs jobs,
     int ci = 0;
     for (; ci < nchunks; ci++) {
         const int kc = ci % nck, kb0 = kc * KC, kcnt = min(KC, nb - kb0);
-        if (!mbar_wait(&full[warp][ci % kRoBufs], (ci / kRoBufs) & 1)) {
+        if (!mbar_wait_sleep(&full[warp][ci % kRoBufs], (ci / kRoBufs) & 1)) {
             if (jobs.err && lane == 0) atomicExch(jobs.err, G4_ERR_TIMEOUT);
             break;
         }
