@@ -98,6 +98,13 @@ struct g4_engine {
     float *tc_part = nullptr;
     size_t tc_part_bytes = 0;
     int *tc_tickets = nullptr;  // per row tile, zero between launches (in-kernel merge of split tiles)
+    // side lane: the V projection's tensor-core GEMM runs on its own stream, beside the Q+K launch
+    // (both read the same normed input), with its own split partials and tickets
+    cudaStream_t st2 = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    float *tc_part2 = nullptr;
+    size_t tc_part2_bytes = 0;
+    int *tc_tickets2 = nullptr;
     int attn_split_swa = 0, attn_split_full = 0;  // attention rows per CTA (0: the kernel's default)
     int nsm = 0, tc_min_batch = 2;  // measured: the tensor-core step wins from 2 sequences (5.2 vs 9.2 ms)
     std::mutex mu;
@@ -221,6 +228,10 @@ void destroy(g4_engine *e) {
     if (e->h_cand_v) cudaFreeHost(e->h_cand_v);
     if (e->h_rows) cudaFreeHost(e->h_rows);
     if (e->h_cand_i) cudaFreeHost(e->h_cand_i);
+    if (e->st2) cudaStreamSynchronize(e->st2);
+    if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+    if (e->ev_join) cudaEventDestroy(e->ev_join);
+    if (e->st2) cudaStreamDestroy(e->st2);
     if (e->st) cudaStreamDestroy(e->st);
     delete e;
 }
@@ -293,30 +304,37 @@ int tc_maps(g4_engine *e, const void *w, int type, int n, int rows, const void *
 // y[B][rows] = W . act (fp32 [B][ld]) on the tensor cores, in groups of up
 // to 64 sequences.  act_ready: the B operand of this activation is already
 // in place (same activation as the previous call of the same type class).
+struct TcLane {  // where a tensor-core GEMM runs: stream, split partials, tickets
+    cudaStream_t st;
+    float *part;
+    size_t part_bytes;
+    int *tickets;
+};
 int tc_gemm(g4_engine *e, const void *w, int type, int n, int rows, const float *act, int ld, bool act_ready,
             float *out, int ldo, int B, int epi = EPI_STORE, unsigned long long *keys = nullptr, float cap = 0.0f,
-            const float *evec = nullptr, int ld_evec = 0) {
+            const float *evec = nullptr, int ld_evec = 0, const TcLane *lane = nullptr) {
     const void *maps = nullptr;
     TRY(tc_maps(e, w, type, n, rows, &maps));
+    const TcLane ln = lane ? *lane : TcLane{e->st, e->tc_part, e->tc_part_bytes, e->tc_tickets};
     if (B > 64) act_ready = false;
     for (int g0 = 0; g0 < B; g0 += 64) {
         const int gb = B - g0 < 64 ? B - g0 : 64, np = tc_np(gb);
         float *o = out ? out + (size_t)g0 * ldo : nullptr;
         if (type == G4_BF16) {
-            if (!act_ready) TRY(launch_bf3_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tcb, e->st));
-            TRY(launch_gemm_bf16tc((const CUtensorMap *)maps, n, rows, e->tcb, gb, np, o, ldo, e->tc_part,
-                                   e->tc_part_bytes, e->d_err, e->nsm, epi,
-                                   evec ? evec + (size_t)g0 * ld_evec : nullptr, ld_evec, e->st));
+            if (!act_ready) TRY(launch_bf3_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tcb, ln.st));
+            TRY(launch_gemm_bf16tc((const CUtensorMap *)maps, n, rows, e->tcb, gb, np, o, ldo, ln.part,
+                                   ln.part_bytes, e->d_err, e->nsm, epi,
+                                   evec ? evec + (size_t)g0 * ld_evec : nullptr, ld_evec, ln.st));
         } else if (type == G4_Q6_K) {
             float *ys = (float *)(e->tc6 + tc6_ys_offset(n));
-            if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, e->st));
-            TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, e->tc_part, e->tc_part_bytes,
-                                 e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, e->st, e->tc_tickets));
+            if (!act_ready) TRY(launch_tc6_split(act + (size_t)g0 * ld, ld, gb, n, np, e->tc6, ys, ln.st));
+            TRY(launch_gemm_q6tc(maps, w, n, rows, e->tc6, ys, gb, np, o, ldo, ln.part, ln.part_bytes,
+                                 e->d_err, e->nsm, epi, cap, keys ? keys + g0 : nullptr, ln.st, ln.tickets));
         } else {
             float *yd = (float *)(e->tcq + tc_yd_offset(n));
-            if (!act_ready) TRY(launch_tc_quant(type, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, e->st));
-            TRY(launch_gemm_tc((const CUtensorMap *)maps, w, type, n, rows, e->tcq, yd, gb, np, o, ldo, e->tc_part,
-                               e->tc_part_bytes, e->d_err, e->nsm, e->st, e->tc_tickets));
+            if (!act_ready) TRY(launch_tc_quant(type, act + (size_t)g0 * ld, ld, gb, n, np, e->tcq, yd, ln.st));
+            TRY(launch_gemm_tc((const CUtensorMap *)maps, w, type, n, rows, e->tcq, yd, gb, np, o, ldo, ln.part,
+                               ln.part_bytes, e->d_err, e->nsm, ln.st, ln.tickets));
         }
     }
     return G4_OK;
@@ -446,6 +464,17 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         Proj pr[3] = {{ly.wq, ly.wq_t, ly.qd, e->q}, {ly.wk, ly.wk_t, ly.kvd, e->k}, {ly.wv, ly.wv_t, ly.kvd, e->v}};
         const int np = has_kv ? 3 : 1;
         const int ktypes[3] = {G4_Q4_K, G4_Q5_K, G4_Q6_K};
+        // V on the side stream, concurrently with the Q+K launch: both read xn; attention joins it
+        const bool v_side = tcq_l && np == 3 && pr[2].t == G4_Q6_K && ready6 && e->st2 && e->tc_part2 &&
+                            pr[0].t == G4_Q4_K && pr[1].t == G4_Q4_K;
+        if (v_side) {
+            G4_CUDA(cudaEventRecord(e->ev_fork, e->st));
+            G4_CUDA(cudaStreamWaitEvent(e->st2, e->ev_fork, 0));
+            const TcLane side{e->st2, e->tc_part2, e->tc_part2_bytes, e->tc_tickets2};
+            TRY(tc_gemm(e, pr[2].w, pr[2].t, dim, pr[2].rows, e->xn, dim, true, pr[2].out, pr[2].rows, B, EPI_STORE,
+                        nullptr, 0.0f, nullptr, 0, &side));
+            G4_CUDA(cudaEventRecord(e->ev_join, e->st2));
+        }
         if (tcq_l) {
             int i0 = 0;
             if (np > 1 && pr[0].t == G4_Q4_K && pr[1].t == G4_Q4_K) {  // Q and K in one launch
@@ -454,7 +483,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                 ready8 = true;
                 i0 = 2;
             }
-            for (int i = i0; i < np; i++) {
+            for (int i = i0; i < (v_side ? 2 : np); i++) {
                 if (use_tc(e, B, pr[i].t, EPI_STORE)) {
                     bool &rdy = pr[i].t == G4_Q6_K ? ready6 : ready8;
                     // Q4_K and Q5_K operands differ in layout: reuse only within one type
@@ -484,6 +513,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
             if (pr[i].t == G4_F32 || pr[i].t == G4_F16 || pr[i].t == G4_BF16)
                 TRY(gemv(e, pr[i].w, pr[i].t, dim, pr[i].rows, e->xn, dim, false, pr[i].out, pr[i].rows, B));
 
+        if (v_side) G4_CUDA(cudaStreamWaitEvent(e->st, e->ev_join, 0));
         // attention (main.c:1886-1950)
         if (prefill) {
             AttnLayer A = attn_args(e, l);
@@ -990,6 +1020,12 @@ int create(g4_engine *e, const g4_model_desc *m, int max_seq, int max_batch, int
         e->tc_part_bytes = std::max(part, (size_t)16);
         TRY(dalloc_t(e, &e->tc_part, e->tc_part_bytes / sizeof(float)));
         TRY(dalloc_t(e, &e->tc_tickets, (size_t)e->vocab / 128 + 4096));  // zeroed; every launch leaves them zero
+        e->tc_part2_bytes = std::max(tc_part_bytes(e->kvd_max, dim, e->nsm), (size_t)16);
+        TRY(dalloc_t(e, &e->tc_part2, e->tc_part2_bytes / sizeof(float)));
+        TRY(dalloc_t(e, &e->tc_tickets2, 4096));
+        G4_CUDA(cudaStreamCreateWithFlags(&e->st2, cudaStreamNonBlocking));
+        G4_CUDA(cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming));
+        G4_CUDA(cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming));
     }
     TRY(dalloc_t(e, &e->attn_ctr, B * e->nkv));
     TRY(dalloc_t(e, &e->d_err, 1));
