@@ -99,8 +99,8 @@ struct AttnLayer {
     float *part;                    // scratch [B][n_heads][max_chunks][hd+2]
     int *counters;                  // [B][n_kv] zero-initialised tickets
     int max_chunks;
-    int split;                      // rows per CTA of attn_stream_kernel (a multiple of 32); 0: 128 for a
-                                    // sliding window, 256 otherwise
+    int split;                      // rows per canonical split of attn_stream_kernel (a multiple of 32);
+                                    // 0: 64 for a sliding window, 256 otherwise
     int early;                      // 1: every cache row but `pos` was written before the launch's
                                     //    stream predecessor started (earlier graph launches), so it
                                     //    may be copied before the grid dependency wait

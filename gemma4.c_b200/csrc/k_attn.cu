@@ -400,7 +400,8 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
 }
 
 template <int EPL, int G>
-__global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span) {
+__global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span,
+                                                                      int per) {
     constexpr int HD = EPL * 32, NW = kStreamWarps, RPW = kSub / NW, NV = RPW * G;
     static_assert(RPW == 2, "two rows per warp and sub-chunk: rows differ in lane bit 4 after the transpose sum");
     constexpr int H = NV == 2 ? 1 : NV == 4 ? 2 : 3;  // log2(NV)
@@ -422,10 +423,12 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     int t0 = 0;
     if (L.window > 0) { t0 = pos + 1 - L.window; if (t0 < 0) t0 = 0; }
     const int nwin = pos + 1 - t0;
-    const int nsplit = (nwin + span - 1) / span;
-    if (c >= nsplit) return;
-    const int beg = c * span, ctot = min(span, nwin - beg), nsub = (ctot + kSub - 1) / kSub;
-    const bool new_row = L.append && c == nsplit - 1;  // this CTA owns row `pos`
+    const int nsplit = (nwin + span - 1) / span;  // canonical splits of `span` rows
+    const int ncta = (nsplit + per - 1) / per;     // this CTA: splits [c*per, c*per + per)
+    if (c >= ncta) return;
+    const int sp0 = c * per, sp1 = min(nsplit, sp0 + per);
+    const int beg = sp0 * span, ctot = min(sp1 * span, nwin) - beg, nsub = (ctot + kSub - 1) / kSub;
+    const bool new_row = L.append && c == ncta - 1;  // this CTA owns row `pos`
     const int qd = L.n_heads * HD, kvd = L.n_kv * HD;
     const size_t head_base = ((size_t)cb * L.n_kv + h) * L.src_ring;
     const float2 *cs = L.rope ? L.rope + (size_t)pos * (L.n_rot / 2) : nullptr;
@@ -448,7 +451,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     // Sub-chunk j may be copied before the dependency wait (L.early) unless it holds row `pos` of a
     // cache that an earlier kernel of this step writes (a layer without its own cache reads row
     // `pos` of layer 22/23).  Row `pos` of a layer that appends comes from knew/vnew instead.
-    auto early_ok = [&](int j) { return L.append || c != nsplit - 1 || (j + 1) * kSub < ctot; };
+    auto early_ok = [&](int j) { return L.append || c != ncta - 1 || (j + 1) * kSub < ctot; };
     if (tid == 0) {
         for (int k = 0; k < kStages; k++) mbar_init(&full[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -483,17 +486,59 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
 #pragma unroll
     for (int g = 0; g < G; g++) load_row_il<EPL>(qv[g], qs[g], lane);
     float m[G], l[G], acc[G][EPL];
+    // the NW warp states of canonical split sp combined (M = max m, S = sum f l, o = sum f acc in
+    // warp order, f = e^(m - M)) into its partial (m, l, o); red: [NW][GH][HD] floats, GH heads at a time
+    auto combine = [&](int sp, float *red, int GH) {
+        if (lane == 0)
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
+            for (int g = 0; g < G; g++) { wml[warp][g][0] = m[g]; wml[warp][g][1] = l[g]; }
+        __syncthreads();
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int w = 0; w < NW; w++) M = fmaxf(M, wml[w][tid][0]);
+            float S = 0.0f;
+            for (int w = 0; w < NW; w++) {
+                const float f = wml[w][tid][0] == -INFINITY ? 0.0f : expf(wml[w][tid][0] - M);
+                wml[w][tid][0] = f;  // combine weight of warp w
+                S = fmaf(f, wml[w][tid][1], S);
+            }
+            mlf[tid][0] = M;
+            mlf[tid][1] = S;
+        }
+        const size_t ps_ = (size_t)HD + 2;
+        for (int g0 = 0; g0 < G; g0 += GH) {
 #pragma unroll
-        for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
-    }
+            for (int g = 0; g < G; g++)
+                if (g >= g0 && g < g0 + GH)
+#pragma unroll
+                    for (int e = 0; e < EPL; e++)
+                        red[((size_t)warp * GH + (g - g0)) * HD + row_elem<EPL>(lane, e)] = acc[g][e];
+            __syncthreads();
+            for (int i = tid; i < GH * HD; i += NW * 32) {
+                const int gg = i / HD, d = i % HD, g = g0 + gg;
+                float o = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NW; w++) o = fmaf(wml[w][g][0], red[((size_t)w * GH + gg) * HD + d], o);
+                float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + sp) * ps_;
+                pr[2 + d] = o;
+                if (d == 0) { pr[0] = mlf[g][0]; pr[1] = mlf[g][1]; }
+            }
+            __syncthreads();
+        }
+    };
     // this lane's score after the transpose sum: row r_l = idx / G, head g_l = idx % G
     const int idx = (lane >> (5 - H)) & (NV - 1), g_l = idx % G, r_l = idx / G;
     for (int j = 0; j < nsub; j++) {
         const int st = j % kStages, cnt = min(kSub, ctot - j * kSub);
+        if ((j * kSub) % span == 0) {  // a new canonical split: fresh softmax state
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                m[g] = -INFINITY;
+                l[g] = 0.0f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
+            }
+        }
         // bounded: on expiry record the status and go on (every thread still reaches the barriers)
         if (!mbar_wait(&full[st], (j / kStages) & 1) && L.err) atomicExch(L.err, G4_ERR_TIMEOUT);
         const float *kb = ring + (size_t)st * 2 * kSub * HD, *vb = kb + kSub * HD;
@@ -551,46 +596,18 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
         }
         __syncthreads();  // stage st consumed by every warp
         if (tid == 0 && j + kStages < nsub) issue(j + kStages);
-    }
-    // combine the NW warp states (the ring is free now)
-    float *red = ring;  // [NW][G][HD]
-    if (lane == 0)
-#pragma unroll
-        for (int g = 0; g < G; g++) { wml[warp][g][0] = m[g]; wml[warp][g][1] = l[g]; }
-#pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int e = 0; e < EPL; e++) red[((size_t)warp * G + g) * HD + row_elem<EPL>(lane, e)] = acc[g][e];
-    __syncthreads();
-    if (tid < G) {
-        float M = -INFINITY;
-        for (int w = 0; w < NW; w++) M = fmaxf(M, wml[w][tid][0]);
-        float S = 0.0f;
-        for (int w = 0; w < NW; w++) {
-            const float f = wml[w][tid][0] == -INFINITY ? 0.0f : expf(wml[w][tid][0] - M);
-            wml[w][tid][0] = f;  // combine weight of warp w
-            S = fmaf(f, wml[w][tid][1], S);
-        }
-        mlf[tid][0] = M;
-        mlf[tid][1] = S;
-    }
-    __syncthreads();
-    const size_t ps_ = (size_t)HD + 2;
-    for (int i = tid; i < G * HD; i += NW * 32) {
-        const int g = i / HD, d = i % HD;
-        float o = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) o = fmaf(wml[w][g][0], red[((size_t)w * G + g) * HD + d], o);
-        float *pr = L.part + (((size_t)b * L.n_heads + (size_t)h * G + g) * L.max_chunks + c) * ps_;
-        pr[2 + d] = o;
-        if (d == 0) { pr[0] = mlf[g][0]; pr[1] = mlf[g][1]; }
+        if (j == nsub - 1)  // the last split of the CTA: the ring is free, all heads at once
+            combine(sp0 + (j * kSub) / span, ring, G);
+        else if (((j + 1) * kSub) % span == 0)  // a split ends, the ring is still streaming: one head at a time
+            combine(sp0 + (j * kSub) / span, wts, 1);
     }
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket = atomicAdd(L.counters + (size_t)b * L.n_kv + h, 1);
     __syncthreads();
-    if (ticket != nsplit - 1) return;
+    if (ticket != ncta - 1) return;
     __threadfence();
+    const size_t ps_ = (size_t)HD + 2;
     // merge: M = max_c m_c; out = sum_c e^(m_c-M) o_c / sum_c e^(m_c-M) l_c
     if (warp < G) {
         const float *base = L.part + ((size_t)b * L.n_heads + (size_t)h * G + warp) * L.max_chunks * ps_;
@@ -623,18 +640,18 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
 }
 
 template <int EPL, int G>
-static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, cudaStream_t st) {
+static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, int per, cudaStream_t st) {
     G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(kStreamWarps * 32), attn_stream_smem<EPL, G>(), st, L,
-                       pos_dev, span));
+                       pos_dev, span, per));
     return G4_OK;
 }
 
 template <int EPL>
-static int launch_stream_g(const AttnLayer &L, int G, dim3 grid, const int *pos_dev, int span, cudaStream_t st) {
+static int launch_stream_g(const AttnLayer &L, int G, dim3 grid, const int *pos_dev, int span, int per, cudaStream_t st) {
     switch (G) {
-    case 1: return launch_stream_eg<EPL, 1>(grid, L, pos_dev, span, st);
-    case 2: return launch_stream_eg<EPL, 2>(grid, L, pos_dev, span, st);
-    case 4: return launch_stream_eg<EPL, 4>(grid, L, pos_dev, span, st);
+    case 1: return launch_stream_eg<EPL, 1>(grid, L, pos_dev, span, per, st);
+    case 2: return launch_stream_eg<EPL, 2>(grid, L, pos_dev, span, per, st);
+    case 4: return launch_stream_eg<EPL, 4>(grid, L, pos_dev, span, per, st);
     default: set_error(G4_ERR_ARG, "attention: GQA group %d unsupported", G); return G4_ERR_ARG;
     }
 }
@@ -697,18 +714,33 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
     dim3 grid(nch, L.n_kv, B);
     int rc;
     if (L.hd <= 256) {
-        // Split length: a fixed number of rows per CTA for each layer kind (by default 128 for a
-        // sliding window, 256 for the global context), never derived from the batch or the cache length.
-        // The float sums of a sequence then follow the same split boundaries whether it is decoded
-        // alone or in a batch, so batched and single-sequence decoding give identical results.
-        // (Both are multiples of kChunk, which keeps the partials within max_chunks.)
-        const int sp = L.split > 0 ? L.split : (L.window > 0 ? 128 : 256);
+        // Split length: a fixed number of rows per canonical split for each layer kind (by default
+        // 64 for a sliding window, 256 for the global context), never derived from the batch or the
+        // cache length.  The float sums of a sequence then follow the same split boundaries whether
+        // it is decoded alone or in a batch, so batched and single-sequence decoding give identical
+        // results.  (Both are multiples of kChunk, which keeps the partials within max_chunks.)
+        // A CTA takes `per` consecutive splits when there are more than four CTAs per SM of them
+        // (sliding layers of a large batch): fewer, longer CTAs, the same per-split arithmetic.
+        const int sp = L.split > 0 ? L.split : (L.window > 0 ? 64 : 256);
         if (sp % kChunk) { set_error(G4_ERR_ARG, "attention: split %d not a multiple of %d", sp, kChunk); return G4_ERR_ARG; }
-        const dim3 g2((span + sp - 1) / sp, L.n_kv, B);
+        static int nsm = 0;
+        if (!nsm) {
+            int dev = 0;
+            G4_CUDA(cudaGetDevice(&dev));
+            G4_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        }
+        const int nsp = (span + sp - 1) / sp;
+        int per = 1;
+        const long ctas1 = (long)nsp * L.n_kv * B, target = 4L * nsm;
+        // a split that ends while the ring still streams is combined one head at a time in the merge
+        // weights' shared memory: kStreamWarps * hd floats must fit in G * kMaxWts
+        if (L.window > 0 && ctas1 > target && kStreamWarps * L.hd <= G * kMaxWts)
+            per = (int)std::min<long>(nsp, (ctas1 + target - 1) / target);
+        const dim3 g2((nsp + per - 1) / per, L.n_kv, B);
         switch (L.hd) {
-        case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, st); break;
-        case 128: rc = launch_stream_g<4>(L, G, g2, pos_dev, sp, st); break;
-        default: rc = launch_stream_g<8>(L, G, g2, pos_dev, sp, st); break;
+        case 64: rc = launch_stream_g<2>(L, G, g2, pos_dev, sp, per, st); break;
+        case 128: rc = launch_stream_g<4>(L, G, g2, pos_dev, sp, per, st); break;
+        default: rc = launch_stream_g<8>(L, G, g2, pos_dev, sp, per, st); break;
         }
         if (rc) return rc;
         G4_LAUNCHED();

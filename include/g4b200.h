@@ -340,7 +340,7 @@ int g4_engine_set_tc_min_batch(g4_engine *e, int min_batch);
 
 /* Rows of the KV window that one CTA of the decode attention takes, for the
  * sliding-window layers and for the global layers (multiples of 32; 0 keeps
- * the default 128 / 256).  Fixed per engine, never derived from the batch, so
+ * the default 64 / 256).  Fixed per engine, never derived from the batch, so
  * a sequence's results do not depend on the batch size; changing it changes
  * the float summation order of attention.  Not part of the reference
  * interface (main.c:1909-1950 has one sequential pass). */
