@@ -399,7 +399,7 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
     return r;
 }
 
-template <int EPL, int G>
+template <int EPL, int G, bool MULTI>
 __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnLayer L, const int *__restrict__ pos_dev, int span,
                                                                       int per) {
     constexpr int HD = EPL * 32, NW = kStreamWarps, RPW = kSub / NW, NV = RPW * G;
@@ -528,9 +528,11 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
     };
     // this lane's score after the transpose sum: row r_l = idx / G, head g_l = idx % G
     const int idx = (lane >> (5 - H)) & (NV - 1), g_l = idx % G, r_l = idx / G;
+    const int spl = MULTI ? span / kSub : nsub;  // sub-chunks per canonical split
+    int jj = 0;                                     // sub-chunk within the current split
     for (int j = 0; j < nsub; j++) {
         const int st = j % kStages, cnt = min(kSub, ctot - j * kSub);
-        if ((j * kSub) % span == 0) {  // a new canonical split: fresh softmax state
+        if (jj == 0) {  // a new canonical split: fresh softmax state
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 m[g] = -INFINITY;
@@ -596,11 +598,13 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
         }
         __syncthreads();  // stage st consumed by every warp
         if (tid == 0 && j + kStages < nsub) issue(j + kStages);
-        if (j == nsub - 1)  // the last split of the CTA: the ring is free, all heads at once
-            combine(sp0 + (j * kSub) / span, ring, G);
-        else if (((j + 1) * kSub) % span == 0)  // a split ends, the ring is still streaming: one head at a time
-            combine(sp0 + (j * kSub) / span, wts, 1);
+        ++jj;
+        if (MULTI && jj == spl && j != nsub - 1) {  // a split ends, the ring still streams: one head at a time
+            combine(sp0 + j / spl, wts, 1);
+            jj = 0;
+        }
     }
+    combine(MULTI ? sp0 + (nsub - 1) / spl : sp0, ring, G);  // the CTA's last split: the ring is free, all heads at once
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket = atomicAdd(L.counters + (size_t)b * L.n_kv + h, 1);
@@ -641,8 +645,12 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
 
 template <int EPL, int G>
 static int launch_stream_eg(dim3 grid, const AttnLayer &L, const int *pos_dev, int span, int per, cudaStream_t st) {
-    G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G>, grid, dim3(kStreamWarps * 32), attn_stream_smem<EPL, G>(), st, L,
-                       pos_dev, span, per));
+    if (per > 1)
+        G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G, true>, grid, dim3(kStreamWarps * 32), attn_stream_smem<EPL, G>(), st,
+                           L, pos_dev, span, per));
+    else
+        G4_CUDA(launch_pdl(attn_stream_kernel<EPL, G, false>, grid, dim3(kStreamWarps * 32), attn_stream_smem<EPL, G>(), st,
+                           L, pos_dev, span, per));
     return G4_OK;
 }
 
@@ -768,7 +776,9 @@ static int prime_one() {
 }
 template <int EPL, int G>
 static int prime_stream() {
-    G4_CUDA(cudaFuncSetAttribute(attn_stream_kernel<EPL, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    G4_CUDA(cudaFuncSetAttribute(attn_stream_kernel<EPL, G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attn_stream_smem<EPL, G>()));
+    G4_CUDA(cudaFuncSetAttribute(attn_stream_kernel<EPL, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)attn_stream_smem<EPL, G>()));
     return G4_OK;
 }
