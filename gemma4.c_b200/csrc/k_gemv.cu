@@ -44,15 +44,66 @@ __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp
 
 // ---------------------------------------------------------------- dense GEMV
 
-// One warp per row; x staged in shared memory as fp32.  Epilogues: plain
-// store, or GELU(acc) * evec[row] (the PLE gate, main.c:1986-1991).
+// Canonical order of a dense row dot (every dense kernel, any batch): the row is cut into chunks
+// of kDenseChunk elements; in a chunk each lane runs an fmaf chain over its elements in order
+// (vectors of 8 (16-bit weights) / 4 (fp32) at lane stride), the 32 lane sums are added by the
+// warp_sum butterfly, and the chunk sums are added in chunk order, (0 + C0) + C1 + ...
+constexpr int kDenseChunk = 512;
+constexpr int kDenseMaxSlots = 128;  // chunk sums of one CTA (rows per CTA x chunks)
+
+// Lane chain of chunk c of one row (weights r, activation xs in shared memory).
+__device__ __forceinline__ float dense_chunk(const void *r, int type, int n, const float *xs, int c, int lane) {
+    float acc = 0.0f;
+    const int j0 = c * kDenseChunk, j1 = min(n, j0 + kDenseChunk);
+    const bool vec = (n % 8) == 0;
+    if (type == G4_F32) {
+        const float *rf = (const float *)r;
+        if (vec) {
+#pragma unroll 4
+            for (int j = j0 + lane * 4; j < j1; j += 128) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(rf + j));
+                acc = fmaf(a.x, xs[j], acc); acc = fmaf(a.y, xs[j + 1], acc);
+                acc = fmaf(a.z, xs[j + 2], acc); acc = fmaf(a.w, xs[j + 3], acc);
+            }
+        } else {
+            for (int j = j0 + lane; j < j1; j += 32) acc = fmaf(__ldg(rf + j), xs[j], acc);
+        }
+    } else {
+        const uint16_t *rh = (const uint16_t *)r;
+        const bool bf = type == G4_BF16;
+        if (vec) {
+#pragma unroll 2
+            for (int j = j0 + lane * 8; j < j1; j += 256) {
+                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(rh + j));
+                const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint16_t l = (uint16_t)(ww[i] & 0xffffu), h = (uint16_t)(ww[i] >> 16);
+                    acc = fmaf(xs[j + 2 * i], bf ? bf16_to_f32(l) : f16_to_f32(l), acc);
+                    acc = fmaf(xs[j + 2 * i + 1], bf ? bf16_to_f32(h) : f16_to_f32(h), acc);
+                }
+            }
+        } else {
+            for (int j = j0 + lane; j < j1; j += 32) {
+                const uint16_t v = __ldg(rh + j);
+                acc = fmaf(xs[j], bf ? bf16_to_f32(v) : f16_to_f32(v), acc);
+            }
+        }
+    }
+    return warp_sum(acc);
+}
+
+// One sequence per blockIdx.y; a CTA takes rpc rows, a warp one (row, chunk) at a time (so a long
+// row keeps several warps busy); x staged in shared memory as fp32.  Epilogues: plain store, or
+// GELU(acc) * evec[row] (the PLE gate, main.c:1986-1991).
 __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                          const float *__restrict__ x, int ldx,
                                                          float *__restrict__ out, int ldo, int epi,
                                                          const float *__restrict__ evec, int ld_evec, Prologue pro,
-                                                         int has_pro, int pro_writer) {
+                                                         int has_pro, int pro_writer, int rpc) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ float pred[8];
+    __shared__ float csum[kDenseMaxSlots];
     pdl_trigger();
     pdl_wait();
     float *xs = (float *)smem_raw;
@@ -69,49 +120,24 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const void *__restrict_
         for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[(size_t)s * ldx + i];
         __syncthreads();
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (row >= rows) return;
-    float acc = 0.0f;
-    const bool vec = (n % 8) == 0;
-    if (type == G4_F32) {
-        const float *r = (const float *)w + (size_t)row * n;
-        if (vec) {
-#pragma unroll 5
-            for (int j = lane * 4; j < n; j += 128) {
-                const float4 a = __ldg(reinterpret_cast<const float4 *>(r + j));
-                acc = fmaf(a.x, xs[j], acc); acc = fmaf(a.y, xs[j + 1], acc);
-                acc = fmaf(a.z, xs[j + 2], acc); acc = fmaf(a.w, xs[j + 3], acc);
-            }
-        } else {
-            for (int j = lane; j < n; j += 32) acc = fmaf(__ldg(r + j), xs[j], acc);
-        }
-    } else {
-        const uint16_t *r = (const uint16_t *)w + (size_t)row * n;
-        const bool bf = type == G4_BF16;
-        if (vec) {
-#pragma unroll 5
-            for (int j = lane * 8; j < n; j += 256) {
-                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + j));
-                const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint16_t l = (uint16_t)(ww[i] & 0xffffu), h = (uint16_t)(ww[i] >> 16);
-                    acc = fmaf(xs[j + 2 * i], bf ? bf16_to_f32(l) : f16_to_f32(l), acc);
-                    acc = fmaf(xs[j + 2 * i + 1], bf ? bf16_to_f32(h) : f16_to_f32(h), acc);
-                }
-            }
-        } else {
-            for (int j = lane; j < n; j += 32) {
-                const uint16_t v = __ldg(r + j);
-                acc = fmaf(xs[j], bf ? bf16_to_f32(v) : f16_to_f32(v), acc);
-            }
-        }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int S = (n + kDenseChunk - 1) / kDenseChunk, row0 = blockIdx.x * rpc;
+    const size_t rb = (size_t)n * (type == G4_F32 ? 4 : 2);
+    for (int u = warp; u < rpc * S; u += nw) {
+        const int rr = u / S, c = u % S, row = row0 + rr;
+        if (row >= rows) continue;
+        const float v = dense_chunk((const uint8_t *)w + (size_t)row * rb, type, n, xs, c, lane);
+        if (lane == 0) csum[u] = v;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) {
-        if (epi == EPI_GELU_SCALE) acc = gelu_f32(acc) * evec[(size_t)s * ld_evec + row];
-        out[(size_t)s * ldo + row] = acc;
+    __syncthreads();
+    if ((int)threadIdx.x < rpc) {
+        const int row = row0 + threadIdx.x;
+        if (row < rows) {
+            float acc = 0.0f;
+            for (int c = 0; c < S; c++) acc = __fadd_rn(acc, csum[threadIdx.x * S + c]);
+            if (epi == EPI_GELU_SCALE) acc = gelu_f32(acc) * evec[(size_t)s * ld_evec + row];
+            out[(size_t)s * ldo + row] = acc;
+        }
     }
 }
 
@@ -146,9 +172,9 @@ __device__ __forceinline__ float warp_sum_many(float (&v)[NV], int lane) {
 // shared memory once per CTA, and each warp works on RW rows at a time, so an
 // activation value read from shared memory serves RW rows and a weight value
 // read from memory serves NS sequences.  The CTAs loop over the rows.  Every
-// accumulator (row, sequence) sees exactly the operation order of
-// gemv_dense_kernel (lane-strided fmaf chain, then the warp_sum butterfly), so
-// the result of a sequence does not depend on the batch.
+// (row, sequence) follows the canonical chunked order of gemv_dense_kernel
+// (lane-strided fmaf chains per chunk, the warp_sum butterfly, chunk sums in
+// order), so the result of a sequence does not depend on the batch.
 template <int NS, int RW>
 __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                             const float *__restrict__ x, int ldx, int B,
@@ -184,17 +210,22 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool vec = (n % 8) == 0, f32 = type == G4_F32, bf = type == G4_BF16;
+    constexpr int NV = RW * NS, LPV = 32 / NV;
+    const int S = (n + kDenseChunk - 1) / kDenseChunk;
     for (int row0 = (blockIdx.x * (blockDim.x >> 5) + warp) * RW; row0 < rows; row0 += gridDim.x * (blockDim.x >> 5) * RW) {
+        int rr[RW];  // rows past the end repeat the last row (computed, not stored)
+#pragma unroll
+        for (int r = 0; r < RW; r++) rr[r] = min(row0 + r, rows - 1);
+        float vt = 0.0f;  // this lane's value (index lane / LPV): the chunk sums in chunk order
+        for (int c = 0; c < S; c++) {
+        const int j0 = c * kDenseChunk, j1 = min(n, j0 + kDenseChunk);
         float acc[RW][NS];
 #pragma unroll
         for (int r = 0; r < RW; r++)
 #pragma unroll
             for (int s = 0; s < NS; s++) acc[r][s] = 0.0f;
-        int rr[RW];  // rows past the end repeat the last row (computed, not stored)
-#pragma unroll
-        for (int r = 0; r < RW; r++) rr[r] = min(row0 + r, rows - 1);
         if (f32 && vec) {
-            for (int j = lane * 4; j < n; j += 128) {
+            for (int j = j0 + lane * 4; j < j1; j += 128) {
                 float4 a[RW];
 #pragma unroll
                 for (int r = 0; r < RW; r++) a[r] = __ldg(reinterpret_cast<const float4 *>((const float *)w + (size_t)rr[r] * n + j));
@@ -210,7 +241,7 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
                 }
             }
         } else if (f32) {
-            for (int j = lane; j < n; j += 32) {
+            for (int j = j0 + lane; j < j1; j += 32) {
                 float a[RW];
 #pragma unroll
                 for (int r = 0; r < RW; r++) a[r] = __ldg((const float *)w + (size_t)rr[r] * n + j);
@@ -223,7 +254,7 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
             }
         } else if (vec) {
 #pragma unroll 2
-            for (int j = lane * 8; j < n; j += 256) {
+            for (int j = j0 + lane * 8; j < j1; j += 256) {
                 float wf[RW][8];
 #pragma unroll
                 for (int r = 0; r < RW; r++) {
@@ -250,7 +281,7 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
                 }
             }
         } else {
-            for (int j = lane; j < n; j += 32) {
+            for (int j = j0 + lane; j < j1; j += 32) {
                 float wv[RW];
 #pragma unroll
                 for (int r = 0; r < RW; r++) {
@@ -265,14 +296,15 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
                 }
             }
         }
-        // totals: value index r * NS + s, one per lane group of 32 / (RW * NS) lanes
+        // chunk totals: value index r * NS + s, one per lane group of 32 / (RW * NS) lanes
         float flat[RW * NS];
 #pragma unroll
         for (int r = 0; r < RW; r++)
 #pragma unroll
             for (int s = 0; s < NS; s++) flat[r * NS + s] = acc[r][s];
-        constexpr int NV = RW * NS, LPV = 32 / NV;
-        const float tot = warp_sum_many<NV>(flat, lane);
+        vt = __fadd_rn(vt, warp_sum_many<NV>(flat, lane));
+        }
+        const float tot = vt;
         if ((lane & (LPV - 1)) == 0) {
             const int idx = lane / LPV, r = idx / NS, s = idx % NS, row = row0 + r;
             if (row < rows && s < ns) {
@@ -330,8 +362,13 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
     if (pro && pro->dim != n) { set_error(G4_ERR_ARG, "gemv_dense: prologue dim %d != n %d", pro->dim, n); return G4_ERR_ARG; }
     Prologue P{};
     if (pro) P = *pro;
-    G4_CUDA(launch_pdl(gemv_dense_kernel, dim3((rows + 7) / 8, B), dim3(256), smem, st, w, type, n, rows, x, ldx, out,
-                       ldo, epi, evec, ld_evec, P, pro ? 1 : 0, pro_writer));
+    // rows per CTA: every warp busy on short rows; at most about four CTAs per SM on tall matrices
+    const int S = (n + kDenseChunk - 1) / kDenseChunk, nsm = g_tm_sms_dense > 0 ? g_tm_sms_dense : 148;
+    int rpc = std::max(S >= 8 ? 1 : 8 / S, (rows + 4 * nsm - 1) / (4 * nsm));
+    rpc = std::min(rpc, std::max(1, kDenseMaxSlots / S));
+    if (rpc * S > kDenseMaxSlots) { set_error(G4_ERR_ARG, "gemv_dense: n=%d too large", n); return G4_ERR_ARG; }
+    G4_CUDA(launch_pdl(gemv_dense_kernel, dim3((rows + rpc - 1) / rpc, B), dim3(256), smem, st, w, type, n, rows, x, ldx,
+                       out, ldo, epi, evec, ld_evec, P, pro ? 1 : 0, pro_writer, rpc));
     G4_LAUNCHED();
     return G4_OK;
 }
