@@ -26,6 +26,8 @@
 // CTA returns instead of hanging the GPU.
 #include <math.h>
 
+#include <algorithm>
+
 #include "g4_async.cuh"
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
@@ -663,7 +665,7 @@ static void tm_launch_r(GemvJobs &jobs, int ctas, size_t smem, int B, const TmPl
 }
 
 template <int TYPE>
-static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st) {
+static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st, int tr_cap) {
     const GemvJob &J0 = jobs.j[0];
     const int n = J0.n, nb = n / G4_QK, R = J0.w2 ? 2 : 1;
     for (int i = 1; i < jobs.njobs; i++)
@@ -683,7 +685,7 @@ static int tm_dispatch(GemvJobs &jobs, int ctas, int B, cudaStream_t st) {
     plan.term_warp = (int)((size_t)(4 / plan.gpr) * R * nb * nbs * sizeof(float2));
     plan.act_bytes = (int)((tm_act_bytes<TYPE>(nbs, n, pro, plan.gpr, R) + 127) & ~(size_t)127);
     // rows per tile: one row per GPR groups, at most what lets >= 3 stages fit
-    int tr = kTmGroups / plan.gpr;
+    int tr = std::min(kTmGroups / plan.gpr, tr_cap);
     const int fit = (kTmSmemBudget - plan.act_bytes) / (3 * R * plan.row_bytes);
     if (tr > fit) tr = fit > 1 ? fit : 1;
     plan.tr = tr;
@@ -777,7 +779,7 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
     }
     long total_work = 0;
     for (int i = 0; i < jobs.njobs; i++) total_work += (long)jobs.j[i].rows * (jobs.j[i].n / G4_QK);
-    int ctas = 0;
+    int ctas = 0, tr_cap = kTmGroups;
     for (int i = 0; i < jobs.njobs; i++) {
         GemvJob &J = jobs.j[i];
         if (J.type != type) { set_error(G4_ERR_ARG, "gemv: one launch takes one tensor type"); return G4_ERR_ARG; }
@@ -810,7 +812,13 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
         // persistent CTAs (1 per SM) shared out in proportion to the job's bytes
         const int nbj = J.n / G4_QK;
         const int gpr = nbj <= 6 ? 1 : nbj <= 12 ? 2 : 4;
-        const long tiles = (J.rows + kTmGroups / gpr - 1) / (kTmGroups / gpr);
+        // rows per tile: a single small matrix gets smaller tiles, so that about half of the SMs
+        // (or more) stream it instead of a few (fewer lane groups per tile, more tiles in flight)
+        int trj = kTmGroups / gpr;
+        if (jobs.njobs == 1)
+            while (trj > 1 && (J.rows + trj - 1) / trj < g_tm_sms / 2) trj /= 2;
+        tr_cap = std::min(tr_cap, trj);
+        const long tiles = (J.rows + trj - 1) / trj;
         long cj = ((long)g_tm_sms * J.rows * nbj + total_work - 1) / total_work;
         if (cj > tiles) cj = tiles;
         if (cj < 1) cj = 1;
@@ -828,9 +836,9 @@ int launch_gemv_kquant(GemvJobs &jobs, int B, cudaStream_t st) {
     }
     int rc;
     switch (type) {
-    case G4_Q4_K: rc = tm_dispatch<G4_Q4_K>(jobs, ctas, B, st); break;
-    case G4_Q5_K: rc = tm_dispatch<G4_Q5_K>(jobs, ctas, B, st); break;
-    default: rc = tm_dispatch<G4_Q6_K>(jobs, ctas, B, st); break;
+    case G4_Q4_K: rc = tm_dispatch<G4_Q4_K>(jobs, ctas, B, st, tr_cap); break;
+    case G4_Q5_K: rc = tm_dispatch<G4_Q5_K>(jobs, ctas, B, st, tr_cap); break;
+    default: rc = tm_dispatch<G4_Q6_K>(jobs, ctas, B, st, tr_cap); break;
     }
     if (rc) return rc;
     G4_LAUNCHED();
