@@ -521,13 +521,23 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
             if (A.append) TRY(launch_kv_append(A, B, e->st));
             A.append = 0;
             TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
-        } else {
-            TRY(launch_attention(attn_args(e, l), B, e->d_pos, e->max_seq, e->st));
+        }
+        // the merging attention CTAs quantize qo into the Q4_K output projection's operand
+        const bool o_fused = !prefill && use_tc(e, B, ly.wo_t, EPI_STORE) && ly.wo_t == G4_Q4_K && B <= 64 &&
+                             ly.hd <= 256 && ((e->nh / e->nkv) * ly.hd) % G4_QK == 0;
+        if (!prefill) {
+            AttnLayer A = attn_args(e, l);
+            if (o_fused) {
+                A.op_bq = e->tcq;
+                A.op_yd = (float *)(e->tcq + tc_yd_offset(ly.qd));
+                A.op_np = tc_np(B);
+            }
+            TRY(launch_attention(A, B, e->d_pos, e->max_seq, e->st));
         }
 
         // output projection + post-attention norm + residual, FFN pre-norm (1959-1975)
         if (use_tc(e, B, ly.wo_t, EPI_STORE))
-            TRY(tc_gemm(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
+            TRY(tc_gemm(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, o_fused, e->o_raw, dim, B));
         else
             TRY(gemv(e, ly.wo, ly.wo_t, ly.qd, dim, e->qo, ly.qd, false, e->o_raw, dim, B));
         const bool tc_ffn = use_tc(e, B, ly.gate_t, EPI_STORE) && use_tc(e, B, ly.up_t, EPI_STORE);

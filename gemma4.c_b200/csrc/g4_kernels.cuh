@@ -99,6 +99,9 @@ struct AttnLayer {
     float *part;                    // scratch [B][n_heads][max_chunks][hd+2]
     int *counters;                  // [B][n_kv] zero-initialised tickets
     int max_chunks;
+    uint8_t *op_bq;                 // tensor-core operand of qo for a Q4_K output projection (tc4_store_q8
+    float *op_yd;                   // layout, one group of op_np <= 64 sequences), written by the merging
+    int op_np;                      // CTAs; null: not written
     int split;                      // rows per canonical split of attn_stream_kernel (a multiple of 32);
                                     // 0: 64 for a sliding window, 256 otherwise
     int early;                      // 1: every cache row but `pos` was written before the launch's

@@ -27,6 +27,8 @@
 #include "g4_async.cuh"
 #include "g4_internal.cuh"
 #include "g4_kernels.cuh"
+#include "g4_quant.cuh"
+#include "g4_tc.cuh"
 
 namespace g4 {
 
@@ -638,9 +640,22 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
             const float wgt = cc < kMaxWts ? wts[g * kMaxWts + cc] : expf(__ldcg(base + cc * ps_) - mlf[g][0]);
             o = fmaf(wgt, __ldcg(base + cc * ps_ + 2 + d), o);
         }
-        L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = o * mlf[g][1];
+        const float y = o * mlf[g][1];
+        L.qo[(size_t)b * qd + (size_t)(h * G + g) * HD + d] = y;
+        if (L.op_bq) ring[i] = y;
     }
     if (tid == 0) L.counters[(size_t)b * L.n_kv + h] = 0;  // ready for the next launch
+    if (L.op_bq) {  // the Q8_K blocks of these G heads for the output projection (as tc4_quant_kernel)
+        __syncthreads();
+        for (int w = warp; w < G * HD / G4_QK; w += NW) {
+            const int kb = (h * G * HD) / G4_QK + w;
+            uint32_t q[2];
+            float d;
+            int ls;
+            warp_quant_block(ring + w * G4_QK, lane, q, d, ls);
+            tc4_store_q8(L.op_bq + (size_t)kb * 544 * L.op_np, L.op_yd + (size_t)kb * L.op_np, L.op_np, b, lane, q, d, ls);
+        }
+    }
 }
 
 template <int EPL, int G>
