@@ -30,8 +30,10 @@
 // warp 1 owns TMEM and one lane issues the MMAs; warps 2..9 expand the raw
 // weight tile into the A operands (core-matrix layout, no swizzle) and run the
 // epilogue of the previous super-block.  Work units are (128-row tile,
-// K-slice); the slices of a tile leave fp32 partials that tc_merge_kernel
-// sums in slice order (Q4_K: stream-K units, summed by sk_merge_kernel).
+// K-slice); the slices of a tile leave fp32 partials that are summed in slice
+// order: inside the GEMM by the CTA that completes the tile when the caller
+// passes tickets (the engine), else by tc_merge_kernel / sk_merge_kernel
+// (Q4_K: stream-K units).
 //
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // G4_ERR_TIMEOUT in *err, the producer waits for its copies in flight, the
@@ -766,7 +768,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1) gemm_q4tc_kernel(const __grid_c
         };
         // End of this CTA's units of row tile t.  A tile wholly inside this CTA is stored (unless
         // a.all_part); a tile shared by several CTAs leaves its partial in slot (CTA - first CTA of
-        // the tile), and sk_merge_kernel sums the slots in slot order.
+        // the tile), and the slots are summed in slot order: by the CTA that completes the tile (tickets)
+        // or by sk_merge_kernel.
         auto finish = [&](int t) {
             const bool m2 = t >= a.tiles0;
             const int row = (m2 ? t - a.tiles0 : t) * 128 + r;

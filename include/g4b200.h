@@ -168,9 +168,10 @@ int g4d_mm(float *o, const float *x, const void *w, int n, int d, int type, g4_b
 /* K-quant and BF16 matrices with batch >= the tensor-core threshold (default
  * 16) run as tcgen05 GEMMs over groups of up to 64 activations: Q4_K as exact
  * fp16 integer products, Q5_K as int8 x int8 -> int32 (both with exact
- * integer block sums and an fp32 block epilogue), Q6_K and BF16 on
- * activations split into fp16 / bf16 parts; smaller batches use the
- * streaming GEMV.  The tensor-core path keeps a per-device scratch
+ * integer block sums and an fp32 block epilogue), Q6_K as int8 x int8 ->
+ * int32 on the activation's three fixed-point pieces (exact block dots), BF16
+ * on activations split into three bf16 parts; smaller batches use the
+ * streaming GEMV (bit-identical to the tensor-core results for the K-quants).  The tensor-core path keeps a per-device scratch
  * (activation operand, K-slice partials) shared by all calls: calls on
  * different streams must be ordered by the caller.  Not part of the
  * reference interface: sets the threshold (>= 1) and returns the previous
