@@ -440,6 +440,9 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         TRY(gemv(e, e->ple_proj, e->ple_proj_t, dim, pd * L, e->x, dim, false, e->ple_ctx, pd * L, B));
     TRY(launch_ple_mix(e->ple_tokb, e->ple_ctx, e->ple_proj_norm, pd, L, e->ctx_scale, e->mix_scale, e->eps, e->ple,
                        B, e->st));
+    // The residual stream lives in e->x, except between a per-layer-embedding gate GEMV that folded
+    // the post-FFN residual into its prologue (it writes e->x2) and the next residual/norm launch.
+    const float *xres = e->x;
     for (int l = 0; l < L; l++) {
         const LayerDev &ly = e->layers[l];
         const LayerDev *prev = l > 0 ? &e->layers[l - 1] : nullptr;
@@ -447,7 +450,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         const bool tcq_l = use_tc(e, B, ly.wq_t, EPI_STORE);  // projections of this layer on the tensor cores
         const bool q8_in = !tcq_l && (is_q8_type(ly.wq_t) || (has_kv && (is_q8_type(ly.wk_t) || is_q8_type(ly.wv_t))));
         ResNorm r{};
-        r.x_in = e->x; r.delta = prev ? e->p_raw : nullptr; r.post_w = prev ? prev->post_norm : nullptr;
+        r.x_in = xres; r.delta = prev ? e->p_raw : nullptr; r.post_w = prev ? prev->post_norm : nullptr;
         r.scale = prev ? prev->out_scale : nullptr; r.x_out = e->x; r.pre_w = ly.attn_norm; r.xn_out = e->xn;
         r.q8_out = q8_in ? e->q8 : nullptr; r.dim = dim; r.eps = e->eps;
         // operands of xn for the Q (Q4_K) and V (Q6_K) tensor-core GEMMs, written by this launch
@@ -458,6 +461,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
                      attach_operand(e, r, B, G4_Q6_K, dim);
         }
         TRY(launch_resnorm(r, B, e->st));
+        xres = e->x;
 
         // Q / K / V projections (main.c:1884-1891): one launch per tensor type
         struct Proj { const void *w; int t; int rows; float *out; };
@@ -581,15 +585,26 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
         r3.x_in = e->x; r3.delta = e->d_raw; r3.post_w = ly.post_ffw_norm; r3.x_out = e->x; r3.dim = dim;
         r3.eps = e->eps;
         const bool tc_gate = use_tc(e, B, ly.inp_gate_t, EPI_GELU_SCALE) && (ly.inp_gate_t != G4_BF16 || dim % 64 == 0);
-        const bool gate_ready = tc_gate && attach_operand(e, r3, B, ly.inp_gate_t, dim);
-        TRY(launch_resnorm(r3, B, e->st));
+        const bool dense_gate = ly.inp_gate_t == G4_F32 || ly.inp_gate_t == G4_F16 || ly.inp_gate_t == G4_BF16;
         // per-layer embedding injection (1986-1997)
-        if (tc_gate)
-            TRY(tc_gemm(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, gate_ready, e->g, pd, B, EPI_GELU_SCALE, nullptr,
-                        0.0f, e->ple + (size_t)l * pd, pd * L));
-        else
-            TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
-                     e->ple + (size_t)l * pd, pd * L));
+        if (!tc_gate && dense_gate) {
+            // the dense gate GEMV computes x + rmsnorm(down)*w itself (each CTA for its sequences, one
+            // CTA per group writes it to e->x2): no separate residual launch
+            Prologue P{};
+            P.x_in = e->x; P.delta = e->d_raw; P.post_w = ly.post_ffw_norm; P.x_out = e->x2; P.dim = dim; P.eps = e->eps;
+            TRY(launch_gemv_dense(ly.inp_gate, ly.inp_gate_t, dim, pd, e->x2, dim, e->g, pd, B, EPI_GELU_SCALE,
+                                  e->ple + (size_t)l * pd, pd * L, e->st, &P, 1));
+            xres = e->x2;
+        } else {
+            const bool gate_ready = tc_gate && attach_operand(e, r3, B, ly.inp_gate_t, dim);
+            TRY(launch_resnorm(r3, B, e->st));
+            if (tc_gate)
+                TRY(tc_gemm(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, gate_ready, e->g, pd, B, EPI_GELU_SCALE,
+                            nullptr, 0.0f, e->ple + (size_t)l * pd, pd * L));
+            else
+                TRY(gemv(e, ly.inp_gate, ly.inp_gate_t, dim, pd, e->x, dim, false, e->g, pd, B, EPI_GELU_SCALE,
+                         e->ple + (size_t)l * pd, pd * L));
+        }
         if (use_tc(e, B, ly.proj_t, EPI_STORE) && (ly.proj_t != G4_BF16 || pd % 64 == 0))
             TRY(tc_gemm(e, ly.proj, ly.proj_t, pd, dim, e->g, pd, false, e->p_raw, dim, B));
         else
@@ -598,7 +613,7 @@ int enqueue_step_unfused(g4_engine *e, int B, int lm_mode, bool from_keys, bool 
     // last residual + out_scale (1995-2003), output norm (2021)
     const LayerDev &last = e->layers[L - 1];
     ResNorm rf{};
-    rf.x_in = e->x; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = e->x;
+    rf.x_in = xres; rf.delta = e->p_raw; rf.post_w = last.post_norm; rf.scale = last.out_scale; rf.x_out = e->x;
     rf.pre_w = lm_mode ? e->norm_out : nullptr; rf.xn_out = e->xf; rf.dim = dim; rf.eps = e->eps;
     const bool tc_head = lm_mode && !e->comm && use_tc(e, B, e->embd_t, EPI_SOFTCAP_ARGMAX);
     const bool head_ready = tc_head && attach_operand(e, rf, B, e->embd_t, dim);

@@ -179,13 +179,23 @@ template <int NS, int RW>
 __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                             const float *__restrict__ x, int ldx, int B,
                                                             float *__restrict__ out, int ldo, int epi,
-                                                            const float *__restrict__ evec, int ld_evec) {
+                                                            const float *__restrict__ evec, int ld_evec, Prologue pro,
+                                                            int has_pro, int pro_writer) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ float pred[8];
     pdl_trigger();
     pdl_wait();
     float *xs = (float *)smem_raw;  // [NS][n]
     const int s0 = blockIdx.y * NS, ns = min(NS, B - s0);
-    if ((n % 4) == 0 && (ldx % 4) == 0) {  // 16-byte loads, 8 in flight per thread
+    if (has_pro) {  // x' = x + rmsnorm(delta)*w of this CTA's sequences (the residual glue of the batched step)
+        Prologue P = pro;
+        P.x_in += (size_t)s0 * P.dim;
+        if (P.delta) P.delta += (size_t)s0 * P.dim;
+        if (P.x_out) P.x_out += (size_t)s0 * P.dim;
+        if (P.xn_out) P.xn_out += (size_t)s0 * P.dim;
+        if (prologue_reg_ok(P)) prologue_run_reg<10>(P, ns, xs, pro_writer && blockIdx.x == 0, pred);
+        else prologue_run(P, ns, xs, nullptr, pro_writer && blockIdx.x == 0, pred);
+    } else if ((n % 4) == 0 && (ldx % 4) == 0) {  // 16-byte loads, 8 in flight per thread
         const int n4 = n / 4, tot = ns * n4;
         for (int i0 = threadIdx.x; i0 < tot; i0 += 8 * blockDim.x) {
             float4 v[8];
@@ -319,7 +329,9 @@ __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__res
 int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, int ldx, float *out, int ldo,
                       int B, int epi, const float *evec, int ld_evec, cudaStream_t st, const Prologue *pro,
                       int pro_writer) {
-    if (!pro && B > 1 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0) {
+    if (B > 1 && (type == G4_F32 || type == G4_F16 || type == G4_BF16) && rows > 0 && n > 0 && (!pro || pro->dim == n)) {
+        Prologue P{};
+        if (pro) P = *pro;
         const size_t per = (size_t)n * 4;
         // NS sequences per CTA (<= 100 KB of staged activations: two CTAs per SM), RW rows per warp
         int NS = per * 8 <= 100 * 1024 ? 8 : per * 4 <= 100 * 1024 ? 4 : per * 2 <= 100 * 1024 ? 2 : 0;
@@ -343,7 +355,7 @@ int launch_gemv_dense(const void *w, int type, int n, int rows, const float *x, 
 #define G4_DMS(NSV, RWV)                                                                                          \
     if (NS == NSV && RW == RWV)                                                                                    \
         G4_CUDA(launch_pdl(gemv_dense_ms_kernel<NSV, RWV>, grid, dim3(256), per * NSV, st, w, type, n, rows, x, ldx, \
-                           B, out, ldo, epi, evec, ld_evec));
+                           B, out, ldo, epi, evec, ld_evec, P, pro ? 1 : 0, pro_writer));
             G4_DMS(8, 4) else G4_DMS(8, 2) else G4_DMS(8, 1)
             else G4_DMS(4, 8) else G4_DMS(4, 4) else G4_DMS(4, 2) else G4_DMS(4, 1)
             else G4_DMS(2, 8) else G4_DMS(2, 4) else G4_DMS(2, 2) else G4_DMS(2, 1)
