@@ -406,6 +406,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
                                                                       int per) {
     constexpr int HD = EPL * 32, NW = kStreamWarps, RPW = kSub / NW, NV = RPW * G;
     static_assert(RPW == 2, "two rows per warp and sub-chunk: rows differ in lane bit 4 after the transpose sum");
+    static_assert(NW * G <= 2 * kSub, "a split's warp states fit in one ring stage");
     constexpr int H = NV == 2 ? 1 : NV == 4 ? 2 : 3;  // log2(NV)
     extern __shared__ __align__(16) float dsm[];
     float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(dsm);  // [G][HD]
@@ -599,11 +600,18 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2) attn_stream_kernel(AttnL
             }
         }
         __syncthreads();  // stage st consumed by every warp
-        if (tid == 0 && j + kStages < nsub) issue(j + kStages);
         ++jj;
-        if (MULTI && jj == spl && j != nsub - 1) {  // a split ends, the ring still streams: one head at a time
-            combine(sp0 + j / spl, wts, 1);
+        if (MULTI && jj == spl && j != nsub - 1) {
+            // a split ends while the ring still streams: its warp states are combined in stage st
+            // (NW * G * HD floats <= 2 * kSub * HD for G <= 4), whose next copy waits until then
+            combine(sp0 + j / spl, ring + (size_t)st * 2 * kSub * HD, G);
             jj = 0;
+            if (tid == 0 && j + kStages < nsub) {
+                fence_proxy_async_smem();  // the combine's shared stores before the copy's writes
+                issue(j + kStages);
+            }
+        } else if (tid == 0 && j + kStages < nsub) {
+            issue(j + kStages);
         }
     }
     combine(MULTI ? sp0 + (nsub - 1) / spl : sp0, ring, G);  // the CTA's last split: the ring is free, all heads at once
@@ -742,8 +750,8 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
         // cache length.  The float sums of a sequence then follow the same split boundaries whether
         // it is decoded alone or in a batch, so batched and single-sequence decoding give identical
         // results.  (Both are multiples of kChunk, which keeps the partials within max_chunks.)
-        // A CTA takes `per` consecutive splits when there are more than four CTAs per SM of them
-        // (sliding layers of a large batch): fewer, longer CTAs, the same per-split arithmetic.
+        // A CTA takes `per` consecutive splits when there are more than two CTAs per SM of them
+        // (sliding layers of a large batch): one wave of longer CTAs, the same per-split arithmetic.
         const int sp = L.split > 0 ? L.split : (L.window > 0 ? 64 : 256);
         if (sp % kChunk) { set_error(G4_ERR_ARG, "attention: split %d not a multiple of %d", sp, kChunk); return G4_ERR_ARG; }
         static int nsm = 0;
@@ -754,10 +762,8 @@ int launch_attention(const AttnLayer &L, int B, const int *pos_dev, int max_seq,
         }
         const int nsp = (span + sp - 1) / sp;
         int per = 1;
-        const long ctas1 = (long)nsp * L.n_kv * B, target = 4L * nsm;
-        // a split that ends while the ring still streams is combined one head at a time in the merge
-        // weights' shared memory: kStreamWarps * hd floats must fit in G * kMaxWts
-        if (L.window > 0 && ctas1 > target && kStreamWarps * L.hd <= G * kMaxWts)
+        const long ctas1 = (long)nsp * L.n_kv * B, target = 2L * nsm;
+        if (L.window > 0 && ctas1 > target)
             per = (int)std::min<long>(nsp, (ctas1 + target - 1) / target);
         const dim3 g2((nsp + per - 1) / per, L.n_kv, B);
         switch (L.hd) {

@@ -109,17 +109,20 @@ def test_tc_batched_64_sequences_bitwise(g4, gpu, tiny, B):
 
 
 def test_e4b_batch_invariance_at_long_context(g4, gpu):
-    """The benchmarked shape (E4B, Q4_K_M) at context 516: 16 sequences with
-    different cached rows decoded in one batched step equal each sequence
-    decoded alone from the same cache: hidden state, K/V rows of every KV
-    layer and the greedy token, bit for bit."""
+    """The benchmarked shape (E4B, Q4_K_M) at context 516: 40 sequences
+    (eight different caches, every sequence its own token) decoded in one
+    batched step equal each sequence decoded alone from the same cache:
+    hidden state, K/V rows of every KV layer and the greedy token, bit for
+    bit.  At 40 sequences a sliding-window layer has more 64-row splits than
+    two CTAs per SM, so its CTAs take several consecutive splits each, while
+    the single-sequence decode gives every split its own CTA."""
     S = g4.synth
     shape = S.E4B
     m = S.make_model(shape, seed=3)
-    B, ctx = 16, 516
+    B, ctx, ncache = 40, 516, 8
     rng = np.random.default_rng(17)
     caches = []
-    for b in range(B):
+    for b in range(ncache):
         per = []
         for l in range(24):
             hd = shape.head_dim_swa if S.is_swa(shape, l) else shape.head_dim_full
@@ -132,7 +135,7 @@ def test_e4b_batch_invariance_at_long_context(g4, gpu):
     try:
         for b in range(B):
             for l in range(24):
-                eb.set_kv(l, 0, caches[b][l][0], caches[b][l][1], b=b)
+                eb.set_kv(l, 0, caches[b % ncache][l][0], caches[b % ncache][l][1], b=b)
         nxt = eb.decode_batch(toks, ctx, 1)
         hid = [eb.hidden(b) for b in range(B)]
         kvs = [[eb.kv(l, ctx, shape.n_kv_heads * (shape.head_dim_swa if S.is_swa(shape, l) else shape.head_dim_full), b)
@@ -143,7 +146,7 @@ def test_e4b_batch_invariance_at_long_context(g4, gpu):
     try:
         for b in range(B):
             for l in range(24):
-                es.set_kv(l, 0, caches[b][l][0], caches[b][l][1])
+                es.set_kv(l, 0, caches[b % ncache][l][0], caches[b % ncache][l][1])
             n1 = es.forward(int(toks[b]), ctx, 1)
             assert (es.hidden(0) == hid[b]).all(), (b, float(np.abs(es.hidden(0) - hid[b]).max()))
             for i, l in enumerate((0, 5, 22, 23)):
