@@ -238,10 +238,10 @@ def reference_sample(g4, model, ctx: int, n_steps: int, threads: int):
 # DRAM bytes (read + write) per launch over the algorithmic K/V bytes, from
 # one ncu capture of each layer kind in the batch-64 E4B case
 # (bench.py --workload kernel-attn; profiles/attn_stream_e4b_b64.md):
-# sliding (135.01 + 3.95) MB / 134.22 MB, global at context 2048
-# (537.72 + 10.62) MB / 536.87 MB.  The excess is the split partials and
-# the new K/V rows.
-ATTN_TRAFFIC_RATIO = {"sliding": 1.0354, "global": 1.0214}
+# sliding (135.39 + 7.69) MB / 134.22 MB (four 64-row splits per CTA),
+# global at context 2048 (537.72 + 10.62) MB / 536.87 MB.  The excess is the
+# split partials and the new K/V rows.
+ATTN_TRAFFIC_RATIO = {"sliding": 1.0661, "global": 1.0214}
 
 
 def attention_roofline(eng, shape, B: int, pos: int, reps: int = 4):
