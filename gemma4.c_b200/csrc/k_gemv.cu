@@ -174,7 +174,10 @@ __device__ __forceinline__ float warp_sum_many(float (&v)[NV], int lane) {
 // read from memory serves NS sequences.  The CTAs loop over the rows.  Every
 // (row, sequence) follows the canonical chunked order of gemv_dense_kernel
 // (lane-strided fmaf chains per chunk, the warp_sum butterfly, chunk sums in
-// order), so the result of a sequence does not depend on the batch.
+// order), so the result of a sequence does not depend on the batch.  With a
+// prologue each CTA computes x + rmsnorm(delta)*w of its sequences itself
+// (the same expressions as resnorm_reg_kernel), and the CTAs of column 0
+// write it out (pro_writer).
 template <int NS, int RW>
 __global__ void __launch_bounds__(256, 2) gemv_dense_ms_kernel(const void *__restrict__ w, int type, int n, int rows,
                                                             const float *__restrict__ x, int ldx, int B,
