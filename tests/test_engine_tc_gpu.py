@@ -63,7 +63,8 @@ def single(g4, model, prompt, steps, max_seq=48):
     return got, h
 
 
-@pytest.mark.parametrize("which,B", [("tinyf", 9), ("tinyf", 16), ("tiny", 15), ("tiny", 24), ("tinyq5", 17)])
+@pytest.mark.parametrize("which,B", [("tiny", 2), ("tiny", 8), ("tinyf", 9), ("tinyf", 16), ("tiny", 15), ("tiny", 24),
+                                     ("tinyq5", 17)])
 def test_batched_streams_identical_to_single(g4, gpu, request, which, B):
     model = request.getfixturevalue(which)
     rng = np.random.default_rng(100 + B)
